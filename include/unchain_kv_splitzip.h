@@ -1,0 +1,148 @@
+/*
+ * unchain_kv_splitzip.h -- C ABI of the B200 (sm_100a) splitzip bf16 KV codec.
+ *
+ * Library: unchainkv_b200/lib/libunchain_kv_splitzip_cuda.so (same file name
+ * as the reference build, native/unchain_kv/CMakeLists.txt:21).
+ *
+ * Conventions shared by every entry point (the reference's,
+ * native/unchain_kv/kvq_splitzip_cuda.cu:288-463):
+ *   - pointers are device addresses passed as unsigned long long; the caller
+ *     owns all memory; `block_ids_ptr` points at int64 block ids on the device
+ *     (0 = the contiguous run starting at `block_start`);
+ *   - `stream_ptr` is a cudaStream_t (0 = legacy default stream); work is
+ *     enqueued asynchronously and nothing is synchronised;
+ *   - return > 0: bytes encoded / bytes written; 0: declined (bad argument,
+ *     size mismatch, not enough capacity, would not compress); -1: a CUDA
+ *     launch failed, message in kvq_splitzip_last_error() as
+ *     "<Kernel>: <cudaGetErrorString>" (thread-local);
+ *   - codec overflow is reported in band: byte 0 of the stream is 255.
+ *
+ * Strides and counts are in 16-bit words.  A paged KV layer is the tensor
+ * [2, num_blocks, block_size, kv_heads, head_dim] (bf16); plane_stride and
+ * block_stride are its strides along dims 0 and 1, block_words the product of
+ * dims 2.. .  The packed word order is K plane then V plane, blocks in
+ * block-table order -- exactly torch.index_select(kv_layer, 1, ids) flattened.
+ */
+#ifndef UNCHAIN_KV_SPLITZIP_H_
+#define UNCHAIN_KV_SPLITZIP_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define KVQ_API __attribute__((visibility("default")))
+#else
+#define KVQ_API
+#endif
+
+/* Replaces kvq_splitzip_last_error (kvq_splitzip_cuda.cu:288). */
+KVQ_API const char* kvq_splitzip_last_error(void);
+
+/* Replaces kvq_splitzip_bf16_encode_mode (kvq_splitzip_cuda.cu:292).
+ * fixed6 (bits 6, mode 3) or fixed5 (bits 5, mode 4) encode of `count`
+ * contiguous bf16 words.  Needs capacity >= align4(encoded) + 1032 (the
+ * reference's scratch rule); the first 36 scratch bytes hold the palette
+ * bitmap.  Palette = distinct high bytes in ascending order. */
+KVQ_API long long kvq_splitzip_bf16_encode_mode(unsigned long long src_ptr,
+                                                unsigned long long dst_ptr,
+                                                unsigned long long count,
+                                                unsigned long long capacity,
+                                                unsigned long long stream_ptr,
+                                                int bits);
+
+/* Replaces kvq_splitzip_bf16_encode (kvq_splitzip_cuda.cu:335): bits = 6. */
+KVQ_API long long kvq_splitzip_bf16_encode(unsigned long long src_ptr,
+                                           unsigned long long dst_ptr,
+                                           unsigned long long count,
+                                           unsigned long long capacity,
+                                           unsigned long long stream_ptr);
+
+/* Replaces kvq_splitzip_bf16_decode_fixed6_blocks (kvq_splitzip_cuda.cu:344).
+ * Decode a mode-3 stream and scatter it into the paged cache. */
+KVQ_API long long kvq_splitzip_bf16_decode_fixed6_blocks(
+    unsigned long long src_ptr, unsigned long long encoded_bytes,
+    unsigned long long dst_ptr, unsigned long long count_words,
+    unsigned long long block_count, unsigned long long block_words,
+    unsigned long long plane_stride, unsigned long long block_stride,
+    unsigned long long block_start, unsigned long long block_ids_ptr,
+    unsigned long long stream_ptr);
+
+/* Replaces kvq_splitzip_bf16_decode_fixed6 (kvq_splitzip_cuda.cu:370). */
+KVQ_API long long kvq_splitzip_bf16_decode_fixed6(
+    unsigned long long src_ptr, unsigned long long encoded_bytes,
+    unsigned long long dst_ptr, unsigned long long count_words,
+    unsigned long long block_count, unsigned long long block_words,
+    unsigned long long plane_stride, unsigned long long block_stride,
+    unsigned long long block_start, unsigned long long stream_ptr);
+
+/* Replaces kvq_splitzip_bf16_encode_top16 (kvq_splitzip_cuda.cu:381).
+ * top16 encode of `count` contiguous words with a 544-byte table
+ * ([0,256) K exponent->code, [256,512) V, [512,528) K books, [528,544) V
+ * books; code 255 = escape).  Escape entries are written in ascending
+ * position order.  Scratch after the stream: the reference's 8 bytes plus
+ * 16 + 8*ceil(count/8192) bytes at the next 16-byte aligned address
+ * (a 2*count-byte buffer, as the reference's callers use, always fits). */
+KVQ_API long long kvq_splitzip_bf16_encode_top16(unsigned long long src_ptr,
+                                                 unsigned long long dst_ptr,
+                                                 unsigned long long count,
+                                                 unsigned long long capacity,
+                                                 unsigned long long tables_ptr,
+                                                 unsigned long long stream_ptr);
+
+/* Replaces kvq_splitzip_bf16_decode_top16_blocks (kvq_splitzip_cuda.cu:416).
+ * Decode a mode-5 stream into the paged cache; escape entries in any order
+ * are accepted (sorted streams are patched in registers, others by a
+ * device-side fallback pass).  Returns 2*count_words, also when the stream's
+ * mode byte is not 5 (then nothing is written), as the reference does. */
+KVQ_API long long kvq_splitzip_bf16_decode_top16_blocks(
+    unsigned long long src_ptr, unsigned long long encoded_bytes,
+    unsigned long long dst_ptr, unsigned long long count_words,
+    unsigned long long block_count, unsigned long long block_words,
+    unsigned long long plane_stride, unsigned long long block_stride,
+    unsigned long long block_start, unsigned long long block_ids_ptr,
+    unsigned long long tables_ptr, unsigned long long stream_ptr);
+
+/* Replaces kvq_splitzip_bf16_decode_top16 (kvq_splitzip_cuda.cu:453). */
+KVQ_API long long kvq_splitzip_bf16_decode_top16(
+    unsigned long long src_ptr, unsigned long long encoded_bytes,
+    unsigned long long dst_ptr, unsigned long long count_words,
+    unsigned long long block_count, unsigned long long block_words,
+    unsigned long long plane_stride, unsigned long long block_stride,
+    unsigned long long block_start, unsigned long long tables_ptr,
+    unsigned long long stream_ptr);
+
+/* ---- extensions (same conventions) ------------------------------------ */
+
+/* Fused gather + top16 encode: replaces the torch.index_select pack of
+ * src/unchain_kv/vllm_connector.py:2854-2866 followed by
+ * kvq_splitzip_bf16_encode_top16; output bytes are identical to that pair. */
+KVQ_API long long kvq_splitzip_bf16_encode_top16_blocks(
+    unsigned long long cache_ptr, unsigned long long plane_stride,
+    unsigned long long block_stride, unsigned long long block_words,
+    unsigned long long block_ids_ptr, unsigned long long block_start,
+    unsigned long long block_count, unsigned long long dst_ptr,
+    unsigned long long capacity, unsigned long long tables_ptr,
+    unsigned long long stream_ptr);
+
+/* Fused gather + fixed6/fixed5 encode: replaces the same pack followed by
+ * kvq_splitzip_bf16_encode_mode (vllm_connector.py:3110-3118, 4592). */
+KVQ_API long long kvq_splitzip_bf16_encode_mode_blocks(
+    unsigned long long cache_ptr, unsigned long long plane_stride,
+    unsigned long long block_stride, unsigned long long block_words,
+    unsigned long long block_ids_ptr, unsigned long long block_start,
+    unsigned long long block_count, unsigned long long dst_ptr,
+    unsigned long long capacity, unsigned long long stream_ptr, int bits);
+
+/* Count of device-side bounded waits that ran out on the current device
+ * since load (0 in normal operation).  Synchronous; -1 on CUDA error. */
+KVQ_API long long kvq_splitzip_device_errors(void);
+
+/* ABI revision of the extension entry points. */
+KVQ_API long long kvq_splitzip_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UNCHAIN_KV_SPLITZIP_H_ */

@@ -1,0 +1,311 @@
+// Device-side building blocks shared by the splitzip kernels (sm_100a).
+//
+// * TMA bulk staging: cp.async.bulk global->shared with an mbarrier carrying
+//   the transaction count; every wait is bounded.
+// * Warp "funnel" stores: a warp writes a contiguous run of output bytes whose
+//   start is not aligned (the splitzip stream regions begin at byte 5, 65 or
+//   33 and at 5+n, ...).  Each lane owns K slots of S bytes; the lane shifts
+//   its bytes by the run's misalignment, borrowing the next lane's first
+//   bytes, so every interior store is an aligned S-byte store.  Only the two
+//   end slots of a run are written bytewise, clipped to the run.
+// * Release/acquire helpers for the decoupled look-back of the escape scan.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ukv {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnitWords = 16;                        // words per lane per step
+constexpr int kStepWords = 32 * kUnitWords;           // 512 words per warp step
+constexpr int kStepsPerWarp = 2;
+constexpr int kTileWords = kWarps * kStepsPerWarp * kStepWords;  // 8192
+constexpr unsigned kFull = 0xffffffffu;
+// Bounded waits: iterations of a polling loop before a wait is abandoned and
+// the error flag is raised (each iteration is at least a few hundred ns).
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+// ---------------------------------------------------------------- layouts
+
+// Packed word index i in [0, n) -> element offset.  block_words == 0 is a flat
+// buffer.  Otherwise the index walks the [2, block_count, block_words] view of
+// a paged cache [2, num_blocks, ...] whose block `id(b)` starts at
+// plane*plane_stride + id(b)*block_stride; id(b) = ids[b] or block_start + b.
+struct Layout {
+  uint64_t n;
+  uint64_t plane_words;
+  uint64_t block_words;
+  uint64_t plane_stride;
+  uint64_t block_stride;
+  uint64_t block_start;
+  const int64_t* ids;
+  int bw_shift;  // log2(block_words) when a power of two, else -1
+};
+
+__device__ __forceinline__ uint64_t layout_addr(const Layout& L, uint64_t i) {
+  if (L.block_words == 0) return i;
+  const uint64_t plane = i >= L.plane_words;
+  const uint64_t rem = i - (plane ? L.plane_words : 0);
+  uint64_t blk, within;
+  if (L.bw_shift >= 0) {
+    blk = rem >> L.bw_shift;
+    within = rem & (L.block_words - 1);
+  } else {
+    blk = rem / L.block_words;
+    within = rem - blk * L.block_words;
+  }
+  const uint64_t b = L.ids ? static_cast<uint64_t>(__ldg(L.ids + blk)) : L.block_start + blk;
+  return plane * L.plane_stride + b * L.block_stride + within;
+}
+
+// Words left in the contiguous run that starts at packed index i.
+__device__ __forceinline__ uint64_t layout_run(const Layout& L, uint64_t i) {
+  if (L.block_words == 0) return L.n - i;
+  const uint64_t rem = i >= L.plane_words ? i - L.plane_words : i;
+  const uint64_t within = L.bw_shift >= 0 ? (rem & (L.block_words - 1)) : rem % L.block_words;
+  return L.block_words - within;
+}
+
+// ------------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  Returns false if the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
+// 1-D TMA bulk copy global -> shared, completion counted on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(sdst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void st_release(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_acquire(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p);
+}
+
+// ------------------------------------------------------- warp funnel store
+
+// Store bytes [max(slot,lo), min(slot+S,hi)) of the little-endian value v
+// that belongs at `slot` (an S-aligned address).  Full slots use one aligned
+// store; clipped slots fall back to 4/2/1-byte aligned stores.
+template <typename T>
+__device__ __forceinline__ void store_clipped(uintptr_t slot, uint64_t v, uintptr_t lo,
+                                              uintptr_t hi) {
+  constexpr uintptr_t S = sizeof(T);
+  uintptr_t a = slot > lo ? slot : lo;
+  uintptr_t b = slot + S < hi ? slot + S : hi;
+  if (a >= b) return;
+  if (a == slot && b == slot + S) {
+    *reinterpret_cast<T*>(slot) = static_cast<T>(v);
+    return;
+  }
+  while (a < b) {
+    const uint32_t off = static_cast<uint32_t>(a - slot);
+    const uintptr_t rem = b - a;
+    if ((a & 3) == 0 && rem >= 4) {
+      *reinterpret_cast<uint32_t*>(a) = static_cast<uint32_t>(v >> (8 * off));
+      a += 4;
+    } else if ((a & 1) == 0 && rem >= 2) {
+      *reinterpret_cast<uint16_t*>(a) = static_cast<uint16_t>(v >> (8 * off));
+      a += 2;
+    } else {
+      *reinterpret_cast<uint8_t*>(a) = static_cast<uint8_t>(v >> (8 * off));
+      a += 1;
+    }
+  }
+}
+
+// A warp writes a contiguous byte run starting at g: lane L owns bytes
+// [g + L*K*S, g + (L+1)*K*S) given as K little-endian S-byte values d[k].
+// Bytes at or past g + valid, and bytes before g, are never written.  All 32
+// lanes must call this (it shuffles).
+template <typename T, int K>
+__device__ __forceinline__ void warp_store(uint8_t* g, uint32_t valid, const T (&d)[K],
+                                           int lane) {
+  constexpr uint32_t S = sizeof(T);
+  const uintptr_t base = reinterpret_cast<uintptr_t>(g);
+  const uintptr_t hi = base + valid;
+  const uint32_t s = static_cast<uint32_t>(base % S);
+  const uintptr_t mine = base + static_cast<uintptr_t>(lane) * K * S;
+  const T next0 = __shfl_down_sync(kFull, d[0], 1);
+  if (s == 0) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) store_clipped<T>(mine + k * S, static_cast<uint64_t>(d[k]), base, hi);
+    return;
+  }
+  const uintptr_t s0 = mine - s;
+  if (lane == 0) store_clipped<T>(s0, static_cast<uint64_t>(d[0]) << (8 * s), base, hi);
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const uint64_t cur = static_cast<uint64_t>(d[k]);
+    const uint64_t nxt = static_cast<uint64_t>(k + 1 < K ? d[(k + 1) % K] : next0);
+    const uint64_t v = (cur >> (8 * (S - s))) | (nxt << (8 * s));
+    const uintptr_t slot = s0 + (k + 1) * S;
+    uintptr_t h = hi;
+    if (k == K - 1 && lane == 31 && slot + s < h) h = slot + s;
+    store_clipped<T>(slot, v, base, h);
+  }
+}
+
+// Read 16 bytes starting at an arbitrary byte offset of a 4-byte aligned
+// shared buffer (the buffer must extend 4 bytes past the read).
+__device__ __forceinline__ void smem_read16(const uint8_t* buf, uint32_t off, uint32_t (&out)[4]) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + (off >> 2);
+  const uint32_t sh = (off & 3) * 8;
+  uint32_t a[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) a[k] = w[k];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) out[k] = __funnelshift_r(a[k], a[k + 1], sh);
+}
+
+template <int N>
+__device__ __forceinline__ void smem_read_words(const uint8_t* buf, uint32_t off, uint32_t (&out)[N]) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(buf) + (off >> 2);
+  const uint32_t sh = (off & 3) * 8;
+  uint32_t a[N + 1];
+#pragma unroll
+  for (int k = 0; k < N + 1; ++k) a[k] = w[k];
+#pragma unroll
+  for (int k = 0; k < N; ++k) out[k] = __funnelshift_r(a[k], a[k + 1], sh);
+}
+
+// ---------------------------------------------------------------- staging
+
+// Stage words [t0, t0+len) of a layout into shared memory (sin[j] = word
+// t0+j).  With `bulk` set (base 16-byte aligned and every run a multiple of 8
+// words at an 8-word aligned offset) thread 0 issues one TMA bulk copy per
+// contiguous run and registers the bytes on `bar`; a ragged flat tail is
+// copied by all threads.  Without it all threads gather word by word.
+// Thread 0 always arrives on `bar` once.  Caller waits on `bar`, then
+// __syncthreads().
+__device__ __forceinline__ void stage_words(const uint16_t* __restrict__ base, const Layout& L,
+                                            bool bulk, uint64_t t0, uint32_t len,
+                                            uint16_t* sin, uint64_t* bar) {
+  const int tid = threadIdx.x;
+  if (bulk) {
+    uint32_t aligned_len = len;
+    if (L.block_words == 0) aligned_len = len & ~7u;
+    if (tid == 0) {
+      uint64_t i = t0;
+      const uint64_t end = t0 + aligned_len;
+      while (i < end) {
+        uint64_t run = layout_run(L, i);
+        if (run > end - i) run = end - i;
+        const uint32_t bytes = static_cast<uint32_t>(run * 2);
+        mbar_expect_tx(bar, bytes);
+        bulk_g2s(sin + (i - t0), base + layout_addr(L, i), bytes, bar);
+        i += run;
+      }
+      mbar_arrive(bar);
+    }
+    for (uint32_t j = aligned_len + tid; j < len; j += kThreads) sin[j] = base[t0 + j];
+  } else {
+    if (tid == 0) mbar_arrive(bar);
+    for (uint32_t j = tid; j < len; j += kThreads) sin[j] = base[layout_addr(L, t0 + j)];
+  }
+}
+
+// Stage bytes [off, off+nbytes) of the global buffer [g, g+glen) into shared
+// memory so that byte off+i lands at smem[pad+i], pad = (g+off) % 16.  The
+// 16-byte aligned interior goes by TMA bulk copy (thread 0, bytes registered
+// on `bar`, no arrive); the ragged head/tail bytes by plain loads of all
+// threads.  Never reads outside [g, g+glen).  Returns pad.
+__device__ __forceinline__ uint32_t stage_bytes(const uint8_t* __restrict__ g, uint64_t off,
+                                                uint32_t nbytes, uint8_t* smem, uint64_t* bar) {
+  const int tid = threadIdx.x;
+  const uintptr_t A = reinterpret_cast<uintptr_t>(g) + off;
+  const uintptr_t E = A + nbytes;
+  const uintptr_t F = A & ~static_cast<uintptr_t>(15);
+  const uint32_t pad = static_cast<uint32_t>(A - F);
+  const uintptr_t gal = (reinterpret_cast<uintptr_t>(g) + 15) & ~static_cast<uintptr_t>(15);
+  const uintptr_t lo = F > gal ? F : gal;
+  const uintptr_t hi = E & ~static_cast<uintptr_t>(15);
+  if (hi > lo) {
+    if (tid == 0) {
+      mbar_expect_tx(bar, static_cast<uint32_t>(hi - lo));
+      bulk_g2s(smem + (lo - F), reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo),
+               bar);
+    }
+    for (uintptr_t a = A + tid; a < lo; a += kThreads)
+      smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
+    for (uintptr_t a = hi + tid; a < E; a += kThreads)
+      smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
+  } else {
+    for (uintptr_t a = A + tid; a < E; a += kThreads)
+      smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
+  }
+  return pad;
+}
+
+__device__ __forceinline__ uint32_t load_u32le(const uint8_t* __restrict__ p) {
+  return static_cast<uint32_t>(__ldg(p)) | (static_cast<uint32_t>(__ldg(p + 1)) << 8) |
+         (static_cast<uint32_t>(__ldg(p + 2)) << 16) | (static_cast<uint32_t>(__ldg(p + 3)) << 24);
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+}  // namespace ukv

@@ -1,0 +1,484 @@
+"""Operator API of the splitzip bf16 KV codec, backed by the sm_100a library.
+
+Mirrors ``unchain_kv.splitzip_cuda`` of the reference
+(src/unchain_kv/splitzip_cuda.py:159-393): same function names, arguments,
+return values (int bytes, or None when a call does not apply or the library
+declines) and errors (ValueError for bad ``bits``, RuntimeError with the
+library's message when a launch fails).  Calls run on
+``torch.cuda.current_stream(device)`` and never synchronise.
+
+Differences, all additive:
+
+* the library is the in-tree ``lib/libunchain_kv_splitzip_cuda.so`` (or
+  ``UNCHAIN_KV_SPLITZIP_LIB``); when it cannot be loaded, a call with CUDA
+  tensors raises instead of returning None -- there is no other backend;
+* ``register_top16_codebooks`` installs per-layer palettes (the reference's
+  32-layer table is the default);
+* fused gather entry points (``encode_top16_blocks``, ``encode_bf16_blocks``)
+  encode straight from the paged cache, replacing the
+  ``torch.index_select`` pack of vllm_connector.py:2854-2866;
+* ``top16_tables`` / ``encode_top16_tables`` take an explicit 544-byte table.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_LIB = None
+_LOAD_ERROR: str | None = None
+_LOAD_LOCK = threading.Lock()
+_TOP16_TABLE_CACHE: dict = {}
+
+# Default top-16 exponent codebooks: 32 layers x (16 K + 16 V) exponents,
+# code = rank.  This is the reference's interface table
+# (src/unchain_kv/splitzip_cuda.py:11-31, Llama-3-8B traces); receivers and
+# senders must agree on it byte for byte, so it is carried unchanged.
+_DEFAULT_TOP16_CODEBOOKS = bytes.fromhex(
+    "7f7e7d807c81857b827a8483867978777c7d7b7a79787e7776757f74737280717f807e817d827c7b837a8479788577767b7c7a797d787776"
+    "7e7574737f7271707f807e7d817c7b827a798378777675747c7d7b7a797e7877767f7574807372717f807e7d817c7b7a8283798478857776"
+    "7c7d7b7e7a79787f77767574737280717f7e807d7c7b817a79827877767574737d7c7b7e7a79787f77768075817473727f7e807d7c7b7a81"
+    "82797877767583747d7e7c7b7f7a797880777675747372717e7f7d807c7b817a82797877767574737d7c7e7b7a7f79787780767574738172"
+    "7f7e807d7c7b817a82797877837675747d7e7c7b7f7a797877807675747372717f7e807d7c817b7a79827877767574737d7e7c7b7f7a7980"
+    "78777681757473727f7e807d7c7b817a82797877767574737d7e7c7b7f7a797877807675747372717f7e807d7c7b817a8279787776758374"
+    "7d7e7c7b7f7a797877807675747372717f7e807d7c7b817a79827877768375747d7e7c7b7f7a797880777675747381727f7e807d7c7b817a"
+    "82797877767574737e7d7c7f7b7a797877807675747372717f7e807d7c817b7a82797883778476757d7e7c7b7f7a79788077767574737271"
+    "7f7e807d7c7b817a79827877767574737d7e7c7f7b7a798078777675817473727f7e807d7c7b817a79827883777675747e7d7f7c7b7a8079"
+    "78777675747372717f7e807d7c817b7a82797877767574737e7d7c7f7b7a798078777675748173727f7e807d7c7b817a7982787776757473"
+    "7e7d7c7f7b7a798078777675747372717f7e7d807c7b817a79827877837675747e7d7f7c7b7a807978777675747381727f7e807d7c817b7a"
+    "82797877847675837e7d7f7c7b7a807978777675748173727f7e807d7c7b817a79827877767574737e7d7f7c7b7a80797877767574737281"
+    "7f7e807d7c7b817a82797877768375747e7d7f7c7b807a7978778176757473727f7e807d7c817b7a82797877767574737e7f7d7c807b7a79"
+    "78817776757473727f7e807d7c7b817a82797877767574737f7e7d807c7b817a79787776757482737f7e807d7c7b817a8279787783767574"
+    "7f7e7d807c7b817a79787776758274737f7e807d7c7b817a79827877768375747f7e807d817c7b7a79827877767574737f7e807d7c7b817a"
+    "7982787776837574807f817e7d827c7b7a797877837675747f7e7d807c7b817a828679838785847880817f7e7d827c7b7a79788377767574"
+    "7f807e7d7c817b7a82798378770076757d7c7e7b7a79787f77767580740073727f807e7d7c817b7a79828378770076757d7c7e7b7a7f7978"
+    "77807675740073727f807e7d7c817b827a797877830076757d7e7c7b7f7a797877807675007473727f807e7d817c7b7a82797877007675837d7e7c7b7f7a79788077767500747381"
+)
+_TOP16_CODEBOOKS = _DEFAULT_TOP16_CODEBOOKS
+
+_U64 = ctypes.c_ulonglong
+_SIGNATURES = {
+    "kvq_splitzip_bf16_encode": [_U64] * 5,
+    "kvq_splitzip_bf16_encode_mode": [_U64] * 5 + [ctypes.c_int],
+    "kvq_splitzip_bf16_decode_fixed6": [_U64] * 10,
+    "kvq_splitzip_bf16_decode_fixed6_blocks": [_U64] * 11,
+    "kvq_splitzip_bf16_encode_top16": [_U64] * 6,
+    "kvq_splitzip_bf16_decode_top16": [_U64] * 11,
+    "kvq_splitzip_bf16_decode_top16_blocks": [_U64] * 12,
+    "kvq_splitzip_bf16_encode_top16_blocks": [_U64] * 11,
+    "kvq_splitzip_bf16_encode_mode_blocks": [_U64] * 10 + [ctypes.c_int],
+    "kvq_splitzip_device_errors": [],
+    "kvq_splitzip_abi_version": [],
+}
+
+
+def library_path() -> Path:
+    """The in-tree build of the sm_100a library."""
+    return Path(__file__).resolve().parent / "lib" / "libunchain_kv_splitzip_cuda.so"
+
+
+def _candidate_paths() -> list[str]:
+    env = os.environ.get("UNCHAIN_KV_SPLITZIP_LIB")
+    if env:
+        return [env]
+    return [str(library_path())]
+
+
+def _load():
+    global _LIB, _LOAD_ERROR
+    if _LIB is not None:
+        return _LIB
+    with _LOAD_LOCK:
+        if _LIB is not None:
+            return _LIB
+        errors = []
+        for path in _candidate_paths():
+            try:
+                lib = ctypes.CDLL(path)
+            except OSError as exc:
+                errors.append(str(exc))
+                continue
+            for name, argtypes in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = ctypes.c_longlong
+            lib.kvq_splitzip_last_error.argtypes = []
+            lib.kvq_splitzip_last_error.restype = ctypes.c_char_p
+            _LIB = lib
+            _LOAD_ERROR = None
+            return lib
+        _LOAD_ERROR = "; ".join(errors[-2:])
+        return None
+
+
+def available() -> bool:
+    return _load() is not None
+
+
+def load_error() -> str | None:
+    _load()
+    return _LOAD_ERROR
+
+
+def _require_lib():
+    """The library, or a loud failure: a CUDA call has no other backend."""
+    lib = _load()
+    if lib is None:
+        raise RuntimeError(
+            "unchainkv_b200: the sm_100a splitzip library is not loadable "
+            f"({_LOAD_ERROR}); build it with `python -m unchainkv_b200._build`"
+        )
+    return lib
+
+
+def _is_cuda(tensor) -> bool:
+    return getattr(getattr(tensor, "device", None), "type", "") == "cuda"
+
+
+def _raise_last(lib, default: str):
+    error = lib.kvq_splitzip_last_error()
+    raise RuntimeError(error.decode() if error else default)
+
+
+# --------------------------------------------------------------- tables
+
+
+def build_top16_tables(codebooks: bytes) -> bytes:
+    """The 544-byte device table of one layer from its 32 codebook bytes:
+    [0,256) K exponent->code, [256,512) V, 255 = escape, later duplicates win;
+    then the 32 codebook bytes (splitzip_cuda.py:290-295 of the reference)."""
+    if len(codebooks) != 32:
+        raise ValueError("a layer's top16 codebooks are 32 bytes (16 K + 16 V)")
+    values = bytearray([255]) * 512
+    for plane in range(2):
+        for code, exponent in enumerate(codebooks[plane * 16 : (plane + 1) * 16]):
+            values[plane * 256 + exponent] = code
+    values.extend(codebooks)
+    return bytes(values)
+
+
+def rank_top16(histogram) -> list[int]:
+    """Top-16 exponents of a 256-bin histogram ranked by (-count, exponent),
+    observed exponents only; code = rank (trace.py:30-33 and
+    scripts/extract_llama_top16_codebooks.py:39-40 of the reference)."""
+    counts = [int(v) for v in histogram]
+    ranked = sorted((e for e in range(len(counts)) if counts[e] > 0), key=lambda e: (-counts[e], e))
+    return ranked[:16]
+
+
+def register_top16_codebooks(codebooks: bytes) -> int:
+    """Install per-layer top16 codebooks (32 bytes per layer, K then V).
+
+    Replaces the module's ``_TOP16_CODEBOOKS`` (so the layer bound of
+    ``_top16_tables`` follows it) and drops cached device tables.  Returns
+    the number of layers.  ``register_top16_codebooks(None)`` restores the
+    reference's default table."""
+    global _TOP16_CODEBOOKS
+    if codebooks is None:
+        codebooks = _DEFAULT_TOP16_CODEBOOKS
+    codebooks = bytes(codebooks)
+    if not codebooks or len(codebooks) % 32:
+        raise ValueError("codebooks must be a non-empty multiple of 32 bytes")
+    _TOP16_CODEBOOKS = codebooks
+    _TOP16_TABLE_CACHE.clear()
+    return len(codebooks) // 32
+
+
+def _top16_tables(layer_index: int, device, torch):
+    if not 0 <= layer_index < len(_TOP16_CODEBOOKS) // 32:
+        return None
+    key = (str(device), layer_index, id(_TOP16_CODEBOOKS))
+    cached = _TOP16_TABLE_CACHE.get(key)
+    if cached is not None:
+        return cached
+    values = build_top16_tables(_TOP16_CODEBOOKS[layer_index * 32 : (layer_index + 1) * 32])
+    cached = torch.tensor(list(values), dtype=torch.uint8, device=device)
+    _TOP16_TABLE_CACHE[key] = cached
+    return cached
+
+
+def top16_tables(layer_index: int, device):
+    """Public form of ``_top16_tables``: the layer's 544-byte uint8 device table."""
+    import torch
+
+    return _top16_tables(layer_index, device, torch)
+
+
+# --------------------------------------------------------------- encode
+
+
+def encode_bf16(source, out, bits: int = 6) -> int | None:
+    """fixed6 (bits 6) / fixed5 (bits 5) encode of a contiguous bf16 tensor
+    into the uint8 tensor ``out``; returns the stream length or None."""
+    if not _is_cuda(source):
+        return None
+    lib = _require_lib()
+    if bits not in {5, 6}:
+        raise ValueError("splitzip bf16 bits must be 5 or 6")
+    import torch
+
+    stream = torch.cuda.current_stream(source.device).cuda_stream
+    encoded = lib.kvq_splitzip_bf16_encode_mode(
+        int(source.data_ptr()),
+        int(out.data_ptr()),
+        int(source.numel()),
+        int(out.numel()),
+        int(stream),
+        int(bits),
+    )
+    if encoded < 0:
+        _raise_last(lib, "splitzip cuda encode failed")
+    return int(encoded)
+
+
+def encode_top16(source, out, layer_index: int) -> int | None:
+    """top16 encode of a contiguous bf16 tensor with layer ``layer_index``'s
+    codebooks; returns the stream length, or None if declined."""
+    if not _is_cuda(source):
+        return None
+    if source.device != getattr(out, "device", None):
+        return None
+    lib = _require_lib()
+    import torch
+
+    if source.dtype != torch.bfloat16 or out.dtype != torch.uint8:
+        return None
+    if not source.is_contiguous() or not out.is_contiguous():
+        return None
+    tables = _top16_tables(layer_index, source.device, torch)
+    if tables is None:
+        return None
+    return encode_top16_tables(source, out, tables, _lib=lib)
+
+
+def encode_top16_tables(source, out, tables, _lib=None) -> int | None:
+    """top16 encode with an explicit 544-byte uint8 device table."""
+    lib = _lib or _require_lib()
+    import torch
+
+    stream = torch.cuda.current_stream(source.device).cuda_stream
+    encoded = lib.kvq_splitzip_bf16_encode_top16(
+        int(source.data_ptr()),
+        int(out.data_ptr()),
+        int(source.numel()),
+        int(out.numel()),
+        int(tables.data_ptr()),
+        int(stream),
+    )
+    if encoded < 0:
+        _raise_last(lib, "splitzip top16 encode failed")
+    return int(encoded) or None
+
+
+def _block_layout(kv_layer, block_ids, torch):
+    """(plane_stride, block_stride, block_words, ids tensor|None, start, count)
+    for a paged layer [2, num_blocks, ...] whose blocks are contiguous."""
+    if kv_layer.dim() < 3 or kv_layer.shape[0] != 2:
+        return None
+    block_words = 1
+    for size in kv_layer.shape[2:]:
+        block_words *= int(size)
+    expected = 1
+    for dim in range(kv_layer.dim() - 1, 1, -1):
+        if kv_layer.shape[dim] != 1 and kv_layer.stride(dim) != expected:
+            return None
+        expected *= int(kv_layer.shape[dim])
+    if isinstance(block_ids, torch.Tensor):
+        ids = block_ids.to(device=kv_layer.device, dtype=torch.int64).contiguous()
+        return (int(kv_layer.stride(0)), int(kv_layer.stride(1)), block_words, ids, 0, int(ids.numel()))
+    block_ids = [int(b) for b in block_ids]
+    if not block_ids:
+        return None
+    start = block_ids[0]
+    if block_ids == list(range(start, start + len(block_ids))):
+        return (int(kv_layer.stride(0)), int(kv_layer.stride(1)), block_words, None, start, len(block_ids))
+    ids = torch.tensor(block_ids, dtype=torch.int64, device=kv_layer.device)
+    return (int(kv_layer.stride(0)), int(kv_layer.stride(1)), block_words, ids, 0, len(block_ids))
+
+
+def encode_top16_blocks(kv_layer, block_ids, out, layer_index: int = 0, tables=None) -> int | None:
+    """Fused gather + top16 encode straight from the paged cache.
+
+    Produces the bytes of ``encode_top16(index_select(kv_layer, 1, ids), out,
+    layer)`` without the packed copy.  ``block_ids`` is a list of ints or an
+    int64 tensor."""
+    if not _is_cuda(kv_layer):
+        return None
+    lib = _require_lib()
+    import torch
+
+    if kv_layer.dtype != torch.bfloat16 or out.dtype != torch.uint8 or not out.is_contiguous():
+        return None
+    layout = _block_layout(kv_layer, block_ids, torch)
+    if layout is None:
+        return None
+    if tables is None:
+        tables = _top16_tables(layer_index, kv_layer.device, torch)
+        if tables is None:
+            return None
+    plane_stride, block_stride, block_words, ids, start, count = layout
+    current = torch.cuda.current_stream(kv_layer.device)
+    encoded = lib.kvq_splitzip_bf16_encode_top16_blocks(
+        int(kv_layer.data_ptr()), plane_stride, block_stride, block_words,
+        int(ids.data_ptr()) if ids is not None else 0, start, count,
+        int(out.data_ptr()), int(out.numel()), int(tables.data_ptr()), int(current.cuda_stream),
+    )
+    if ids is not None and not isinstance(block_ids, torch.Tensor):
+        ids.record_stream(current)
+    if encoded < 0:
+        _raise_last(lib, "splitzip top16 encode failed")
+    return int(encoded) or None
+
+
+def encode_bf16_blocks(kv_layer, block_ids, out, bits: int = 6) -> int | None:
+    """Fused gather + fixed6/fixed5 encode straight from the paged cache."""
+    if not _is_cuda(kv_layer):
+        return None
+    lib = _require_lib()
+    if bits not in {5, 6}:
+        raise ValueError("splitzip bf16 bits must be 5 or 6")
+    import torch
+
+    if kv_layer.dtype != torch.bfloat16 or out.dtype != torch.uint8 or not out.is_contiguous():
+        return None
+    layout = _block_layout(kv_layer, block_ids, torch)
+    if layout is None:
+        return None
+    plane_stride, block_stride, block_words, ids, start, count = layout
+    current = torch.cuda.current_stream(kv_layer.device)
+    encoded = lib.kvq_splitzip_bf16_encode_mode_blocks(
+        int(kv_layer.data_ptr()), plane_stride, block_stride, block_words,
+        int(ids.data_ptr()) if ids is not None else 0, start, count,
+        int(out.data_ptr()), int(out.numel()), int(current.cuda_stream), int(bits),
+    )
+    if ids is not None and not isinstance(block_ids, torch.Tensor):
+        ids.record_stream(current)
+    if encoded < 0:
+        _raise_last(lib, "splitzip cuda encode failed")
+    return int(encoded) or None
+
+
+# --------------------------------------------------------------- decode
+
+
+def _decode_layout(source, out, block_ids, raw_bytes, torch):
+    """Validation and layout of the reference decoder wrappers
+    (splitzip_cuda.py:200-230): same rules, same None results."""
+    if not block_ids or raw_bytes <= 0 or raw_bytes % 2:
+        return None
+    if not _is_cuda(source):
+        return None
+    if source.device != getattr(out, "device", None):
+        return None
+    if source.dtype != torch.uint8 or out.dtype != torch.bfloat16:
+        return None
+    if not source.is_contiguous() or not out.is_contiguous():
+        return None
+    if out.dim() < 3 or out.shape[0] != 2:
+        return None
+    if len(set(block_ids)) != len(block_ids) or any(
+        block < 0 or block >= out.shape[1] for block in block_ids
+    ):
+        return None
+    start = block_ids[0]
+    contiguous = block_ids == list(range(start, start + len(block_ids)))
+    count_words = raw_bytes // 2
+    divisor = 2 * len(block_ids)
+    if count_words % divisor:
+        return None
+    block_words = count_words // divisor
+    current = torch.cuda.current_stream(out.device)
+    block_ids_tensor = None
+    if not contiguous:
+        block_ids_tensor = torch.tensor(block_ids, dtype=torch.int64, device=out.device)
+    return count_words, block_words, start, current, block_ids_tensor
+
+
+def decode_fixed6(source, out, block_ids: list[int], raw_bytes: int) -> int | None:
+    """Decode a mode-3 stream and scatter it into ``out``'s blocks."""
+    if not _is_cuda(source):
+        return None
+    lib = _require_lib()
+    import torch
+
+    layout = _decode_layout(source, out, block_ids, raw_bytes, torch)
+    if layout is None:
+        return None
+    count_words, block_words, start, current, block_ids_tensor = layout
+    if block_ids_tensor is not None:
+        copied = lib.kvq_splitzip_bf16_decode_fixed6_blocks(
+            int(source.data_ptr()), int(source.numel()), int(out.data_ptr()), count_words,
+            len(block_ids), block_words, int(out.stride(0)), int(out.stride(1)), start,
+            int(block_ids_tensor.data_ptr()), int(current.cuda_stream),
+        )
+        block_ids_tensor.record_stream(current)
+    else:
+        copied = lib.kvq_splitzip_bf16_decode_fixed6(
+            int(source.data_ptr()), int(source.numel()), int(out.data_ptr()), count_words,
+            len(block_ids), block_words, int(out.stride(0)), int(out.stride(1)), start,
+            int(current.cuda_stream),
+        )
+    if copied < 0:
+        _raise_last(lib, "splitzip cuda decode failed")
+    return int(copied) or None
+
+
+def decode_top16(source, out, block_ids: list[int], raw_bytes: int, layer_index: int) -> int | None:
+    """Decode a mode-5 stream with layer ``layer_index``'s codebooks and
+    scatter it into ``out``'s blocks."""
+    if not _is_cuda(source):
+        return None
+    lib = _require_lib()
+    import torch
+
+    layout = _decode_layout(source, out, block_ids, raw_bytes, torch)
+    if layout is None:
+        return None
+    tables = _top16_tables(layer_index, source.device, torch)
+    if tables is None:
+        return None
+    return _decode_top16_with(lib, source, out, block_ids, layout, tables)
+
+
+def decode_top16_tables(source, out, block_ids: list[int], raw_bytes: int, tables) -> int | None:
+    """decode_top16 with an explicit 544-byte uint8 device table."""
+    if not _is_cuda(source):
+        return None
+    lib = _require_lib()
+    import torch
+
+    layout = _decode_layout(source, out, block_ids, raw_bytes, torch)
+    if layout is None:
+        return None
+    return _decode_top16_with(lib, source, out, block_ids, layout, tables)
+
+
+def _decode_top16_with(lib, source, out, block_ids, layout, tables):
+    count_words, block_words, start, current, block_ids_tensor = layout
+    if block_ids_tensor is not None:
+        copied = lib.kvq_splitzip_bf16_decode_top16_blocks(
+            int(source.data_ptr()), int(source.numel()), int(out.data_ptr()), count_words,
+            len(block_ids), block_words, int(out.stride(0)), int(out.stride(1)), start,
+            int(block_ids_tensor.data_ptr()), int(tables.data_ptr()), int(current.cuda_stream),
+        )
+        block_ids_tensor.record_stream(current)
+    else:
+        copied = lib.kvq_splitzip_bf16_decode_top16(
+            int(source.data_ptr()), int(source.numel()), int(out.data_ptr()), count_words,
+            len(block_ids), block_words, int(out.stride(0)), int(out.stride(1)), start,
+            int(tables.data_ptr()), int(current.cuda_stream),
+        )
+    if copied < 0:
+        _raise_last(lib, "splitzip top16 decode failed")
+    return int(copied) or None
+
+
+def device_errors() -> int:
+    """Device-side bounded waits that ran out since load (0 normally)."""
+    lib = _require_lib()
+    value = lib.kvq_splitzip_device_errors()
+    if value < 0:
+        _raise_last(lib, "splitzip device error query failed")
+    return int(value)

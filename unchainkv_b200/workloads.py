@@ -1,0 +1,180 @@
+"""Seeded synthetic KV caches and palettes for the benchmark configurations.
+
+No public dataset or checkpoint is involved: the configs specify a value
+distribution, and this module draws it.
+
+* Every (plane, kv_head, head_dim) channel has a scale s_c drawn
+  log-uniform in [0.01, 4].  2% of channels are outliers with s_c x 50.
+* A value is N(0, 1) * s_c in fp32, rounded to nearest-even bf16.
+* The top16 palette of a layer is the 16 most frequent exponents of a
+  seeded 4096-token calibration draw, one palette per plane.  Ties are
+  broken by exponent value, and code = rank: the rule of the reference's
+  trace.py:30-33 and scripts/extract_llama_top16_codebooks.py:39-40.
+* Seeds: calibration 1000+layer, data 2000+layer, block tables 3000+k,
+  request lengths 4000.
+
+Host (numpy, exact) and device (torch CUDA generator) drawers are provided.
+The device drawer is for benchmark-sized caches and is seeded but not
+bit-identical to the numpy one.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+KV_HEADS = 8
+HEAD_DIM = 128
+BLOCK_TOKENS = 16
+
+
+@dataclass(frozen=True)
+class CodecConfig:
+    name: str
+    layers: int
+    tokens: int
+    kv_heads: int = KV_HEADS
+    head_dim: int = HEAD_DIM
+    block_tokens: int = BLOCK_TOKENS
+    pool_factor: int = 2  # pool blocks = pool_factor * blocks used
+
+    @property
+    def blocks(self) -> int:
+        return self.tokens // self.block_tokens
+
+    @property
+    def block_words(self) -> int:
+        return self.block_tokens * self.kv_heads * self.head_dim
+
+    @property
+    def words_per_layer(self) -> int:
+        return 2 * self.blocks * self.block_words
+
+    @property
+    def raw_bytes(self) -> int:
+        return 2 * self.words_per_layer * self.layers
+
+
+# BASELINE.json configs[0..2] (configs[3] and [4] have their own builders).
+CONFIG0 = CodecConfig("c0_single_layer_roundtrip", layers=1, tokens=1024, pool_factor=4)
+CONFIG1 = CodecConfig("c1_llama3_8b_prefill_4096", layers=32, tokens=4096)
+CONFIG2 = CodecConfig("c2_llama3_70b_tp8_shard_32768", layers=80, tokens=32768, kv_heads=1)
+CONFIGS = {"c0": CONFIG0, "c1": CONFIG1, "c2": CONFIG2}
+
+
+def channel_scales(layer: int, kv_heads: int = KV_HEADS, head_dim: int = HEAD_DIM,
+                   outlier_factor: float = 50.0) -> np.ndarray:
+    rng = np.random.Generator(np.random.PCG64(1000 + layer))
+    scales = np.exp(rng.uniform(np.log(0.01), np.log(4.0), size=(2, kv_heads, head_dim)))
+    outliers = rng.random((2, kv_heads, head_dim)) < 0.02
+    scales[outliers] *= outlier_factor
+    return scales.astype(np.float32)
+
+
+def bf16_bits(values: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns, round to nearest even (finite inputs)."""
+    bits = np.ascontiguousarray(values, dtype=np.float32).view(np.uint32)
+    rounded = bits + np.uint32(0x7FFF) + ((bits >> np.uint32(16)) & np.uint32(1))
+    return (rounded >> np.uint32(16)).astype(np.uint16)
+
+
+def draw_tokens(seed: int, scales: np.ndarray, tokens: int, scale_shift: float = 1.0) -> np.ndarray:
+    """[2, tokens, kv_heads, head_dim] bf16 bit patterns (uint16)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    kvh, hd = scales.shape[1:]
+    values = rng.standard_normal((2, tokens, kvh, hd), dtype=np.float32)
+    values *= (scales * np.float32(scale_shift))[:, None, :, :]
+    return bf16_bits(values)
+
+
+def top16_codebooks_from_words(words: np.ndarray) -> bytes:
+    """32 codebook bytes (K then V) from [2, ...] bf16 words."""
+    from .splitzip_cuda import rank_top16
+
+    books = bytearray()
+    for plane in range(2):
+        exps = (words[plane].reshape(-1) >> 7) & 0xFF
+        hist = np.bincount(exps, minlength=256)
+        top = rank_top16(hist)
+        if len(top) < 16:  # pad with unused exponents so the table is complete
+            top += [e for e in range(256) if e not in top][: 16 - len(top)]
+        books.extend(top)
+    return bytes(books)
+
+
+def layer_codebooks(layer: int, kv_heads: int = KV_HEADS, head_dim: int = HEAD_DIM) -> bytes:
+    scales = channel_scales(layer, kv_heads, head_dim)
+    calibration = draw_tokens(1000 + layer + 100000, scales, 4096)
+    return top16_codebooks_from_words(calibration)
+
+
+def block_table(pool_blocks: int, blocks: int, seed: int) -> np.ndarray:
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return rng.permutation(pool_blocks)[:blocks].astype(np.int64)
+
+
+def paged_cache_host(cfg: CodecConfig, layer: int, ids: np.ndarray, scale_shift: float = 1.0,
+                     fill_seed: int | None = None) -> np.ndarray:
+    """A [2, pool, block_tokens, kv_heads, head_dim] uint16 cache whose blocks
+    `ids` hold one request's tokens (in block-table order) and whose other
+    blocks hold independent draws of the same distribution."""
+    pool = cfg.blocks * cfg.pool_factor
+    scales = channel_scales(layer, cfg.kv_heads, cfg.head_dim)
+    cache = draw_tokens(fill_seed if fill_seed is not None else 5000 + layer, scales,
+                        pool * cfg.block_tokens, scale_shift)
+    cache = cache.reshape(2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim)
+    request = draw_tokens(2000 + layer, scales, cfg.tokens, scale_shift)
+    cache[:, ids] = request.reshape(2, cfg.blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim)
+    return cache
+
+
+# ------------------------------------------------------------------ device
+
+
+def draw_tokens_device(seed: int, scales, tokens: int, device, scale_shift: float = 1.0):
+    """Device analogue of draw_tokens: returns a bf16 tensor [2, tokens, kvh, hd]."""
+    import torch
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    sc = torch.as_tensor(np.asarray(scales) * scale_shift, device=device, dtype=torch.float32)
+    kvh, hd = sc.shape[1:]
+    values = torch.randn((2, tokens, kvh, hd), generator=gen, device=device, dtype=torch.float32)
+    values.mul_(sc[:, None])
+    return values.to(torch.bfloat16)
+
+
+def codebooks_device(words_bf16) -> bytes:
+    """Codebooks from a device bf16 tensor [2, ...] (histograms on the GPU)."""
+    import torch
+
+    from .splitzip_cuda import rank_top16
+
+    books = bytearray()
+    for plane in range(2):
+        w = words_bf16[plane].reshape(-1).view(torch.int16).to(torch.int32) & 0xFFFF
+        hist = torch.bincount((w >> 7) & 0xFF, minlength=256).cpu().tolist()
+        top = rank_top16(hist)
+        if len(top) < 16:
+            top += [e for e in range(256) if e not in top][: 16 - len(top)]
+        books.extend(top)
+    return bytes(books)
+
+
+def fill_layer_device(cache_layer, cfg: CodecConfig, layer: int, ids, scale_shift: float = 1.0):
+    """Fill a device cache layer [2, pool, bt, kvh, hd] (bf16) in place:
+    request tokens at `ids`, independent draws elsewhere.  Returns the
+    layer's calibrated codebooks (32 bytes)."""
+    import torch
+
+    device = cache_layer.device
+    pool = cache_layer.shape[1]
+    scales = channel_scales(layer, cfg.kv_heads, cfg.head_dim)
+    filler = draw_tokens_device(5000 + layer, scales, pool * cfg.block_tokens, device, scale_shift)
+    cache_layer.copy_(filler.view(2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim))
+    request = draw_tokens_device(2000 + layer, scales, cfg.tokens, device, scale_shift)
+    ids_t = torch.as_tensor(ids, device=device, dtype=torch.int64)
+    cache_layer.index_copy_(1, ids_t, request.view(2, cfg.blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim))
+    calibration = draw_tokens_device(1000 + layer + 100000, scales, 4096, device)
+    return codebooks_device(calibration)
