@@ -1,0 +1,512 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 splitzip KV codec (encode + decode round trip).
+
+Metric: codec GB/s of raw bf16 KV per GPU (encode, decode)
+and % of HBM peak; ratio.
+
+Workload (default, configs[1]): Llama-3-8B full prefill KV, 32 layers, one
+4096-token prompt, 8 kv heads x 128, bf16, paged blocks of 16 tokens with a
+scattered block table; per-layer palettes; synthetic values drawn on the
+device from the config's distribution (per-channel scale log-uniform
+[0.01, 4], 2% outlier channels x50).  One step = fused gather + encode of
+all 32 layers (device-chosen codec: top16, else fixed6, else raw -- the
+reference's fallback chain) + decode + scatter of all 32 streams into a
+second paged cache with another block table.  Inputs (512 MiB raw per step)
+are larger than L2.
+
+`value` = raw KV bytes per step / device time per step, summed over ranks
+(whole job); `e2e` = the same through the public Python API with the stream
+copied device->pinned host->device inside the timed region (the reference's
+producer/consumer path, scripts/bench_codec_matrix.py:159-188).
+
+--impl reference times the reference's CPU path (the CPU oracle's
+multi-threaded restatement of the codec: top16 attempt -> fixed6 fallback ->
+fixed6 decode) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--workload", choices=("c1", "c2"), default="c1")
+    p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--skip-e2e", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ----------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 10:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        rows = [r for r in self.rows if r[0].isdigit() and int(r[0]) in self.gpus]
+        loaded = [r for r in rows if r[4].isdigit() and int(r[4]) >= 30] or rows
+        if not loaded:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in loaded if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in loaded:
+            for name, value in zip(names, r[6:10]):
+                if value.strip().lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": float(loaded[0][2]) if loaded[0][2].replace(".", "").isdigit() else None,
+            "reasons": sorted(reasons),
+            "samples": len(loaded),
+        }
+
+
+# ------------------------------------------------------------- CPU oracle
+
+
+def host_layer(cfg, layer, ids, scale_shift=1.0):
+    from unchainkv_b200 import splitzip_cuda, workloads
+
+    cache = workloads.paged_cache_host(cfg, layer, ids, scale_shift)
+    tables = np.frombuffer(splitzip_cuda.build_top16_tables(workloads.layer_codebooks(layer, cfg.kv_heads, cfg.head_dim)),
+                           dtype=np.uint8).copy()
+    return cache, tables
+
+
+def cpu_pipeline_gbs(cfg, layers: int, repeats: int = 3):
+    """The reference path on host cores: top16 attempt -> (overflow) fixed6
+    encode -> decode into a second cache, per layer, all host threads.
+    Returns (GB/s of raw KV, threads, escape rate, mode histogram)."""
+    from oracle import oracle
+    from unchainkv_b200 import workloads
+
+    lib = oracle.lib()
+    threads = oracle.max_threads()
+    pool = cfg.blocks * cfg.pool_factor
+    ids = np.ascontiguousarray(workloads.block_table(pool, cfg.blocks, 3000))
+    ids2 = np.ascontiguousarray(workloads.block_table(pool, cfg.blocks, 3001))
+    samples = [host_layer(cfg, layer, ids) for layer in range(layers)]
+    n = cfg.words_per_layer
+    bw = cfg.block_words
+    ps = pool * bw
+    out = np.zeros(2 * n + 4096, dtype=np.uint8)
+    target = np.zeros((2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim), dtype=np.uint16)
+    modes = {}
+    escapes = 0
+
+    def run_layer(cache, tables):
+        nonlocal escapes
+        res = lib.orc_encode_top16_blocks_mt(cache.ctypes.data, ps, bw, bw, ids.ctypes.data, 0, cfg.blocks,
+                                             out.ctypes.data, out.size, tables.ctypes.data, threads)
+        mode = int(out[0])
+        if mode == 255:
+            res = lib.orc_encode_mode_blocks_mt(cache.ctypes.data, ps, bw, bw, ids.ctypes.data, 0, cfg.blocks,
+                                                out.ctypes.data, out.size, 6, threads)
+            mode = int(out[0])
+            lib.orc_decode_fixed6_blocks_mt(out.ctypes.data, res, target.ctypes.data, n, cfg.blocks, bw, ps, bw,
+                                            0, ids2.ctypes.data, threads)
+        else:
+            lib.orc_decode_top16_blocks_mt(out.ctypes.data, res, target.ctypes.data, n, cfg.blocks, bw, ps, bw,
+                                           0, ids2.ctypes.data, tables.ctypes.data, threads)
+        return mode
+
+    for cache, tables in samples:  # warm-up + mode census
+        mode = run_layer(cache, tables)
+        modes[mode] = modes.get(mode, 0) + 1
+        escapes += oracle.escape_count(cache[:, ids].reshape(-1), tables)
+    times = []
+    for _ in range(repeats):
+        t = time.perf_counter()
+        for cache, tables in samples:
+            run_layer(cache, tables)
+        times.append(time.perf_counter() - t)
+    sec = statistics.median(times)
+    raw = 2 * n * layers
+    return raw / sec / 1e9, threads, escapes / (n * layers), modes
+
+
+def reference_arm(args):
+    """`--impl reference`: the reference's CPU codec path (restated by the
+    oracle), rank 0 only, bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from unchainkv_b200 import workloads
+
+    cfg = workloads.CONFIGS[args.workload]
+    gbs, threads, esc, modes = cpu_pipeline_gbs(cfg, max(1, args.cpu_layers), repeats=max(1, args.steps))
+    sample = f"{args.cpu_layers} of {cfg.layers} layers per step ({cfg.tokens} tokens, {cfg.kv_heads}x{cfg.head_dim})"
+    line = {
+        "impl": "reference",
+        "metric": "codec GB/s of raw bf16 KV per GPU (encode, decode) and % HBM peak; ratio",
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u16",
+        "data": "synthetic (seeded numpy draw of the config distribution)",
+        "config": {"workload": cfg.name, "layers": cfg.layers, "tokens": cfg.tokens,
+                   "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens,
+                   "pipeline": "top16 attempt -> fixed6 fallback -> decode (host threads)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample, "cpu": cpu_model(), "escape_rate": esc,
+                         "modes": {str(k): v for k, v in modes.items()}},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ B200
+
+
+def b200_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    from unchainkv_b200 import splitzip_cuda as S
+    from unchainkv_b200 import workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if not S.available():
+        raise RuntimeError(f"splitzip library missing: {S.load_error()}")
+
+    cfg = workloads.CONFIGS[args.workload]
+    L = cfg.layers
+    pool = cfg.blocks * cfg.pool_factor
+    n = cfg.words_per_layer
+    ids = workloads.block_table(pool, cfg.blocks, 3000)
+    ids2 = workloads.block_table(pool, cfg.blocks, 3001)
+    shape = (L, 2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim)
+    src = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    dst = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+    books = b"".join(workloads.fill_layer_device(src[l], cfg, l, ids) for l in range(L))
+    tables = torch.tensor(
+        np.frombuffer(b"".join(S.build_top16_tables(books[l * 32:(l + 1) * 32]) for l in range(L)), np.uint8)
+        .reshape(L, 544).copy(), device=device)
+    ids_t = torch.as_tensor(ids, device=device)
+    ids2_t = torch.as_tensor(ids2, device=device)
+    cap = S.auto_capacity(n)
+    streams = torch.zeros((L, cap), dtype=torch.uint8, device=device)
+    enc = S.job_array([S.make_job(src[l], ids_t, streams[l], cap, tables[l]) for l in range(L)])
+    dec = S.job_array([S.make_job(dst[l], ids2_t, streams[l], cap, tables[l]) for l in range(L)])
+    lib = S._load()
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+    raw_bytes = 2 * n * L
+
+    def encode():
+        if lib.kvq_splitzip_bf16_encode_auto_batch(enc, L, sp) <= 0:
+            raise RuntimeError("encode declined: " + lib.kvq_splitzip_last_error().decode())
+
+    def decode():
+        if lib.kvq_splitzip_bf16_decode_auto_batch(dec, L, sp) <= 0:
+            raise RuntimeError("decode declined: " + lib.kvq_splitzip_last_error().decode())
+
+    def step():
+        encode()
+        decode()
+
+    # correctness of the timed configuration (bitwise, every layer)
+    step()
+    torch.cuda.synchronize()
+    modes = streams[:, 0].cpu().tolist()
+    for l in range(L):
+        if not torch.equal(dst[l][:, ids2_t].view(torch.int16), src[l][:, ids_t].view(torch.int16)):
+            raise RuntimeError(f"layer {l}: round trip differs")
+    sizes = [S.stream_bytes(m, n) for m in modes]
+    escapes = 0
+    for l in range(L):
+        t = tables[l]
+        w = src[l][:, ids_t].reshape(2, -1).view(torch.int16).to(torch.int32) & 0xFFFF
+        e = (w >> 7) & 0xFF
+        esc_k = (t[:256][e[0].long()] == 255).sum()
+        esc_v = (t[256:512][e[1].long()] == 255).sum()
+        escapes += int(esc_k + esc_v)
+    encoded_total = sum(s for s in sizes if s)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end)
+        barrier()
+        if world > 1:
+            t = torch.tensor([ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    ms_step = timed(step, args.steps) / args.steps
+    if sampler:
+        sampler.stop()
+    ms_enc = timed(encode, args.steps) / args.steps
+    ms_dec = timed(decode, args.steps) / args.steps
+
+    # per-kernel device times over a second pass of the timed loop
+    prof_steps = max(1, min(args.steps, 200))
+    S.profile_enable(True)
+    for _ in range(prof_steps):
+        step()
+    prof = S.profile_collect()
+    S.profile_enable(False)
+
+    # e2e through the public API: encode -> mode bytes -> exact D2H into
+    # pinned host -> H2D into receive buffers -> decode
+    e2e = None
+    if not args.skip_e2e:
+        recv = torch.zeros((L, cap), dtype=torch.uint8, device=device)
+        host = torch.empty((L, cap), dtype=torch.uint8, pin_memory=True)
+        mode_host = torch.empty((L,), dtype=torch.uint8, pin_memory=True)
+        dec_recv = S.job_array([S.make_job(dst[l], ids2_t, recv[l], cap, tables[l]) for l in range(L)])
+        d2h = torch.cuda.Stream(device)
+        h2d = torch.cuda.Stream(device)
+        moved = {"h2d": 0, "d2h": 0}
+
+        def e2e_step():
+            S.encode_auto_batch(enc)
+            mode_host.copy_(streams[:, 0], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            lengths = [S.stream_bytes(int(m), n) for m in mode_host.tolist()]
+            if any(x is None for x in lengths):
+                raise RuntimeError("a layer produced no stream (mode 255)")
+            ready = torch.cuda.Event()
+            ready.record(stream)
+            d2h.wait_event(ready)
+            events = []
+            for l in range(L):
+                with torch.cuda.stream(d2h):
+                    host[l, : lengths[l]].copy_(streams[l, : lengths[l]], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(d2h)
+                h2d.wait_event(ev)
+                with torch.cuda.stream(h2d):
+                    recv[l, : lengths[l]].copy_(host[l, : lengths[l]], non_blocking=True)
+                    events.append(torch.cuda.Event())
+                    events[-1].record(h2d)
+            stream.wait_event(events[-1])
+            S.decode_auto_batch(dec_recv)
+            moved["d2h"] = sum(lengths) + L
+            moved["h2d"] = sum(lengths)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        end.record(stream)
+        end.synchronize()
+        e2e_ms = start.elapsed_time(end) / args.e2e_steps
+        wall_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        for l in range(L):
+            if not torch.equal(dst[l][:, ids2_t].view(torch.int16), src[l][:, ids_t].view(torch.int16)):
+                raise RuntimeError(f"e2e layer {l}: round trip differs")
+        e2e = {"value": round(world * raw_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": moved["h2d"], "d2h_bytes_per_step": moved["d2h"],
+               "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(wall_ms, 4),
+               "path": "encode_auto_batch -> D2H pinned -> H2D -> decode_auto_batch"}
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peak, peak_kind = peaks()
+    # algorithmic bytes per launch of each kernel of a step
+    mode_bytes = [(m, s) for m, s in zip(modes, sizes)]
+    stream_total = sum(s for _, s in mode_bytes)
+    alg = {
+        "StatsKernel": 2 * n * L,
+        "EncodeAutoKernel": 2 * n * L + stream_total,
+        "DecodeAutoKernel": stream_total + 2 * n * L,
+        "ZeroKernel": 64 * L,
+    }
+    kernels = {}
+    for name, (ms, launches) in prof.items():
+        per = ms / launches
+        kernels[name] = {"launches": launches, "ms_per_launch": round(per, 5),
+                         "alg_bytes_per_launch": alg.get(name),
+                         "gbs": round(alg[name] / (per * 1e-3) / 1e9, 1) if name in alg else None}
+    dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
+    dom = kernels[dominant]
+    traffic = None
+    tpath = ROOT / "profiles" / "ncu_traffic.json"
+    if tpath.exists():
+        traffic = json.loads(tpath.read_text()).get(args.workload, {}).get(dominant)
+    roofline = {"bound": "hbm", "kernel": dominant, "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": round(dom["gbs"] / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                "alg_bytes_per_launch": dom["alg_bytes_per_launch"]}
+    launches_per_step = sum(l for _, l in prof.values()) / prof_steps
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        gbs, threads, esc, cmodes = cpu_pipeline_gbs(cfg, max(1, args.cpu_layers))
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{args.cpu_layers} of {cfg.layers} layers, host numpy draw of the same distribution",
+               "cpu": cpu_model(), "escape_rate": round(esc, 5)}
+
+    value = world * raw_bytes / (ms_step * 1e-3) / 1e9
+    line = {
+        "metric": "codec GB/s of raw bf16 KV per GPU (encode, decode) and % HBM peak; ratio",
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u16",
+        "data": "synthetic (seeded device draw of the config distribution)",
+        "config": {
+            "workload": cfg.name, "layers": L, "tokens": cfg.tokens, "kv_heads": cfg.kv_heads,
+            "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens, "pool_blocks": pool,
+            "raw_bytes_per_step": raw_bytes, "encoded_bytes_per_step": encoded_total,
+            "policy": "device-chosen codec per layer (top16 -> fixed6 -> raw)",
+            "l2": "inputs larger than L2 (raw KV per step 512 MiB+)",
+            "parallelism": f"independent per-GPU shards x{world} (no collective)",
+        },
+        "encode_gbs_per_gpu": round(raw_bytes / (ms_enc * 1e-3) / 1e9, 2),
+        "decode_gbs_per_gpu": round(raw_bytes / (ms_dec * 1e-3) / 1e9, 2),
+        "ratio": round(raw_bytes / encoded_total, 4),
+        "escape_rate": round(escapes / (n * L), 5),
+        "modes": {str(m): modes.count(m) for m in sorted(set(modes))},
+        "hbm_frac_round_trip": round(sum(alg[k] for k in ("StatsKernel", "EncodeAutoKernel", "DecodeAutoKernel"))
+                                     / (ms_step * 1e-3) / 1e9 / peak, 4),
+        "roofline": roofline,
+        "kernels": kernels,
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "clocks": sampler.summary() if sampler else None,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        b200_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -82,7 +82,8 @@ KVQ_API long long kvq_splitzip_bf16_decode_fixed6(
  * books; code 255 = escape).  Escape entries are written in ascending
  * position order.  Scratch after the stream: the reference's 8 bytes plus
  * 16 + 8*ceil(count/8192) bytes at the next 16-byte aligned address
- * (a 2*count-byte buffer, as the reference's callers use, always fits). */
+ * (a 2*count-byte buffer, as the reference's callers use, always fits;
+ * the groups add 8*ceil(tiles/32) bytes). */
 KVQ_API long long kvq_splitzip_bf16_encode_top16(unsigned long long src_ptr,
                                                  unsigned long long dst_ptr,
                                                  unsigned long long count,
@@ -134,12 +135,87 @@ KVQ_API long long kvq_splitzip_bf16_encode_mode_blocks(
     unsigned long long block_count, unsigned long long dst_ptr,
     unsigned long long capacity, unsigned long long stream_ptr, int bits);
 
+/* One call of a batch: a layer (or a request's slice of a layer) of the paged
+ * cache and its stream buffer.  Encode reads `cache_ptr` through the block
+ * table and writes `stream_ptr` (capacity `stream_bytes`); decode reads
+ * `stream_bytes` bytes of `stream_ptr` and scatters into `cache_ptr`.
+ * `tables_ptr` is the layer's 544-byte top16 table (ignored by fixed6). */
+typedef struct kvq_splitzip_job {
+  unsigned long long cache_ptr;
+  unsigned long long plane_stride;
+  unsigned long long block_stride;
+  unsigned long long block_words;
+  unsigned long long block_ids_ptr;
+  unsigned long long block_start;
+  unsigned long long block_count;
+  unsigned long long stream_ptr;
+  unsigned long long stream_bytes;
+  unsigned long long tables_ptr;
+} kvq_splitzip_job;
+
+/* Batched forms: `count` jobs (host array) in as few launches as possible
+ * (up to 96 jobs per launch), so per-layer calls do not each pay a launch
+ * and a single wave of CTAs.  Each job follows the rules of its single-call
+ * counterpart; if any job would be declined nothing is launched and 0 is
+ * returned.  Encode returns the sum of the jobs' encoded sizes, decode the
+ * sum of raw bytes written.  Replaces the per-layer loop of
+ * kvq_splitzip_bf16_encode_top16 / _decode_top16_blocks calls the connector
+ * makes (src/unchain_kv/vllm_connector.py:3104-3118, 5139-5153). */
+KVQ_API long long kvq_splitzip_bf16_encode_top16_batch(const kvq_splitzip_job* jobs,
+                                                       unsigned long long count,
+                                                       unsigned long long stream_ptr);
+KVQ_API long long kvq_splitzip_bf16_encode_mode_batch(const kvq_splitzip_job* jobs,
+                                                      unsigned long long count,
+                                                      unsigned long long stream_ptr, int bits);
+KVQ_API long long kvq_splitzip_bf16_decode_top16_batch(const kvq_splitzip_job* jobs,
+                                                       unsigned long long count,
+                                                       unsigned long long stream_ptr);
+KVQ_API long long kvq_splitzip_bf16_decode_fixed6_batch(const kvq_splitzip_job* jobs,
+                                                        unsigned long long count,
+                                                        unsigned long long stream_ptr);
+
+/* Device-side codec choice: replaces the connector's host fallback chain
+ * top16 -> (D2H, mode byte 255) -> fixed6 -> raw mode 6
+ * (src/unchain_kv/vllm_connector.py:3104-3118, 4526-4633).  A read-only
+ * statistics pass counts top16 escapes and collects the high-byte palette;
+ * the encode pass then writes, per job, the stream the reference chain would
+ * end with: top16 (mode 5) if the escapes fit, else fixed6 (mode 3) if <= 64
+ * high bytes occur, else raw ([6] + words) when stream_bytes >=
+ * align16(2n+1) + scratch, else a fixed6 overflow stream (mode 255) for the
+ * host to replace with raw.  The stream's length follows from byte 0
+ * (5: 5+n+ceil(n/2)+5*ceil(n/200); 3: 65+n+3*ceil(n/4); 6: 2n+1).
+ * Scratch: 64 + 8*ceil(tiles/32) + 4*tiles bytes (tiles = ceil(n/8192)) at
+ * the 16-byte aligned end of the largest form.  Returns the sum over jobs of
+ * the largest form each job may produce. */
+KVQ_API long long kvq_splitzip_bf16_encode_auto_batch(const kvq_splitzip_job* jobs,
+                                                      unsigned long long count,
+                                                      unsigned long long stream_ptr);
+
+/* Decode whichever stream each job holds (mode 5, 3 or 6, read on the
+ * device); `stream_bytes` is the bytes available.  A stream shorter than its
+ * mode's length, or with another mode byte, leaves its blocks untouched. */
+KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_splitzip_job* jobs,
+                                                      unsigned long long count,
+                                                      unsigned long long stream_ptr);
+
 /* Count of device-side bounded waits that ran out on the current device
  * since load (0 in normal operation).  Synchronous; -1 on CUDA error. */
 KVQ_API long long kvq_splitzip_device_errors(void);
 
 /* ABI revision of the extension entry points. */
 KVQ_API long long kvq_splitzip_abi_version(void);
+
+/* Kernel profiler (extension; the device-side analogue of the reference's
+ * UNCHAIN_KV_TRACE_CUDA event pairs, src/unchain_kv/vllm_connector.py:
+ * 3100-3124).  enable(1) clears the record and brackets every later kernel
+ * launch of this library with CUDA events on its stream; collect() waits for
+ * the recorded launches and returns the number of distinct kernels; name(i),
+ * ms(i) and launches(i) read the per-kernel totals. */
+KVQ_API long long kvq_splitzip_profile_enable(int on);
+KVQ_API long long kvq_splitzip_profile_collect(void);
+KVQ_API const char* kvq_splitzip_profile_name(int i);
+KVQ_API double kvq_splitzip_profile_ms(int i);
+KVQ_API long long kvq_splitzip_profile_launches(int i);
 
 #ifdef __cplusplus
 }

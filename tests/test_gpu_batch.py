@@ -1,0 +1,242 @@
+"""GPU parity of the batched and device-chosen (auto) codec paths against the
+CPU oracle: every job of a batch must produce exactly the stream its single
+reference-style call would, and the auto path must end with the stream the
+reference's fallback chain (top16 -> fixed6 -> raw mode 6) ends with."""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import oracle  # noqa: E402
+from unchainkv_b200 import splitzip_cuda as S  # noqa: E402
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU"),
+]
+
+
+def tables_np(layer):
+    return np.frombuffer(S.build_top16_tables(S._DEFAULT_TOP16_CODEBOOKS[layer * 32: layer * 32 + 32]), np.uint8)
+
+
+def dev(a):
+    return torch.from_numpy(np.array(a, copy=True, order="C")).cuda()
+
+
+def to_u16(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def book_cache(rng, pool, shape, layer, rate, escape_choices=None):
+    books = S._DEFAULT_TOP16_CODEBOOKS[layer * 32: layer * 32 + 32]
+    n = 2 * pool * int(np.prod(shape))
+    book = np.frombuffer(books, np.uint8).reshape(2, 16)
+    plane = (np.arange(n) >= n // 2).astype(np.int64)
+    exp = book[plane, rng.integers(0, 16, n)].astype(np.int64)
+    outside = np.array([v for v in range(256) if v not in set(books)])
+    if escape_choices:
+        outside = outside[:escape_choices]
+    mask = rng.random(n) < rate
+    exp[mask] = rng.choice(outside, int(mask.sum()))
+    words = (rng.integers(0, 2, n) << 15) | (exp << 7) | rng.integers(0, 128, n)
+    return words.astype(np.uint16).reshape((2, pool) + shape)
+
+
+def make_case(rng, pool, shape, layer, rate, blocks=None, escape_choices=None):
+    cache = book_cache(rng, pool, shape, layer, rate, escape_choices)
+    blocks = blocks or pool // 2
+    ids = rng.permutation(pool)[:blocks].astype(np.int64)
+    return cache, ids, tables_np(layer)
+
+
+def job_for(kv, ids_t, buf, tables_t, stream_bytes=None):
+    return S.make_job(kv, ids_t, buf, stream_bytes, tables_t)
+
+
+def test_top16_and_fixed6_batches_match_single_calls():
+    rng = np.random.Generator(np.random.PCG64(1))
+    specs = [(40, (16, 8, 128), 0, 0.003), (300, (16, 1, 128), 5, 0.0045), (30, (7, 3), 9, 0.002),
+             (64, (16, 8, 128), 31, 0.0)]
+    cases, jobs, bufs, keep = [], [], [], []
+    for pool, shape, layer, rate in specs:
+        cache, ids, tab = make_case(rng, pool, shape, layer, rate)
+        kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+        ids_t, tab_t = dev(ids), dev(tab)
+        n = 2 * len(ids) * int(np.prod(shape))
+        buf = torch.zeros(2 * n + 4096, dtype=torch.uint8, device="cuda")
+        jobs.append(job_for(kv, ids_t, buf, tab_t))
+        cases.append((cache, ids, tab, n))
+        bufs.append(buf)
+        keep += [kv, ids_t, tab_t]
+    total = S.encode_top16_batch(jobs)
+    torch.cuda.synchronize()
+    expect = 0
+    for (cache, ids, tab, n), buf in zip(cases, bufs):
+        res, stream = oracle.encode_top16_blocks(cache, ids, tab)
+        expect += res
+        assert np.array_equal(buf.cpu().numpy()[:res], stream)
+    assert total == expect
+    # decode the batch into fresh caches with other block tables
+    targets, djobs = [], []
+    for (cache, ids, tab, n), buf in zip(cases, bufs):
+        ids2 = rng.permutation(cache.shape[1])[: len(ids)].astype(np.int64)
+        tgt = torch.zeros(cache.shape, dtype=torch.int16, device="cuda").view(torch.bfloat16)
+        ids2_t, tab_t = dev(ids2), dev(tab)
+        djobs.append(job_for(tgt, ids2_t, buf, tab_t, S.top16_stream_bytes(n)))
+        targets.append((tgt, ids2, cache, ids))
+        keep += [ids2_t, tab_t]
+    assert S.decode_top16_batch(djobs) == sum(2 * c[3] for c in cases)
+    torch.cuda.synchronize()
+    for tgt, ids2, cache, ids in targets:
+        assert np.array_equal(to_u16(tgt)[:, ids2], cache[:, ids])
+
+    # fixed6 batch
+    for buf in bufs:
+        buf.zero_()
+    total6 = S.encode_bf16_batch(jobs, bits=6)
+    torch.cuda.synchronize()
+    expect6 = 0
+    fixed_ok = []
+    for (cache, ids, tab, n), buf in zip(cases, bufs):
+        res, stream = oracle.encode_mode_blocks(cache, ids, bits=6)
+        expect6 += res
+        got = buf.cpu().numpy()
+        if stream[0] == 3:
+            assert np.array_equal(got[:res], stream)
+        else:  # more than 64 high bytes: mode 255 + canonical palette
+            assert got[0] == 255 and np.array_equal(got[:65], stream[:65])
+        fixed_ok.append(stream[0] == 3)
+    assert total6 == expect6
+    assert any(fixed_ok)
+    keep_jobs = [j for j, ok in zip(djobs, fixed_ok) if ok]
+    keep_targets = [t for t, ok in zip(targets, fixed_ok) if ok]
+    keep_cases = [c for c, ok in zip(cases, fixed_ok) if ok]
+    for j, (cache, ids, tab, n) in zip(keep_jobs, keep_cases):
+        j.stream_bytes = S.fixed6_stream_bytes(n)
+    for tgt, *_ in keep_targets:
+        tgt.zero_()
+    assert S.decode_fixed6_batch(keep_jobs) == sum(2 * c[3] for c in keep_cases)
+    torch.cuda.synchronize()
+    for tgt, ids2, cache, ids in keep_targets:
+        assert np.array_equal(to_u16(tgt)[:, ids2], cache[:, ids])
+
+
+def test_auto_picks_the_reference_chain_result():
+    rng = np.random.Generator(np.random.PCG64(2))
+    shape = (16, 8, 128)
+    kinds = []
+    # (a) escapes within capacity -> top16
+    kinds.append(("top16",) + make_case(rng, 48, shape, 3, 0.003))
+    # (b) escapes over capacity, <= 64 high bytes -> fixed6
+    kinds.append(("fixed6",) + make_case(rng, 48, shape, 4, 0.02, escape_choices=3))
+    # (c) > 64 distinct high bytes with room for raw -> raw mode 6
+    raw_cache = rng.integers(0, 1 << 16, size=(2, 48) + shape, dtype=np.uint16)
+    ids = rng.permutation(48)[:24].astype(np.int64)
+    kinds.append(("raw", raw_cache, ids, tables_np(0)))
+    # (d) same without room for raw -> mode 255
+    kinds.append(("overflow", raw_cache, ids, tables_np(0)))
+    jobs, bufs, keep = [], [], []
+    for kind, cache, ids, tab in kinds:
+        kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+        ids_t, tab_t = dev(ids), dev(tab)
+        n = 2 * len(ids) * int(np.prod(shape))
+        cap = S.auto_capacity(n, raw=(kind != "overflow"))
+        buf = torch.zeros(cap, dtype=torch.uint8, device="cuda")
+        jobs.append(job_for(kv, ids_t, buf, tab_t))
+        bufs.append(buf)
+        keep += [kv, ids_t, tab_t]
+    assert S.encode_auto_batch(jobs)
+    torch.cuda.synchronize()
+    for (kind, cache, ids, tab), buf in zip(kinds, bufs):
+        got = buf.cpu().numpy()
+        n = 2 * len(ids) * int(np.prod(shape))
+        if kind == "top16":
+            res, stream = oracle.encode_top16_blocks(cache, ids, tab)
+            assert stream[0] == 5 and np.array_equal(got[:res], stream)
+        elif kind == "fixed6":
+            assert oracle.encode_top16_blocks(cache, ids, tab)[1][0] == 255
+            res, stream = oracle.encode_mode_blocks(cache, ids, bits=6)
+            assert stream[0] == 3 and np.array_equal(got[:res], stream)
+        elif kind == "raw":
+            assert got[0] == 6
+            assert np.array_equal(got[1 : 1 + 2 * n].view(np.uint16), cache[:, ids].reshape(-1))
+        else:
+            res, stream = oracle.encode_mode_blocks(cache, ids, bits=6)
+            assert stream[0] == 255 and got[0] == 255
+            assert np.array_equal(got[1:65], stream[1:65])
+    # decode all four by mode byte; the overflow stream leaves its blocks alone
+    targets, djobs = [], []
+    for (kind, cache, ids, tab), buf in zip(kinds, bufs):
+        ids2 = rng.permutation(48)[: len(ids)].astype(np.int64)
+        tgt = torch.full(cache.shape, 7, dtype=torch.int16, device="cuda").view(torch.bfloat16)
+        ids2_t, tab_t = dev(ids2), dev(tab)
+        djobs.append(job_for(tgt, ids2_t, buf, tab_t))
+        targets.append((kind, tgt, ids2, cache, ids))
+        keep += [ids2_t, tab_t]
+    assert S.decode_auto_batch(djobs)
+    torch.cuda.synchronize()
+    for kind, tgt, ids2, cache, ids in targets:
+        got = to_u16(tgt)
+        if kind == "overflow":
+            assert (got == 7).all()
+        else:
+            assert np.array_equal(got[:, ids2], cache[:, ids]), kind
+
+
+def test_batch_larger_than_one_launch():
+    rng = np.random.Generator(np.random.PCG64(3))
+    pool, shape = 12, (16, 1, 128)
+    jobs, bufs, cases, keep = [], [], [], []
+    for i in range(100):
+        cache, ids, tab = make_case(rng, pool, shape, i % 32, 0.004, blocks=6)
+        kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+        ids_t, tab_t = dev(ids), dev(tab)
+        n = 2 * 6 * 2048
+        buf = torch.zeros(S.auto_capacity(n), dtype=torch.uint8, device="cuda")
+        jobs.append(job_for(kv, ids_t, buf, tab_t))
+        bufs.append(buf)
+        cases.append((cache, ids, tab))
+        keep += [kv, ids_t, tab_t]
+    assert S.encode_top16_batch(jobs) == sum(S.top16_stream_bytes(2 * 6 * 2048) for _ in range(100))
+    torch.cuda.synchronize()
+    for (cache, ids, tab), buf in zip(cases, bufs):
+        res, stream = oracle.encode_top16_blocks(cache, ids, tab)
+        assert np.array_equal(buf.cpu().numpy()[:res], stream)
+
+
+def test_batch_declines_as_a_whole():
+    rng = np.random.Generator(np.random.PCG64(4))
+    cache, ids, tab = make_case(rng, 16, (16, 8, 128), 0, 0.003)
+    kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+    ids_t, tab_t = dev(ids), dev(tab)
+    good = torch.full((1 << 20,), 0x5A, dtype=torch.uint8, device="cuda")
+    small = torch.full((64,), 0x5A, dtype=torch.uint8, device="cuda")
+    jobs = [job_for(kv, ids_t, good, tab_t), job_for(kv, ids_t, small, tab_t)]
+    assert S.encode_top16_batch(jobs) is None
+    torch.cuda.synchronize()
+    assert int(good[0].item()) == 0x5A  # nothing launched
+
+
+def test_profiler_counts_launches():
+    rng = np.random.Generator(np.random.PCG64(5))
+    cache, ids, tab = make_case(rng, 32, (16, 8, 128), 1, 0.02)
+    kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+    ids_t, tab_t = dev(ids), dev(tab)
+    n = 2 * len(ids) * 16 * 8 * 128
+    bufs = [torch.zeros(S.auto_capacity(n), dtype=torch.uint8, device="cuda") for _ in range(2)]
+    jobs = [job_for(kv, ids_t, buf, tab_t) for buf in bufs]
+    S.profile_enable(True)
+    try:
+        for _ in range(3):
+            S.encode_auto_batch(jobs)
+            S.decode_auto_batch(jobs)
+        prof = S.profile_collect()
+    finally:
+        S.profile_enable(False)
+    assert prof["StatsKernel"][1] == 3
+    assert prof["EncodeAutoKernel"][1] == 3
+    assert prof["DecodeAutoKernel"][1] == 3
+    assert prof["ZeroKernel"][1] == 3
+    assert all(ms > 0 for ms, _ in prof.values())

@@ -72,6 +72,26 @@ _SIGNATURES = {
     "kvq_splitzip_device_errors": [],
     "kvq_splitzip_abi_version": [],
 }
+_BATCH_SIGNATURES = {
+    "kvq_splitzip_bf16_encode_top16_batch": None,
+    "kvq_splitzip_bf16_encode_mode_batch": ctypes.c_int,
+    "kvq_splitzip_bf16_encode_auto_batch": None,
+    "kvq_splitzip_bf16_decode_top16_batch": None,
+    "kvq_splitzip_bf16_decode_fixed6_batch": None,
+    "kvq_splitzip_bf16_decode_auto_batch": None,
+}
+
+
+class KvqJob(ctypes.Structure):
+    """``kvq_splitzip_job`` of include/unchain_kv_splitzip.h: one call of a batch."""
+
+    _fields_ = [
+        (name, ctypes.c_ulonglong)
+        for name in (
+            "cache_ptr", "plane_stride", "block_stride", "block_words", "block_ids_ptr",
+            "block_start", "block_count", "stream_ptr", "stream_bytes", "tables_ptr",
+        )
+    ]
 
 
 def library_path() -> Path:
@@ -104,8 +124,22 @@ def _load():
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
                 fn.restype = ctypes.c_longlong
+            for name, extra in _BATCH_SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = [ctypes.POINTER(KvqJob), _U64, _U64] + ([extra] if extra else [])
+                fn.restype = ctypes.c_longlong
             lib.kvq_splitzip_last_error.argtypes = []
             lib.kvq_splitzip_last_error.restype = ctypes.c_char_p
+            lib.kvq_splitzip_profile_enable.argtypes = [ctypes.c_int]
+            lib.kvq_splitzip_profile_enable.restype = ctypes.c_longlong
+            lib.kvq_splitzip_profile_collect.argtypes = []
+            lib.kvq_splitzip_profile_collect.restype = ctypes.c_longlong
+            lib.kvq_splitzip_profile_name.argtypes = [ctypes.c_int]
+            lib.kvq_splitzip_profile_name.restype = ctypes.c_char_p
+            lib.kvq_splitzip_profile_ms.argtypes = [ctypes.c_int]
+            lib.kvq_splitzip_profile_ms.restype = ctypes.c_double
+            lib.kvq_splitzip_profile_launches.argtypes = [ctypes.c_int]
+            lib.kvq_splitzip_profile_launches.restype = ctypes.c_longlong
             _LIB = lib
             _LOAD_ERROR = None
             return lib
@@ -482,3 +516,136 @@ def device_errors() -> int:
     if value < 0:
         _raise_last(lib, "splitzip device error query failed")
     return int(value)
+
+
+# --------------------------------------------------------------- batches
+
+
+def top16_stream_bytes(n: int) -> int:
+    """Length of a top16 (mode 5) stream of n words."""
+    return 5 + n + (n + 1) // 2 + 5 * ((n + 199) // 200)
+
+
+def fixed6_stream_bytes(n: int) -> int:
+    """Length of a fixed6 (mode 3) stream of n words."""
+    return 65 + n + ((n + 3) // 4) * 3
+
+
+def stream_bytes(mode: int, n: int) -> int | None:
+    """Length of a stream of n words from its mode byte (None: no stream)."""
+    if mode == 5:
+        return top16_stream_bytes(n)
+    if mode == 3:
+        return fixed6_stream_bytes(n)
+    if mode == 6:
+        return 1 + 2 * n
+    return None
+
+
+def auto_capacity(n: int, raw: bool = True) -> int:
+    """Stream-buffer bytes for encode_auto_batch: room for the largest form
+    (raw mode 6 when ``raw``) plus the statistics scratch."""
+    tiles = (n + 8191) // 8192
+    scratch = 64 + 8 * ((tiles + 31) // 32) + 4 * tiles
+    largest = 1 + 2 * n if raw else max(top16_stream_bytes(n), fixed6_stream_bytes(n))
+    return ((largest + 15) // 16) * 16 + scratch + 16
+
+
+def make_job(kv_layer, block_ids, stream_buffer, stream_bytes_: int | None = None, tables=None,
+             block_start: int = 0, block_count: int | None = None) -> KvqJob:
+    """Describe one call: ``kv_layer`` [2, num_blocks, ...] (bf16, blocks
+    contiguous), ``block_ids`` an int64 device tensor (or None with
+    ``block_start``/``block_count`` for a contiguous run), ``stream_buffer``
+    a uint8 device tensor (its size is the capacity unless
+    ``stream_bytes_`` is given), ``tables`` the layer's 544-byte table."""
+    block_words = 1
+    for size in kv_layer.shape[2:]:
+        block_words *= int(size)
+    if block_ids is not None:
+        block_count = int(block_ids.numel())
+    job = KvqJob()
+    job.cache_ptr = int(kv_layer.data_ptr())
+    job.plane_stride = int(kv_layer.stride(0))
+    job.block_stride = int(kv_layer.stride(1))
+    job.block_words = block_words
+    job.block_ids_ptr = int(block_ids.data_ptr()) if block_ids is not None else 0
+    job.block_start = int(block_start)
+    job.block_count = int(block_count)
+    job.stream_ptr = int(stream_buffer.data_ptr())
+    job.stream_bytes = int(stream_bytes_ if stream_bytes_ is not None else stream_buffer.numel())
+    job.tables_ptr = int(tables.data_ptr()) if tables is not None else 0
+    return job
+
+
+def job_array(jobs) -> "ctypes.Array":
+    array = (KvqJob * len(jobs))()
+    for i, job in enumerate(jobs):
+        array[i] = job
+    return array
+
+
+def _run_batch(name: str, jobs, stream=None, extra=None) -> int | None:
+    lib = _require_lib()
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream().cuda_stream
+    array = jobs if isinstance(jobs, ctypes.Array) else job_array(list(jobs))
+    args = [array, len(array), int(stream)] + ([extra] if extra is not None else [])
+    result = getattr(lib, name)(*args)
+    if result < 0:
+        _raise_last(lib, f"{name} failed")
+    return int(result) or None
+
+
+def encode_top16_batch(jobs, stream=None) -> int | None:
+    """Fused gather + top16 encode of every job in one launch; returns the
+    total encoded bytes, None if any job is declined (nothing launched)."""
+    return _run_batch("kvq_splitzip_bf16_encode_top16_batch", jobs, stream)
+
+
+def encode_bf16_batch(jobs, bits: int = 6, stream=None) -> int | None:
+    if bits not in {5, 6}:
+        raise ValueError("splitzip bf16 bits must be 5 or 6")
+    return _run_batch("kvq_splitzip_bf16_encode_mode_batch", jobs, stream, int(bits))
+
+
+def encode_auto_batch(jobs, stream=None) -> int | None:
+    """Device-chosen codec per job (top16, else fixed6, else raw, else 255);
+    byte 0 of each stream tells which (see ``stream_bytes``)."""
+    return _run_batch("kvq_splitzip_bf16_encode_auto_batch", jobs, stream)
+
+
+def decode_top16_batch(jobs, stream=None) -> int | None:
+    return _run_batch("kvq_splitzip_bf16_decode_top16_batch", jobs, stream)
+
+
+def decode_fixed6_batch(jobs, stream=None) -> int | None:
+    return _run_batch("kvq_splitzip_bf16_decode_fixed6_batch", jobs, stream)
+
+
+def decode_auto_batch(jobs, stream=None) -> int | None:
+    """Decode each job's stream by its mode byte (5, 3 or 6) on the device."""
+    return _run_batch("kvq_splitzip_bf16_decode_auto_batch", jobs, stream)
+
+
+# --------------------------------------------------------------- profiler
+
+
+def profile_enable(on: bool = True) -> None:
+    """Start (or stop) bracketing this library's kernel launches with CUDA
+    events; clears earlier records."""
+    _require_lib().kvq_splitzip_profile_enable(1 if on else 0)
+
+
+def profile_collect() -> dict[str, tuple[float, int]]:
+    """Wait for the recorded launches; {kernel: (total device ms, launches)}."""
+    lib = _require_lib()
+    count = lib.kvq_splitzip_profile_collect()
+    if count < 0:
+        _raise_last(lib, "profile collect failed")
+    return {
+        lib.kvq_splitzip_profile_name(i).decode(): (
+            float(lib.kvq_splitzip_profile_ms(i)), int(lib.kvq_splitzip_profile_launches(i)))
+        for i in range(count)
+    }
