@@ -205,6 +205,26 @@ KVQ_API long long kvq_splitzip_device_errors(void);
 /* ABI revision of the extension entry points. */
 KVQ_API long long kvq_splitzip_abi_version(void);
 
+/* top16 encode that allocates nothing (no counterpart in the reference).
+ * Same arguments, stream bytes and return values as
+ * kvq_splitzip_bf16_encode_top16, for callers that cannot allocate device
+ * memory or leave no spare bytes past the stream (graph capture, serving
+ * engines that give all of HBM to their KV pool, runtimes that size stream
+ * buffers exactly): the tile-scan scratch lives in a 135,184-byte static
+ * device array of this library, held by every GPU that loads it until exit.
+ * Needs only the reference's capacity (align4(encoded) + 8).  count above
+ * 2^27 words (134,217,728) returns -1 with a message in
+ * kvq_splitzip_last_error().  The first call on a device looks up the
+ * array's device address with that device current; make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * (concurrent streams, or graphs replayed concurrently) race. */
+KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned long long src_ptr,
+                                                         unsigned long long dst_ptr,
+                                                         unsigned long long count,
+                                                         unsigned long long capacity,
+                                                         unsigned long long tables_ptr,
+                                                         unsigned long long stream_ptr);
+
 /* Kernel profiler (extension; the device-side analogue of the reference's
  * UNCHAIN_KV_TRACE_CUDA event pairs, src/unchain_kv/vllm_connector.py:
  * 3100-3124).  enable(1) clears the record and brackets every later kernel

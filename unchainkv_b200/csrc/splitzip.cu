@@ -673,3 +673,110 @@ extern "C" KVQ_API long long kvq_splitzip_profile_launches(int i) {
   std::lock_guard<std::mutex> lock(g_prof_mu);
   return i >= 0 && i < static_cast<int>(g_prof_launches.size()) ? g_prof_launches[i] : 0;
 }
+
+// ---------------------------------------------------------------------
+// top16 encode that allocates nothing and needs no scratch in the caller's
+// buffer.
+//
+// Some callers cannot allocate device memory on the encode path:
+// - code being captured into a CUDA graph, where allocation is not allowed
+//   and every address must stay fixed across replays;
+// - serving engines that hand nearly all of HBM to their own paged KV pool
+//   (vLLM's gpu_memory_utilization), where a transient allocation can fail;
+// - plugins whose host runtime owns device memory and sizes each stream
+//   buffer exactly to the stream, leaving no spare bytes past it for the
+//   scratch kvq_splitzip_bf16_encode_top16 keeps there.
+// This variant keeps its tile-scan scratch in a fixed device array of this
+// library instead.  The array is part of the module image: every GPU that
+// loads the library holds it until process exit, and no call here (or in the
+// kernel) allocates or frees memory.
+// ---------------------------------------------------------------------
+
+namespace {
+
+// Largest `count` the static scratch covers: 2^27 words (256 MiB of raw bf16,
+// 16384 tiles); the array is 16 + 8*512 + 8*16384 = 135184 bytes.
+constexpr uint64_t kNoAllocMaxWords = 1ull << 27;
+constexpr uint64_t kNoAllocTiles = (kNoAllocMaxWords + kTileWords - 1) / kTileWords;
+constexpr uint64_t kNoAllocScratchBytes = top16_scratch_bytes(kNoAllocTiles);
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on each device.  Host code cannot use
+// the symbol itself (it names a host-side shadow); the address is looked up
+// once per device, with that device current, the first time this entry point
+// runs on it.
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_address[kNoAllocMaxDevices] = {};
+
+void* noalloc_scratch_for_current_device() {
+  int device = 0;
+  cudaError_t st = cudaGetDevice(&device);
+  if (st != cudaSuccess) {
+    Fail("cudaGetDevice", st);
+    return nullptr;
+  }
+  if (device < 0 || device >= kNoAllocMaxDevices) {
+    g_last_error = "kvq_splitzip_bf16_encode_top16_noalloc: device index out of range";
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_address[device] == nullptr) {
+    void* address = nullptr;
+    st = cudaGetSymbolAddress(&address, g_noalloc_scratch);
+    if (st != cudaSuccess) {
+      Fail("cudaGetSymbolAddress", st);
+      return nullptr;
+    }
+    g_noalloc_address[device] = address;
+  }
+  return g_noalloc_address[device];
+}
+
+}  // namespace
+
+extern "C" KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned long long src_ptr,
+                                                                    unsigned long long dst_ptr,
+                                                                    unsigned long long count,
+                                                                    unsigned long long capacity,
+                                                                    unsigned long long tables_ptr,
+                                                                    unsigned long long stream_ptr) {
+  if (src_ptr == 0 || dst_ptr == 0 || tables_ptr == 0 || count == 0 || count > 0xFFFFFFFFULL) {
+    return 0;
+  }
+  if (count > kNoAllocMaxWords) {
+    g_last_error = "kvq_splitzip_bf16_encode_top16_noalloc: count " + std::to_string(count) +
+                   " words exceeds the static scratch maximum of " +
+                   std::to_string(kNoAllocMaxWords) + " words";
+    return -1;
+  }
+  const uint64_t n = count;
+  const uint64_t encoded = top16_size(n);
+  // the reference's decline rules (.cu:385-395); no room past the stream is
+  // needed beyond the reference's own 8 bytes
+  if (encoded >= n * 2 || ((encoded + 3) & ~3ULL) + 8 > capacity) return 0;
+  void* scratch = noalloc_scratch_for_current_device();
+  if (scratch == nullptr) return -1;
+  auto* dst = reinterpret_cast<uint8_t*>(dst_ptr);
+  const auto stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  EncBatch<1> b{};
+  b.jobs = 1;
+  b.job[0] = base_job(reinterpret_cast<const uint16_t*>(src_ptr), flat_layout(n), dst,
+                      reinterpret_cast<const uint8_t*>(tables_ptr));
+  b.job[0].scratch = static_cast<uint8_t*>(scratch);
+  b.tile_start[0] = 0;
+  b.tile_start[1] = b.job[0].tiles;
+  // Every call shares the array and finds the previous call's contents in
+  // it: clear the ticket, error flag, group and status words, and the escape
+  // entries of the stream (unused slots must read zero).
+  const uint64_t entries = 5 + n + (n + 1) / 2;
+  cudaError_t st = cudaMemsetAsync(dst + entries, 0, encoded - entries, stream);
+  if (st != cudaSuccess) return Fail("cudaMemsetAsync", st);
+  st = cudaMemsetAsync(scratch, 0, top16_scratch_bytes(b.job[0].tiles), stream);
+  if (st != cudaSuccess) return Fail("cudaMemsetAsync", st);
+  EncodeTop16Kernel<1><<<b.job[0].tiles, kThreads, 0, stream>>>(b);
+  st = cudaGetLastError();
+  if (st != cudaSuccess) return Fail("EncodeTop16Kernel", st);
+  return static_cast<long long>(encoded);
+}

@@ -69,6 +69,7 @@ _SIGNATURES = {
     "kvq_splitzip_bf16_decode_top16_blocks": [_U64] * 12,
     "kvq_splitzip_bf16_encode_top16_blocks": [_U64] * 11,
     "kvq_splitzip_bf16_encode_mode_blocks": [_U64] * 10 + [ctypes.c_int],
+    "kvq_splitzip_bf16_encode_top16_noalloc": [_U64] * 6,
     "kvq_splitzip_device_errors": [],
     "kvq_splitzip_abi_version": [],
 }
