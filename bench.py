@@ -53,6 +53,8 @@ def parse_args():
     p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
+    p.add_argument("--layers", type=int, default=None,
+                   help="override the layer count (small ncu captures only; the bench line uses the config's)")
     return p.parse_args()
 
 
@@ -259,6 +261,10 @@ def b200_arm(args):
         raise RuntimeError(f"splitzip library missing: {S.load_error()}")
 
     cfg = workloads.CONFIGS[args.workload]
+    if args.layers:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, layers=args.layers)
     L = cfg.layers
     pool = cfg.blocks * cfg.pool_factor
     n = cfg.words_per_layer

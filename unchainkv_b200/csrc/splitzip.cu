@@ -93,6 +93,52 @@ void prof_end(long long slot, const char* name, cudaStream_t stream) {
   cudaEventRecord(g_prof_pending[slot].end, stream);
 }
 
+// ----------------------------------------------------------- launch sizing
+//
+// The kernels are persistent: the grid is the number of CTAs that fit on the
+// device at once (occupancy x SMs), capped by the tile count.  Dynamic
+// shared memory above 48 KiB is opted into once per kernel and device.
+
+struct GeometryKey {
+  const void* kernel;
+  int device;
+  bool operator<(const GeometryKey& o) const {
+    return kernel < o.kernel || (kernel == o.kernel && device < o.device);
+  }
+};
+
+std::mutex g_geometry_mu;
+std::map<GeometryKey, int> g_geometry;  // resident CTAs per device
+
+template <typename Kernel>
+long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* grid) {
+  int device = 0;
+  cudaError_t st = cudaGetDevice(&device);
+  if (st != cudaSuccess) return Fail("cudaGetDevice", st);
+  const GeometryKey key{reinterpret_cast<const void*>(kernel), device};
+  int resident = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_geometry_mu);
+    auto it = g_geometry.find(key);
+    if (it != g_geometry.end()) resident = it->second;
+  }
+  if (resident == 0) {
+    st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn_smem));
+    if (st != cudaSuccess) return Fail("cudaFuncSetAttribute", st);
+    int per_sm = 0, sms = 0;
+    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kCtaThreads, dyn_smem);
+    if (st != cudaSuccess) return Fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", st);
+    st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
+    resident = std::max(1, per_sm) * std::max(1, sms);
+    std::lock_guard<std::mutex> lock(g_geometry_mu);
+    g_geometry[key] = resident;
+  }
+  *grid = static_cast<unsigned>(std::min<uint64_t>(tiles, static_cast<uint64_t>(resident)));
+  if (*grid == 0) *grid = 1;
+  return 0;
+}
+
 // ------------------------------------------------------------------ layouts
 
 int log2_exact(uint64_t v) {
@@ -228,7 +274,7 @@ bool prepare_auto(const uint16_t* src, const Layout& L, uint8_t* dst, uint64_t c
   p.job.raw_ok = raw_ok;
   p.job.scratch = dst + (raw_ok ? raw_so : so);
   p.zero_ptr = p.job.scratch;
-  p.zero_bytes = 64;
+  p.zero_bytes = scratch;  // totals, bitmap, group sums and tile counts start at zero
   p.result = raw_ok ? 1 + 2 * n : compressed;
   return true;
 }
@@ -277,6 +323,44 @@ long long launch_zero(const std::vector<Prepared>& jobs, size_t first, size_t co
   return st == cudaSuccess ? 0 : Fail("ZeroKernel", st);
 }
 
+// Launch one persistent kernel over `tiles` tiles, bracketed by the profiler.
+template <typename Kernel, typename Batch>
+long long launch_persistent(Kernel kernel, const char* name, size_t dyn_smem, const Batch& b, uint64_t tiles,
+                            cudaStream_t stream) {
+  unsigned grid = 0;
+  const long long rc = grid_for(kernel, dyn_smem, tiles, &grid);
+  if (rc < 0) return rc;
+  const long long prof = prof_begin(stream);
+  kernel<<<grid, kCtaThreads, dyn_smem, stream>>>(b);
+  prof_end(prof, name, stream);
+  const cudaError_t st = cudaGetLastError();
+  return st == cudaSuccess ? 0 : Fail(name, st);
+}
+
+template <int kMax>
+long long launch_encode_kernels(EncOp op, const EncBatch<kMax>& b, uint32_t tiles, cudaStream_t stream) {
+  switch (op) {
+    case EncOp::kTop16:
+      return launch_persistent(EncodeTop16Kernel<kMax>, "EncodeTop16Kernel", kEncSmemBytes, b, tiles, stream);
+    case EncOp::kFixed6:
+    case EncOp::kFixed5: {
+      const long long rc =
+          launch_persistent(PresenceKernel<kMax, false>, "PresenceKernel", kEncSmemBytes, b, tiles, stream);
+      if (rc < 0) return rc;
+      return op == EncOp::kFixed6
+                 ? launch_persistent(EncodeFixedKernel<kMax, 6>, "EncodeFixed6Kernel", kEncSmemBytes, b, tiles, stream)
+                 : launch_persistent(EncodeFixedKernel<kMax, 5>, "EncodeFixed5Kernel", kEncSmemBytes, b, tiles, stream);
+    }
+    case EncOp::kAuto: {
+      const long long rc =
+          launch_persistent(PresenceKernel<kMax, true>, "StatsKernel", kEncSmemBytes, b, tiles, stream);
+      if (rc < 0) return rc;
+      return launch_persistent(EncodeAutoKernel<kMax>, "EncodeAutoKernel", kEncSmemBytes, b, tiles, stream);
+    }
+  }
+  return 0;
+}
+
 template <int kMax>
 long long launch_encode(EncOp op, const std::vector<Prepared>& jobs, size_t first, size_t count,
                         cudaStream_t stream) {
@@ -291,46 +375,7 @@ long long launch_encode(EncOp op, const std::vector<Prepared>& jobs, size_t firs
     tiles += b.job[i].tiles;
   }
   b.tile_start[count] = tiles;
-  const char* name = "";
-  long long prof = -1;
-  switch (op) {
-    case EncOp::kTop16:
-      name = "EncodeTop16Kernel";
-      prof = prof_begin(stream);
-      EncodeTop16Kernel<kMax><<<tiles, kThreads, 0, stream>>>(b);
-      break;
-    case EncOp::kFixed6:
-    case EncOp::kFixed5: {
-      prof = prof_begin(stream);
-      PresenceKernel<kMax, false><<<tiles, kThreads, 0, stream>>>(b);
-      prof_end(prof, "PresenceKernel", stream);
-      const cudaError_t st = cudaGetLastError();
-      if (st != cudaSuccess) return Fail("PresenceKernel", st);
-      prof = prof_begin(stream);
-      if (op == EncOp::kFixed6) {
-        name = "EncodeFixed6Kernel";
-        EncodeFixedKernel<kMax, 6><<<tiles, kThreads, 0, stream>>>(b);
-      } else {
-        name = "EncodeFixed5Kernel";
-        EncodeFixedKernel<kMax, 5><<<tiles, kThreads, 0, stream>>>(b);
-      }
-      break;
-    }
-    case EncOp::kAuto: {
-      prof = prof_begin(stream);
-      PresenceKernel<kMax, true><<<tiles, kThreads, 0, stream>>>(b);
-      prof_end(prof, "StatsKernel", stream);
-      const cudaError_t st = cudaGetLastError();
-      if (st != cudaSuccess) return Fail("StatsKernel", st);
-      name = "EncodeAutoKernel";
-      prof = prof_begin(stream);
-      EncodeAutoKernel<kMax><<<tiles, kThreads, 0, stream>>>(b);
-      break;
-    }
-  }
-  prof_end(prof, name, stream);
-  const cudaError_t st = cudaGetLastError();
-  return st == cudaSuccess ? 0 : Fail(name, st);
+  return launch_encode_kernels(op, b, tiles, stream);
 }
 
 long long run_encode(EncOp op, const std::vector<Prepared>& jobs, cudaStream_t stream) {
@@ -362,11 +407,7 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
   b.tile_start[count] = tiles;
   const char* name =
       kMode == 5 ? "DecodeTop16Kernel" : kMode == 3 ? "DecodeFixed6Kernel" : "DecodeAutoKernel";
-  const long long prof = prof_begin(stream);
-  DecodeKernel<kMax, kMode><<<tiles, kThreads, 0, stream>>>(b);
-  prof_end(prof, name, stream);
-  const cudaError_t st = cudaGetLastError();
-  return st == cudaSuccess ? 0 : Fail(name, st);
+  return launch_persistent(DecodeKernel<kMax, kMode>, name, kDecSmemBytes, b, tiles, stream);
 }
 
 template <int kMode>
@@ -775,8 +816,7 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned lon
   if (st != cudaSuccess) return Fail("cudaMemsetAsync", st);
   st = cudaMemsetAsync(scratch, 0, top16_scratch_bytes(b.job[0].tiles), stream);
   if (st != cudaSuccess) return Fail("cudaMemsetAsync", st);
-  EncodeTop16Kernel<1><<<b.job[0].tiles, kThreads, 0, stream>>>(b);
-  st = cudaGetLastError();
-  if (st != cudaSuccess) return Fail("EncodeTop16Kernel", st);
-  return static_cast<long long>(encoded);
+  const long long rc =
+      launch_persistent(EncodeTop16Kernel<1>, "EncodeTop16Kernel", kEncSmemBytes, b, b.job[0].tiles, stream);
+  return rc < 0 ? rc : static_cast<long long>(encoded);
 }

@@ -96,22 +96,27 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
       : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// One try_wait that suspends the thread (up to `hint_ns`) while the phase is
+// incomplete, so a waiting warp does not spin on the issue slots of the
+// warps that are working.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase.  Returns false if the limit ran out.
+// Bounded wait on an mbarrier phase: at most kBarrierTries suspended tries of
+// up to 1 ms each.  Returns false if the limit ran out.
+constexpr uint32_t kBarrierTries = 4096;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+  for (uint32_t i = 0; i < kBarrierTries; ++i) {
+    if (mbar_try_wait(bar, parity, 1000000u)) return true;
   }
   return false;
 }
@@ -142,6 +147,15 @@ __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
 }
 
 // ------------------------------------------------------- warp funnel store
+
+// Byte store to global memory under a predicate (no branch).
+__device__ __forceinline__ void st_global_u8_if(bool p, uint8_t* a, uint32_t v) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %0, 0;\n\t@q st.global.u8 [%1], %2;\n\t}" ::"r"(
+          static_cast<uint32_t>(p)),
+      "l"(a), "r"(v)
+      : "memory");
+}
 
 // Store bytes [max(slot,lo), min(slot+S,hi)) of the little-endian value v
 // that belongs at `slot` (an S-aligned address).  Full slots use one aligned
@@ -205,6 +219,109 @@ __device__ __forceinline__ void warp_store(uint8_t* g, uint32_t valid, const T (
   }
 }
 
+// Bytes [0, count) of the little-endian value v to the (unaligned) address a.
+__device__ __forceinline__ void store_bytes(uintptr_t a, uint64_t v, uint32_t count) {
+  for (uint32_t i = 0; i < count; ++i) reinterpret_cast<uint8_t*>(a)[i] = static_cast<uint8_t>(v >> (8 * i));
+}
+
+// warp_store for a run whose 32*K*S bytes are all valid: every interior slot
+// is one aligned S-byte store; only lane 0's head and lane 31's tail (less
+// than S bytes each) are written bytewise.
+template <typename T, int K>
+__device__ __forceinline__ void warp_store_full(uint8_t* g, const T (&d)[K], int lane) {
+  constexpr uint32_t S = sizeof(T);
+  const uintptr_t base = reinterpret_cast<uintptr_t>(g);
+  const uint32_t s = static_cast<uint32_t>(base % S);
+  if (s == 0) {
+    T* p = reinterpret_cast<T*>(base) + lane * K;
+#pragma unroll
+    for (int k = 0; k < K; ++k) p[k] = d[k];
+    return;
+  }
+  const T next0 = __shfl_down_sync(kFull, d[0], 1);
+  T* slots = reinterpret_cast<T*>(base - s) + lane * K + 1;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const uint64_t cur = static_cast<uint64_t>(d[k]);
+    const uint64_t nxt = static_cast<uint64_t>(k + 1 < K ? d[(k + 1) % K] : next0);
+    const uint64_t v = (cur >> (8 * (S - s))) | (nxt << (8 * s));
+    if (k < K - 1 || lane < 31) slots[k] = static_cast<T>(v);
+  }
+  if (lane == 0) store_bytes(base, static_cast<uint64_t>(d[0]), S - s);
+  if (lane == 31) store_bytes(base + 32 * K * S - s, static_cast<uint64_t>(d[K - 1]) >> (8 * (S - s)), s);
+}
+
+// warp_store_full on 32-bit words: lane L owns the NW words D (bytes
+// [g + 4*NW*L, g + 4*NW*(L+1))) and writes aligned S-byte slots (S = 4 or 8,
+// 4*NW a multiple of S).  The slot data comes from one uniform word select
+// and one funnel shift per word; the less-than-S bytes at each end of the run
+// are written by up to 7 lanes with one byte store each (no divergent loop).
+template <int NW, int S>
+__device__ __forceinline__ void warp_store_words(uint8_t* g, const uint32_t (&D)[NW], int lane) {
+  static_assert(S == 4 || S == 8, "slot size");
+  static_assert((4 * NW) % S == 0, "whole slots per lane");
+  const uintptr_t base = reinterpret_cast<uintptr_t>(g);
+  const uint32_t s = static_cast<uint32_t>(base % S);
+  if (s == 0) {
+    if (S == 8) {
+      uint2* p = reinterpret_cast<uint2*>(base) + lane * (NW / 2);
+#pragma unroll
+      for (int k = 0; k < NW / 2; ++k) p[k] = make_uint2(D[2 * k], D[2 * k + 1]);
+    } else {
+      uint32_t* p = reinterpret_cast<uint32_t*>(base) + lane * NW;
+#pragma unroll
+      for (int k = 0; k < NW; ++k) p[k] = D[k];
+    }
+    return;
+  }
+  const uint32_t o = S - s;                 // run bytes before the first aligned slot
+  const bool q = (o & 4) != 0;              // word offset of that slot in the lane's data
+  const uint32_t r = (o & 3) * 8;           // bit offset inside the word
+  // the lane's words followed by the next lane's first two
+  uint32_t W[NW + 2];
+#pragma unroll
+  for (int k = 0; k < NW; ++k) W[k] = D[k];
+  W[NW] = __shfl_down_sync(kFull, D[0], 1);
+  W[NW + 1] = NW > 1 ? __shfl_down_sync(kFull, D[NW > 1 ? 1 : 0], 1) : 0u;
+  uint32_t Wq[NW + 1];
+#pragma unroll
+  for (int k = 0; k < NW + 1; ++k) Wq[k] = q ? W[k + 1] : W[k];
+  uint32_t out[NW];
+#pragma unroll
+  for (int k = 0; k < NW; ++k) out[k] = __funnelshift_r(Wq[k], Wq[k + 1], r);
+  // aligned slots; lane 31's last slot reaches past the run and is left to
+  // the tail bytes below
+  const uintptr_t first = base + o + static_cast<uintptr_t>(lane) * 4 * NW;
+  if (S == 8) {
+    uint2* p = reinterpret_cast<uint2*>(first);
+#pragma unroll
+    for (int k = 0; k < NW / 2; ++k)
+      if (k < NW / 2 - 1 || lane < 31) p[k] = make_uint2(out[2 * k], out[2 * k + 1]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < NW; ++k)
+      if (k < NW - 1 || lane < 31) reinterpret_cast<uint32_t*>(first)[k] = out[k];
+  }
+  // head: run bytes [0, o) are lane 0's first bytes; tail: the run's last s
+  // bytes are lane 31's last bytes
+  const uint32_t h0 = __shfl_sync(kFull, D[0], 0);
+  const uint32_t h1 = __shfl_sync(kFull, D[NW > 1 ? 1 : 0], 0);
+  const uint32_t t0 = __shfl_sync(kFull, D[NW > 1 ? NW - 2 : 0], 31);
+  const uint32_t t1 = __shfl_sync(kFull, D[NW - 1], 31);
+  {
+    const uint32_t word = lane < 4 ? h0 : h1;
+    st_global_u8_if(static_cast<uint32_t>(lane) < o, reinterpret_cast<uint8_t*>(base) + lane,
+                    (word >> (8 * (lane & 3))) & 0xFFu);
+  }
+  {
+    // byte (4*NW - s + lane) of lane 31's data
+    const uint32_t idx = 4 * NW - s + lane;
+    const uint32_t word = (idx >> 2) == static_cast<uint32_t>(NW - 1) ? t1 : t0;
+    st_global_u8_if(static_cast<uint32_t>(lane) < s, reinterpret_cast<uint8_t*>(base + 32 * 4 * NW - s) + lane,
+                    (word >> (8 * (idx & 3))) & 0xFFu);
+  }
+}
+
 // Read 16 bytes starting at an arbitrary byte offset of a 4-byte aligned
 // shared buffer (the buffer must extend 4 bytes past the read).
 __device__ __forceinline__ void smem_read16(const uint8_t* buf, uint32_t off, uint32_t (&out)[4]) {
@@ -215,6 +332,45 @@ __device__ __forceinline__ void smem_read16(const uint8_t* buf, uint32_t off, ui
   for (int k = 0; k < 5; ++k) a[k] = w[k];
 #pragma unroll
   for (int k = 0; k < 4; ++k) out[k] = __funnelshift_r(a[k], a[k + 1], sh);
+}
+
+// Read 16 bytes at byte offset `off` of a 16-byte aligned shared buffer with
+// two aligned 16-byte loads (lanes reading consecutive 16-byte units hit
+// distinct banks) and a funnel shift.  The buffer must extend 32 bytes past
+// off & ~15.
+__device__ __forceinline__ void smem_read16_window(const uint8_t* buf, uint32_t off, uint32_t (&out)[4]) {
+  const uint4* q = reinterpret_cast<const uint4*>(buf) + (off >> 4);
+  const uint4 a = q[0];
+  const uint4 b = q[1];
+  const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  const bool s2 = (off & 8) != 0;
+  const bool s1 = (off & 4) != 0;
+  uint32_t w[6];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) w[k] = s2 ? v[k + 2] : v[k];
+  uint32_t u[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) u[k] = s1 ? w[k + 1] : w[k];
+  const uint32_t sh = (off & 3) * 8;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) out[k] = __funnelshift_r(u[k], u[k + 1], sh);
+}
+
+// Read 8 bytes at byte offset `off` of an 8-byte aligned shared buffer with
+// two aligned 8-byte loads and a funnel shift (buffer extends 16 bytes past
+// off & ~7).
+__device__ __forceinline__ void smem_read8_window(const uint8_t* buf, uint32_t off, uint32_t (&out)[2]) {
+  const uint2* q = reinterpret_cast<const uint2*>(buf) + (off >> 3);
+  const uint2 a = q[0];
+  const uint2 b = q[1];
+  const uint32_t v[4] = {a.x, a.y, b.x, b.y};
+  const bool s1 = (off & 4) != 0;
+  uint32_t w[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) w[k] = s1 ? v[k + 1] : v[k];
+  const uint32_t sh = (off & 3) * 8;
+  out[0] = __funnelshift_r(w[0], w[1], sh);
+  out[1] = __funnelshift_r(w[1], w[2], sh);
 }
 
 template <int N>
@@ -230,70 +386,60 @@ __device__ __forceinline__ void smem_read_words(const uint8_t* buf, uint32_t off
 
 // ---------------------------------------------------------------- staging
 
-// Stage words [t0, t0+len) of a layout into shared memory (sin[j] = word
-// t0+j).  With `bulk` set (base 16-byte aligned and every run a multiple of 8
-// words at an 8-word aligned offset) thread 0 issues one TMA bulk copy per
-// contiguous run and registers the bytes on `bar`; a ragged flat tail is
-// copied by all threads.  Without it all threads gather word by word.
-// Thread 0 always arrives on `bar` once.  Caller waits on `bar`, then
-// __syncthreads().
-__device__ __forceinline__ void stage_words(const uint16_t* __restrict__ base, const Layout& L,
-                                            bool bulk, uint64_t t0, uint32_t len,
-                                            uint16_t* sin, uint64_t* bar) {
-  const int tid = threadIdx.x;
-  if (bulk) {
-    uint32_t aligned_len = len;
-    if (L.block_words == 0) aligned_len = len & ~7u;
-    if (tid == 0) {
-      uint64_t i = t0;
-      const uint64_t end = t0 + aligned_len;
-      while (i < end) {
-        uint64_t run = layout_run(L, i);
-        if (run > end - i) run = end - i;
-        const uint32_t bytes = static_cast<uint32_t>(run * 2);
-        mbar_expect_tx(bar, bytes);
-        bulk_g2s(sin + (i - t0), base + layout_addr(L, i), bytes, bar);
-        i += run;
-      }
-      mbar_arrive(bar);
-    }
-    for (uint32_t j = aligned_len + tid; j < len; j += kThreads) sin[j] = base[t0 + j];
-  } else {
-    if (tid == 0) mbar_arrive(bar);
-    for (uint32_t j = tid; j < len; j += kThreads) sin[j] = base[layout_addr(L, t0 + j)];
+// Stage words [t0, t0+len) of a bulk-capable layout (base 16-byte aligned,
+// every run a multiple of 8 words at an 8-word aligned offset) into shared
+// memory, sin[j] = word t0+j, by the calling thread alone: one TMA bulk copy
+// per contiguous run with its bytes registered on `bar`; a ragged flat tail
+// of < 8 words by plain loads.  Does not arrive on `bar`.
+__device__ __forceinline__ void stage_words_tma(const uint16_t* __restrict__ base, const Layout& L, uint64_t t0,
+                                                uint32_t len, uint16_t* sin, uint64_t* bar) {
+  const uint32_t aligned_len = L.block_words == 0 ? (len & ~7u) : len;
+  uint64_t i = t0;
+  const uint64_t end = t0 + aligned_len;
+  while (i < end) {
+    uint64_t run = layout_run(L, i);
+    if (run > end - i) run = end - i;
+    const uint32_t bytes = static_cast<uint32_t>(run * 2);
+    mbar_expect_tx(bar, bytes);
+    bulk_g2s(sin + (i - t0), base + layout_addr(L, i), bytes, bar);
+    i += run;
   }
+  for (uint32_t j = aligned_len; j < len; ++j) sin[j] = base[t0 + j];
+}
+
+// Stage words of any layout word by word with the 32 lanes of one warp.
+__device__ __forceinline__ void gather_words_warp(const uint16_t* __restrict__ base, const Layout& L, uint64_t t0,
+                                                  uint32_t len, uint16_t* sin) {
+  for (uint32_t j = threadIdx.x & 31; j < len; j += 32) sin[j] = base[layout_addr(L, t0 + j)];
 }
 
 // Stage bytes [off, off+nbytes) of the global buffer [g, g+glen) into shared
-// memory so that byte off+i lands at smem[pad+i], pad = (g+off) % 16.  The
-// 16-byte aligned interior goes by TMA bulk copy (thread 0, bytes registered
-// on `bar`, no arrive); the ragged head/tail bytes by plain loads of all
-// threads.  Never reads outside [g, g+glen).  Returns pad.
-__device__ __forceinline__ uint32_t stage_bytes(const uint8_t* __restrict__ g, uint64_t off,
-                                                uint32_t nbytes, uint8_t* smem, uint64_t* bar) {
-  const int tid = threadIdx.x;
-  const uintptr_t A = reinterpret_cast<uintptr_t>(g) + off;
+// memory so that byte off+i lands at smem[pad+i], pad = (g+off) % 16, by the
+// calling thread alone: one TMA bulk copy (bytes registered on `bar`, no
+// arrive) covers the range rounded out to 16-byte boundaries as far as the
+// buffer allows; only bytes that rounding cannot reach (at the very start or
+// end of the buffer) are loaded by plain loads.  Never reads outside
+// [g, g+glen).  smem must hold pad + nbytes + 16 bytes.  Returns pad.
+__device__ __forceinline__ uint32_t stage_bytes_one(const uint8_t* __restrict__ g, uint64_t glen, uint64_t off,
+                                                    uint32_t nbytes, uint8_t* smem, uint64_t* bar) {
+  const uintptr_t base = reinterpret_cast<uintptr_t>(g);
+  const uintptr_t A = base + off;
   const uintptr_t E = A + nbytes;
   const uintptr_t F = A & ~static_cast<uintptr_t>(15);
-  const uint32_t pad = static_cast<uint32_t>(A - F);
-  const uintptr_t gal = (reinterpret_cast<uintptr_t>(g) + 15) & ~static_cast<uintptr_t>(15);
+  const uintptr_t gal = (base + 15) & ~static_cast<uintptr_t>(15);
+  const uintptr_t gend = (base + glen) & ~static_cast<uintptr_t>(15);
+  const uintptr_t Ealign = (E + 15) & ~static_cast<uintptr_t>(15);
   const uintptr_t lo = F > gal ? F : gal;
-  const uintptr_t hi = E & ~static_cast<uintptr_t>(15);
+  const uintptr_t hi = Ealign < gend ? Ealign : gend;
   if (hi > lo) {
-    if (tid == 0) {
-      mbar_expect_tx(bar, static_cast<uint32_t>(hi - lo));
-      bulk_g2s(smem + (lo - F), reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo),
-               bar);
-    }
-    for (uintptr_t a = A + tid; a < lo; a += kThreads)
-      smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
-    for (uintptr_t a = hi + tid; a < E; a += kThreads)
-      smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
+    mbar_expect_tx(bar, static_cast<uint32_t>(hi - lo));
+    bulk_g2s(smem + (lo - F), reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo), bar);
+    for (uintptr_t a = A; a < lo; ++a) smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
+    for (uintptr_t a = hi > A ? hi : A; a < E; ++a) smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
   } else {
-    for (uintptr_t a = A + tid; a < E; a += kThreads)
-      smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
+    for (uintptr_t a = A; a < E; ++a) smem[a - F] = *reinterpret_cast<const uint8_t*>(a);
   }
-  return pad;
+  return static_cast<uint32_t>(A - F);
 }
 
 __device__ __forceinline__ uint32_t load_u32le(const uint8_t* __restrict__ p) {

@@ -1,16 +1,19 @@
-// Batched splitzip kernels (sm_100a).
+// Batched, persistent splitzip kernels (sm_100a).
 //
-// Every kernel takes a batch of jobs as a __grid_constant__ parameter: one job
-// is one reference ABI call (one layer of one request).  The grid covers the
-// 8192-word tiles of all jobs; a CTA finds its job by binary search of the
-// tile offsets.  A single ABI call is a batch of one.
+// Every kernel takes a batch of jobs as a __grid_constant__ parameter (one
+// job = one reference ABI call: one layer of one request).  The work is the
+// 8192-word tiles of all jobs.  Kernels are persistent: the grid is sized to
+// the resident CTAs, each CTA walks a contiguous chunk of tiles, and a
+// 3-stage ring of shared-memory buffers filled by TMA bulk copies keeps the
+// next two tiles in flight while the current one is coded.  Only the top16
+// encoder, whose escape offsets chain tile to tile, takes tiles by atomic
+// ticket instead (so every tile it waits for is held by a running CTA).
 //
-// Tile work (one CTA of 256 threads, 8 warps x 2 steps x 32 lanes x 16 words):
-//   encode: words staged by TMA bulk copies (one per contiguous run of the
-//     block table) -> per lane 16 words in registers -> body/low plane by
-//     byte_perm SIMD, codes by a shared-memory table -> warp funnel stores
-//     into the unaligned stream regions;
-//   decode: stream bytes staged by TMA -> per lane 16 output words -> two
+// Per tile: one CTA of 256 threads = 8 warps x 2 steps x 32 lanes x 16 words.
+//   encode: 16 words per lane in registers -> body/low plane by byte_perm,
+//     codes by one shared-memory lookup per word -> warp funnel stores into
+//     the unaligned stream regions (aligned 8/4/2-byte stores);
+//   decode: stream bytes staged by TMA -> 16 output words per lane -> two
 //     16-byte stores into the paged cache block.
 #pragma once
 
@@ -24,6 +27,12 @@ namespace ukv {
 constexpr int kMaxBatch = 96;
 constexpr uint64_t kStatusFlag = 1ull << 63;
 constexpr int kDecodeSlots = 1024;
+constexpr int kStages = 3;
+constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 16 KiB of words
+constexpr uint32_t kDecStageBytes = 2 * kTileWords + 128;
+constexpr uint32_t kDecCodesOffset = kTileWords + 128;  // top16/fixed6 codes inside a stage
+constexpr uint32_t kEncSmemBytes = kStages * kEncStageBytes;
+constexpr uint32_t kDecSmemBytes = kStages * kDecStageBytes;
 
 struct DecodeSlot {
   unsigned int done;
@@ -68,7 +77,7 @@ struct DecJob {
   const uint8_t* tables;
   uint32_t tiles;
   uint32_t slot;
-  int vec;
+  int vec;  // 16-byte stores of whole units into the destination layout
   int pad;
 };
 
@@ -95,6 +104,25 @@ __device__ __forceinline__ int find_job(const uint32_t* start, uint32_t jobs, ui
     if (start[mid] <= t) lo = mid; else hi = mid - 1;
   }
   return lo;
+}
+
+// Tiles are visited in increasing order, so the job index only moves forward.
+template <int kMax>
+__device__ __forceinline__ int advance_job(const uint32_t* start, int j, uint32_t t) {
+  if (kMax == 1) return 0;
+  while (t >= start[j + 1]) ++j;
+  return j;
+}
+
+struct Chunk {
+  uint32_t first;
+  uint32_t last;
+};
+
+__device__ __forceinline__ Chunk cta_chunk(uint32_t total) {
+  const uint32_t per = (total + gridDim.x - 1) / gridDim.x;
+  const uint32_t first = min(blockIdx.x * per, total);
+  return {first, min(first + per, total)};
 }
 
 // Scratch layouts (byte offsets from EncJob::scratch).
@@ -127,24 +155,11 @@ __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
   return v;
 }
 
-// ------------------------------------------------------------ tile staging
-
 __device__ __forceinline__ uint32_t tile_len(uint64_t n, uint64_t t0) {
   return static_cast<uint32_t>(n - t0 < kTileWords ? n - t0 : kTileWords);
 }
 
-// Stage the tile's words, wait (bounded) and make them visible to the CTA.
-__device__ __forceinline__ void load_tile_words(const EncJob& J, uint64_t t0, uint32_t len,
-                                                uint16_t* sin, uint64_t* bar, uint32_t* error) {
-  stage_words(J.src, J.L, J.bulk != 0, t0, len, sin, bar);
-  const bool ok = mbar_wait(bar, 0);
-  if (__syncthreads_or(!ok)) {
-    if (threadIdx.x == 0) raise_error(error);
-    mbar_wait(bar, 0);
-    __syncthreads();
-  }
-}
-
+// 16 words (8 registers) of a lane's unit from a staged tile.
 __device__ __forceinline__ void load_unit(const uint16_t* sin, uint32_t w0, uint32_t (&x)[8]) {
   const uint4 v0 = *reinterpret_cast<const uint4*>(sin + w0);
   const uint4 v1 = *reinterpret_cast<const uint4*>(sin + w0 + 8);
@@ -152,40 +167,211 @@ __device__ __forceinline__ void load_unit(const uint16_t* sin, uint32_t w0, uint
   x[4] = v1.x; x[5] = v1.y; x[6] = v1.z; x[7] = v1.w;
 }
 
-// ------------------------------------------------------------ top16 encode
-
-// Codes + escape mask of 16 words.  tbl entries: nibble*0x11, or 0x100 for
-// "escape" (code 255 of the reference table; the stored nibble is then 0).
-template <bool kPerWordPlane>
-__device__ __forceinline__ void top16_codes(const uint32_t (&x)[8], const uint32_t* tbl,
-                                            uint32_t plane_mask, uint32_t& c0, uint32_t& c1,
-                                            uint32_t& esc) {
-  uint32_t bytes[8];
-  esc = 0;
-#pragma unroll
-  for (int p = 0; p < 8; ++p) {
-    const uint32_t e0 = (x[p] >> 7) & 0xFFu;
-    const uint32_t e1 = (x[p] >> 23) & 0xFFu;
-    uint32_t t0, t1;
-    if (kPerWordPlane) {
-      t0 = tbl[(((plane_mask >> (2 * p)) & 1u) << 8) + e0];
-      t1 = tbl[(((plane_mask >> (2 * p + 1)) & 1u) << 8) + e1];
-    } else {
-      t0 = tbl[e0];
-      t1 = tbl[e1];
-    }
-    bytes[p] = (t0 & 0x0Fu) | (t1 & 0xF0u);
-    esc |= ((t0 >> 8) & 1u) << (2 * p);
-    esc |= ((t1 >> 8) & 1u) << (2 * p + 1);
-  }
-  c0 = bytes[0] | (bytes[1] << 8) | (bytes[2] << 16) | (bytes[3] << 24);
-  c1 = bytes[4] | (bytes[5] << 8) | (bytes[6] << 16) | (bytes[7] << 24);
+__device__ __forceinline__ uint32_t step_valid_words(uint32_t len, uint32_t sb) {
+  return len > sb ? min(len - sb, static_cast<uint32_t>(kStepWords)) : 0u;
 }
 
+// ------------------------------------------------------- ring pipeline
+//
+// Warp-specialized: warp kProducerWarp stages tiles into a kStages ring of
+// shared-memory buffers (TMA bulk copies issued by its lane 0, plus the
+// per-tile descriptor the consumers need); warps 0..kWarps-1 code the
+// tiles.  full[s] completes when the 32 producer lanes have arrived and the
+// stage's TMA bytes have landed; empty[s] when every consumer warp has
+// released the stage.  The producer ends the sequence with a descriptor
+// whose tile is kEndTile.  Consumers synchronise among themselves with
+// named barrier 1 (consumer_sync), never with __syncthreads.
+
+constexpr int kCtaThreads = kThreads + 32;
+constexpr int kProducerWarp = kWarps;
+constexpr uint32_t kEndTile = 0xFFFFFFFFu;
+
+struct Ring {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+};
+
+__device__ __forceinline__ void ring_init(Ring& R) {
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&R.full[s], 32);
+      mbar_init(&R.empty[s], kWarps);
+    }
+    fence_mbar_init();
+  }
+}
+
+// Position in the ring: uses so far, stage, parity of the stage's current use.
+struct RingPos {
+  uint32_t k = 0;
+  int s = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next() {
+    ++k;
+    if (++s == kStages) {
+      s = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Bounded wait for a ring barrier phase.  A timeout raises the error flag and
+// waits once more so that no copy is left in flight.
+__device__ __forceinline__ void wait_stage(uint64_t* bar, uint32_t parity, uint32_t* error) {
+  if (!mbar_wait(bar, parity)) {
+    raise_error(error);
+    mbar_wait(bar, parity);
+  }
+}
+
+// Producer: wait until every consumer warp released the stage's previous use.
+__device__ __forceinline__ void producer_acquire(Ring& R, const RingPos& p, uint32_t* error) {
+  if (p.k >= kStages) wait_stage(&R.empty[p.s], p.phase ^ 1u, error);
+}
+
+// Producer, every lane: publish the stage (after its descriptor writes).
+__device__ __forceinline__ void producer_commit(Ring& R, const RingPos& p) { mbar_arrive(&R.full[p.s]); }
+
+__device__ __forceinline__ void consumer_wait(Ring& R, const RingPos& p, uint32_t* error) {
+  wait_stage(&R.full[p.s], p.phase, error);
+}
+
+// Consumer warp: done with the stage (all lanes' reads precede lane 0's arrive).
+__device__ __forceinline__ void consumer_release(Ring& R, const RingPos& p) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&R.empty[p.s]);
+}
+
+// Barrier among the kThreads consumer threads (the producer warp never joins).
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+}
+
+// Encode stage descriptor: global tile index (or kEndTile) and its job.
+struct EncDesc {
+  uint32_t tile;
+  uint32_t job;
+};
+
+// Producer warp of the encode kernels: stages the tiles next_tile() yields
+// (increasing; >= total ends) into the ring.  A bulk-capable layout takes one
+// TMA copy per contiguous run from lane 0; any other is gathered word by word
+// by the 32 lanes.
+template <int kMax, typename Next>
+__device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t* ring, Ring& R, EncDesc* D,
+                                                Next&& next_tile) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t total = b.tile_start[b.jobs];
+  RingPos p;
+  int ji = 0;
+  for (;;) {
+    producer_acquire(R, p, nullptr);
+    const uint32_t t = next_tile();
+    if (t >= total) {
+      if (lane == 0) D[p.s].tile = kEndTile;
+      producer_commit(R, p);
+      return;
+    }
+    ji = advance_job<kMax>(b.tile_start, ji, t);
+    const EncJob& J = b.job[ji];
+    const uint64_t t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
+    const uint32_t len = tile_len(J.n, t0);
+    uint16_t* sin = reinterpret_cast<uint16_t*>(ring + p.s * kEncStageBytes);
+    if (lane == 0) {
+      D[p.s].tile = t;
+      D[p.s].job = static_cast<uint32_t>(ji);
+    }
+    if (J.bulk != 0) {
+      if (lane == 0) stage_words_tma(J.src, J.L, t0, len, sin, &R.full[p.s]);
+    } else {
+      gather_words_warp(J.src, J.L, t0, len, sin);
+    }
+    producer_commit(R, p);
+    p.next();
+  }
+}
+
+// Tiles of this CTA's contiguous chunk, for encode_producer (warp-uniform).
+struct ChunkTiles {
+  uint32_t next, last;
+  __device__ __forceinline__ uint32_t operator()() { return next < last ? next++ : kEndTile; }
+};
+
+// Consumer warps of the encode kernels: fn(job, job_index, tile, words,
+// ring position) for every staged tile until the end descriptor.
+template <int kMax, typename Fn>
+__device__ __forceinline__ void encode_consumer(const EncBatch<kMax>& b, uint8_t* ring, Ring& R,
+                                                const EncDesc* D, Fn&& fn) {
+  RingPos p;
+  for (;;) {
+    consumer_wait(R, p, nullptr);
+    const EncDesc d = D[p.s];
+    if (d.tile == kEndTile) return;
+    const EncJob& J = b.job[d.job];
+    fn(J, static_cast<int>(d.job), d.tile - b.tile_start[d.job],
+       reinterpret_cast<const uint16_t*>(ring + p.s * kEncStageBytes), p);
+    consumer_release(R, p);
+    p.next();
+  }
+}
+
+// Chunk-scheduled encode kernel body: producer warp + consumer warps.
+template <int kMax, typename Fn>
+__device__ __forceinline__ void encode_pipeline(const EncBatch<kMax>& b, uint8_t* ring, Ring& R, EncDesc* D,
+                                                Fn&& fn) {
+  if ((threadIdx.x >> 5) == kProducerWarp) {
+    const Chunk c = cta_chunk(b.tile_start[b.jobs]);
+    encode_producer<kMax>(b, ring, R, D, ChunkTiles{c.first, c.last});
+    return;
+  }
+  encode_consumer<kMax>(b, ring, R, D, fn);
+}
+
+// ------------------------------------------------------------ top16 encode
+
+// Table entry per (plane, exponent): code nibble copied into both nibbles,
+// bits 16 and 17 set for "escape" (code 255 of the reference table; the
+// stored nibble is then 0).
 __device__ __forceinline__ void load_top16_table(const uint8_t* tables, uint32_t* stbl) {
   for (int i = threadIdx.x; i < 512; i += kThreads) {
     const uint32_t c = __ldg(tables + i);
-    stbl[i] = c == 255u ? 0x100u : (c & 0xFu) * 0x11u;
+    stbl[i] = c == 255u ? 0x30000u : (c & 0xFu) * 0x11u;
+  }
+}
+
+// Merge the entries of an even and an odd word: bits 0-7 code byte, bit 16
+// even escape, bit 17 odd escape (one LOP3).
+__device__ __forceinline__ uint32_t merge_pair(uint32_t t0, uint32_t t1) {
+  return (t0 & 0x1000Fu) | (t1 & ~0x1000Fu);
+}
+
+// Codes (c0, c1: 8 code bytes) and escape mask (16 bits) of 16 words.
+__device__ __forceinline__ void top16_unit_codes(const uint32_t (&x)[8], const uint32_t* tbl,
+                                                 uint64_t g, uint64_t half, uint32_t& c0,
+                                                 uint32_t& c1, uint32_t& esc) {
+  uint32_t u[8];
+  if (g >= half || g + kUnitWords <= half) {
+    const uint8_t* t = reinterpret_cast<const uint8_t*>(tbl + (g >= half ? 256 : 0));
+#pragma unroll
+    for (int p = 0; p < 8; ++p)
+      u[p] = merge_pair(*reinterpret_cast<const uint32_t*>(t + ((x[p] >> 5) & 0x3FCu)),
+                        *reinterpret_cast<const uint32_t*>(t + ((x[p] >> 21) & 0x3FCu)));
+  } else {
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      const uint32_t* t0 = tbl + ((g + 2 * p) >= half ? 256 : 0);
+      const uint32_t* t1 = tbl + ((g + 2 * p + 1) >= half ? 256 : 0);
+      u[p] = merge_pair(t0[(x[p] >> 7) & 0xFFu], t1[(x[p] >> 23) & 0xFFu]);
+    }
+  }
+  c0 = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
+  c1 = __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410);
+  const uint32_t any = (u[0] | u[1] | u[2] | u[3] | u[4] | u[5] | u[6] | u[7]) & 0x30000u;
+  esc = 0;
+  if (any) {
+#pragma unroll
+    for (int p = 0; p < 8; ++p) esc |= ((u[p] >> 16) & 3u) << (2 * p);
   }
 }
 
@@ -199,54 +385,55 @@ __device__ __forceinline__ void top16_tile_body(const EncJob& J, uint64_t t0, ui
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t sb = (warp * kStepsPerWarp + s) * kStepWords;
     const uint32_t w0 = sb + lane * kUnitWords;
-    const uint32_t step_valid = len > sb ? min(len - sb, static_cast<uint32_t>(kStepWords)) : 0u;
-    const uint32_t valid = len > w0 ? min(len - w0, static_cast<uint32_t>(kUnitWords)) : 0u;
+    const uint32_t step_valid = step_valid_words(len, sb);
+    masks[s] = 0;
+    if (step_valid == 0) continue;  // uniform per warp
     uint32_t x[8];
     load_unit(sin, w0, x);
-    uint32_t b[4];
+    uint32_t bb[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t lo = __byte_perm(x[2 * q], x[2 * q + 1], 0x6420);
       const uint32_t hi = __byte_perm(x[2 * q], x[2 * q + 1], 0x7531);
-      b[q] = (lo & 0x7F7F7F7Fu) | (hi & 0x80808080u);
+      bb[q] = (lo & 0x7F7F7F7Fu) | (hi & 0x80808080u);
     }
-    const uint64_t g = t0 + w0;
     uint32_t c0, c1, esc;
-    if (g >= J.half) {
-      top16_codes<false>(x, stbl + 256, 0, c0, c1, esc);
-    } else if (g + kUnitWords <= J.half) {
-      top16_codes<false>(x, stbl, 0, c0, c1, esc);
+    top16_unit_codes(x, stbl, t0 + w0, J.half, c0, c1, esc);
+    uint8_t* bdst = J.dst + 5 + t0 + sb;
+    uint8_t* cdst = J.dst + 5 + J.n + (t0 + sb) / 2;
+    if (step_valid == kStepWords) {
+      const uint32_t cw[2] = {c0, c1};
+      warp_store_words<4, 8>(bdst, bb, lane);
+      warp_store_words<2, 8>(cdst, cw, lane);
     } else {
-      const uint32_t pm = (0xFFFFu << static_cast<uint32_t>(J.half - g)) & 0xFFFFu;
-      top16_codes<true>(x, stbl, pm, c0, c1, esc);
+      const uint64_t body[2] = {bb[0] | (static_cast<uint64_t>(bb[1]) << 32),
+                                bb[2] | (static_cast<uint64_t>(bb[3]) << 32)};
+      const uint32_t valid = w0 < len ? min(len - w0, static_cast<uint32_t>(kUnitWords)) : 0u;
+      if (valid < kUnitWords) {
+        esc &= (1u << valid) - 1u;
+        const uint64_t keep = valid == 0 ? 0ull : (~0ull >> (64 - 4 * valid));
+        const uint64_t cc = (static_cast<uint64_t>(c1) << 32 | c0) & keep;
+        c0 = static_cast<uint32_t>(cc);
+        c1 = static_cast<uint32_t>(cc >> 32);
+      }
+      const uint64_t codes[1] = {c0 | (static_cast<uint64_t>(c1) << 32)};
+      warp_store<uint64_t, 2>(bdst, step_valid, body, lane);
+      warp_store<uint64_t, 1>(cdst, (step_valid + 1) / 2, codes, lane);
     }
-    if (valid < kUnitWords) {
-      esc &= (1u << valid) - 1u;
-      const uint64_t keep = valid == 0 ? 0ull : (~0ull >> (64 - 4 * valid));
-      const uint64_t cc = (static_cast<uint64_t>(c1) << 32 | c0) & keep;
-      c0 = static_cast<uint32_t>(cc);
-      c1 = static_cast<uint32_t>(cc >> 32);
-    }
-    const uint64_t body[2] = {b[0] | (static_cast<uint64_t>(b[1]) << 32),
-                              b[2] | (static_cast<uint64_t>(b[3]) << 32)};
-    warp_store<uint64_t, 2>(J.dst + 5 + t0 + sb, step_valid, body, lane);
-    const uint64_t codes[1] = {c0 | (static_cast<uint64_t>(c1) << 32)};
-    warp_store<uint64_t, 1>(J.dst + 5 + J.n + (t0 + sb) / 2, (step_valid + 1) / 2, codes, lane);
     masks[s] = esc;
   }
 }
 
-// CTA-wide exclusive offsets of this lane's escapes (position order is warp,
+// CTA-wide exclusive offsets of this lane's escapes (position order: warp,
 // then step, then lane).  Returns the tile total; off[s] = offset of the
-// lane's first escape of step s.  Uses s_wtot[2][kWarps] and syncs.
+// lane's first escape of step s.  Uses s_wtot[2][kWarps] (alternate two of
+// them tile by tile) and one consumer barrier.
 __device__ __forceinline__ uint32_t escape_offsets(const uint32_t (&masks)[kStepsPerWarp],
                                                    uint32_t (*s_wtot)[kWarps],
                                                    uint32_t (&off)[kStepsPerWarp]) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const uint32_t n0 = __popc(masks[0]);
-  const uint32_t n1 = __popc(masks[1]);
-  const uint32_t mine = n0 | (n1 << 16);
+  const uint32_t mine = __popc(masks[0]) | (__popc(masks[1]) << 16);
   uint32_t incl = mine;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -258,7 +445,7 @@ __device__ __forceinline__ uint32_t escape_offsets(const uint32_t (&masks)[kStep
     s_wtot[0][warp] = incl & 0xFFFFu;
     s_wtot[1][warp] = incl >> 16;
   }
-  __syncthreads();
+  consumer_sync();
   uint32_t before = 0, total = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) {
@@ -336,7 +523,7 @@ __device__ __forceinline__ uint64_t wait_group(const uint64_t* p, uint32_t* erro
 // Tile `tile` publishes its count to its status word and to its group of 32
 // tiles, then sums (a) complete groups before its group and (b) the tiles of
 // its own group before it.  Tiles are numbered by ticket, so every tile it
-// waits on is held by a running CTA; the wait does not depend on later tiles.
+// waits on is held by a running CTA; the wait never depends on later tiles.
 __device__ uint64_t tile_prefix(uint8_t* scratch, uint32_t tiles, uint32_t tile, uint32_t count,
                                 uint32_t* error) {
   const int lane = threadIdx.x & 31;
@@ -359,147 +546,171 @@ __device__ uint64_t tile_prefix(uint8_t* scratch, uint32_t tiles, uint32_t tile,
   return prefix;
 }
 
+// top16 encode: tiles by ticket (ascending within each CTA; the producer
+// takes a ticket once it holds a free stage), escape offsets by the
+// two-level scan.
 template <int kMax>
-__global__ void __launch_bounds__(kThreads) EncodeTop16Kernel(const __grid_constant__ EncBatch<kMax> b) {
-  __shared__ __align__(128) uint16_t sin[kTileWords];
+__global__ void __launch_bounds__(kCtaThreads, 3) EncodeTop16Kernel(const __grid_constant__ EncBatch<kMax> b) {
+  extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint32_t stbl[512];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t s_ticket;
-  __shared__ uint32_t s_wtot[2][kWarps];
-  __shared__ uint64_t s_prefix;
+  __shared__ Ring R;
+  __shared__ EncDesc D[kStages];
+  __shared__ uint32_t s_wtot[2][2][kWarps];
+  __shared__ uint64_t s_prefix[2];
   const int tid = threadIdx.x;
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-    s_ticket = atomicAdd(reinterpret_cast<uint32_t*>(b.job[0].scratch), 1u);
-  }
+  ring_init(R);
   __syncthreads();
-  const uint32_t t = s_ticket;
-  const int j = find_job<kMax>(b.tile_start, b.jobs, t);
-  const EncJob& J = b.job[j];
-  const uint32_t tile = t - b.tile_start[j];
-  uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 4);
-  const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-  const uint32_t len = tile_len(J.n, t0);
-  load_top16_table(J.tables, stbl);
-  load_tile_words(J, t0, len, sin, &bar, error);
-
-  uint32_t masks[kStepsPerWarp];
-  top16_tile_body(J, t0, len, sin, stbl, masks);
-  uint32_t off[kStepsPerWarp];
-  const uint32_t total = escape_offsets(masks, s_wtot, off);
-  if ((tid >> 5) == 0) {
-    const uint64_t prefix = tile_prefix(J.scratch, J.tiles, tile, total, error);
-    if (tid == 0) s_prefix = prefix;
+  if ((tid >> 5) == kProducerWarp) {
+    uint32_t* ticket = reinterpret_cast<uint32_t*>(b.job[0].scratch);
+    encode_producer<kMax>(b, ring, R, D, [&]() {
+      uint32_t t = 0;
+      if ((tid & 31) == 0) t = atomicAdd(ticket, 1u);
+      return __shfl_sync(kFull, t, 0);
+    });
+    return;
   }
-  __syncthreads();
-  const uint64_t prefix = s_prefix;
-  write_escapes(J, t0, sin, masks, off, prefix);
-  if (tile == J.tiles - 1 && tid == 0) {
-    write_top16_header(J.dst, prefix + total, J.cap, ld_volatile_u32(error) != 0);
-  }
+  int table_job = -1;
+  encode_consumer<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
+                                           const RingPos& p) {
+    uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 4);
+    if (j != table_job) {  // uniform across the consumers
+      consumer_sync();     // every warp is done with the previous table
+      load_top16_table(J.tables, stbl);
+      table_job = j;
+      consumer_sync();
+    }
+    const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
+    const uint32_t len = tile_len(J.n, t0);
+    uint32_t masks[kStepsPerWarp];
+    top16_tile_body(J, t0, len, sin, stbl, masks);
+    uint32_t off[kStepsPerWarp];
+    const uint32_t count = escape_offsets(masks, s_wtot[p.k & 1], off);
+    if ((tid >> 5) == 0) {
+      const uint64_t prefix = tile_prefix(J.scratch, J.tiles, tile, count, error);
+      if (tid == 0) s_prefix[p.k & 1] = prefix;
+    }
+    consumer_sync();
+    const uint64_t prefix = s_prefix[p.k & 1];
+    write_escapes(J, t0, sin, masks, off, prefix);
+    if (tile == J.tiles - 1 && tid == 0) {
+      write_top16_header(J.dst, prefix + count, J.cap, ld_volatile_u32(error) != 0);
+    }
+  });
 }
 
 // ------------------------------------------------- presence / auto stats
 
-// Per tile: high-byte presence (-> job bitmap) and, for kStats, the top16
-// escape count (-> tile count, group sum, job total).
+// High-byte presence of every word (-> job bitmap) and, for kStats, the
+// top16 escape count of every tile (-> tile count, group sum, job total; each
+// warp adds its own share, so no CTA barrier is needed for the counts).
 template <int kMax, bool kStats>
-__global__ void __launch_bounds__(kThreads) PresenceKernel(const __grid_constant__ EncBatch<kMax> b) {
-  __shared__ __align__(128) uint16_t sin[kTileWords];
+__global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_constant__ EncBatch<kMax> b) {
+  extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint8_t spres[256];
-  __shared__ uint8_t sesc[512];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t s_wsum[kWarps];
+  __shared__ uint8_t sesc[512];  // 1 where the exponent has no top16 code
+  __shared__ Ring R;
+  __shared__ EncDesc D[kStages];
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int j = find_job<kMax>(b.tile_start, b.jobs, blockIdx.x);
-  const EncJob& J = b.job[j];
-  const uint32_t tile = blockIdx.x - b.tile_start[j];
-  uint32_t* bitmap = reinterpret_cast<uint32_t*>(J.scratch + (kStats ? 16 : 0));
-  uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + (kStats ? 4 : 32));
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
   if (tid < 64) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
-  if (kStats) {
-    for (int i = tid; i < 512; i += kThreads) sesc[i] = __ldg(J.tables + i) == 255u;
-  }
+  ring_init(R);
   __syncthreads();
-  const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-  const uint32_t len = tile_len(J.n, t0);
-  load_tile_words(J, t0, len, sin, &bar, error);
-  uint32_t escapes = 0;
+  int pres_job = -1, table_job = -1;
+  // OR the presence bits gathered for a job into its bitmap, then clear them
+  // (consumers only; every warp is past its last presence store)
+  auto flush = [&](const EncJob& P) {
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(P.scratch + (kStats ? 16 : 0));
+    const uint32_t bits = __ballot_sync(kFull, spres[tid] != 0);
+    if (lane == 0 && bits) atomicOr(&bitmap[warp], bits);
+    consumer_sync();
+    if (tid < 64) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
+  };
+  encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
+                                           const RingPos&) {
+    if (j != pres_job || (kStats && j != table_job)) {  // uniform across the consumers
+      consumer_sync();
+      if (j != pres_job) {
+        if (pres_job >= 0) flush(b.job[pres_job]);
+        pres_job = j;
+      }
+      if (kStats && j != table_job) {
+        for (int i = tid; i < 512; i += kThreads) sesc[i] = __ldg(J.tables + i) == 255u;
+        table_job = j;
+      }
+      consumer_sync();
+    }
+    const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
+    const uint32_t len = tile_len(J.n, t0);
+    uint32_t escapes = 0;
+    if (len == kTileWords && (t0 >= J.half || t0 + kTileWords <= J.half)) {
+      // whole tile in one plane: table offset fixed, no bounds
+      const uint32_t poff = t0 >= J.half ? 256u : 0u;
 #pragma unroll
-  for (int s = 0; s < kStepsPerWarp; ++s) {
-    const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-    if (w0 >= len) continue;
-    const uint32_t valid = min(len - w0, static_cast<uint32_t>(kUnitWords));
-    const uint64_t g = t0 + w0;
-    if (valid == kUnitWords) {
-      uint32_t x[8];
-      load_unit(sin, w0, x);
-      const uint8_t* et = sesc + (g >= J.half ? 256 : 0);
-      const bool uniform = g >= J.half || g + kUnitWords <= J.half;
+      for (int s = 0; s < kStepsPerWarp; ++s) {
+        const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
+        uint32_t x[8];
+        load_unit(sin, w0, x);
 #pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        spres[(x[p] >> 8) & 0xFFu] = 1;
-        spres[x[p] >> 24] = 1;
-        if (kStats) {
-          if (uniform) {
-            escapes += et[(x[p] >> 7) & 0xFFu] + et[(x[p] >> 23) & 0xFFu];
-          } else {
-            escapes += sesc[((g + 2 * p) >= J.half ? 256 : 0) + ((x[p] >> 7) & 0xFFu)];
-            escapes += sesc[((g + 2 * p + 1) >= J.half ? 256 : 0) + ((x[p] >> 23) & 0xFFu)];
-          }
+        for (int p = 0; p < 8; ++p) {
+          spres[__byte_perm(x[p], 0, 0x4441)] = 1;
+          spres[x[p] >> 24] = 1;
+          if (kStats) escapes += sesc[((x[p] >> 7) & 0xFFu) | poff] + sesc[((x[p] >> 23) & 0xFFu) | poff];
         }
       }
     } else {
-      for (uint32_t i = 0; i < valid; ++i) {
-        const uint32_t w = sin[w0 + i];
-        spres[w >> 8] = 1;
-        if (kStats) escapes += sesc[((g + i) >= J.half ? 256 : 0) + ((w >> 7) & 0xFFu)];
+#pragma unroll
+      for (int s = 0; s < kStepsPerWarp; ++s) {
+        const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
+        if (w0 >= len) continue;
+        const uint32_t valid = min(len - w0, static_cast<uint32_t>(kUnitWords));
+        const uint64_t g = t0 + w0;
+        for (uint32_t i = 0; i < valid; ++i) {
+          const uint32_t w = sin[w0 + i];
+          spres[w >> 8] = 1;
+          if (kStats) escapes += sesc[((g + i) >= J.half ? 256 : 0) + ((w >> 7) & 0xFFu)];
+        }
       }
     }
-  }
-  if (kStats) {
-    escapes = warp_sum(escapes);
-    if (lane == 0) s_wsum[warp] = escapes;
-  }
-  __syncthreads();
-  const uint32_t bits = __ballot_sync(kFull, spres[tid] != 0);
-  if (lane == 0 && bits) atomicOr(&bitmap[warp], bits);
-  if (kStats && tid == 0) {
-    uint32_t c = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) c += s_wsum[w];
-    uint64_t* groups = reinterpret_cast<uint64_t*>(J.scratch + 64);
-    uint32_t* counts = reinterpret_cast<uint32_t*>(groups + groups_for(J.tiles));
-    counts[tile] = c;
-    atomicAdd(reinterpret_cast<unsigned long long*>(&groups[tile >> 5]), (1ull << 32) | c);
-    atomicAdd(reinterpret_cast<uint32_t*>(J.scratch), c);
-  }
+    if (kStats) {
+      escapes = warp_sum(escapes);
+      if (lane == 0 && escapes) {
+        uint64_t* groups = reinterpret_cast<uint64_t*>(J.scratch + 64);
+        uint32_t* counts = reinterpret_cast<uint32_t*>(groups + groups_for(J.tiles));
+        atomicAdd(&counts[tile], escapes);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&groups[tile >> 5]), static_cast<unsigned long long>(escapes));
+        atomicAdd(reinterpret_cast<uint32_t*>(J.scratch), escapes);
+      }
+    }
+  });
+  if (warp == kProducerWarp) return;
+  consumer_sync();
+  if (pres_job >= 0) flush(b.job[pres_job]);
 }
 
 // ------------------------------------------------------------ fixed encode
 
-// Palette rank of high byte `tid` from a 256-bit presence bitmap.
-__device__ __forceinline__ void palette_ranks(const uint32_t* sbm, uint32_t* srank, uint32_t& distinct,
+// Palette rank of every high byte from a 256-bit presence bitmap (ascending
+// order) into srank[h]; thread tid handles high byte tid.
+__device__ __forceinline__ void palette_ranks(const uint32_t* bitmap, uint8_t* srank, uint32_t& distinct,
                                               bool& present, uint32_t& rank) {
   const int tid = threadIdx.x;
+  uint32_t bm[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) bm[w] = bitmap[w];
   distinct = 0;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) distinct += __popc(sbm[w]);
-  const uint32_t word = sbm[tid >> 5];
+  for (int w = 0; w < 8; ++w) distinct += __popc(bm[w]);
+  const uint32_t word = bm[tid >> 5];
   present = (word >> (tid & 31)) & 1u;
   rank = __popc(word & ((1u << (tid & 31)) - 1u));
-  for (int w = 0; w < (tid >> 5); ++w) rank += __popc(sbm[w]);
-  srank[tid] = rank;
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    if (w < (tid >> 5)) rank += __popc(bm[w]);
+  srank[tid] = static_cast<uint8_t>(rank);
 }
 
-// Header + palette of a fixed stream (written by the job's tile 0).
+// Header + palette of a fixed stream (written by one CTA).
 template <int kBits>
 __device__ __forceinline__ void write_fixed_header(uint8_t* dst, uint32_t distinct, bool present,
                                                    uint32_t rank, bool error) {
@@ -512,7 +723,7 @@ __device__ __forceinline__ void write_fixed_header(uint8_t* dst, uint32_t distin
 
 template <int kBits>
 __device__ __forceinline__ void fixed_tile_body(const EncJob& J, uint64_t t0, uint32_t len,
-                                                const uint16_t* sin, const uint32_t* srank) {
+                                                const uint16_t* sin, const uint8_t* srank) {
   constexpr uint32_t kHeader = kBits == 6 ? 65 : 33;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -520,32 +731,42 @@ __device__ __forceinline__ void fixed_tile_body(const EncJob& J, uint64_t t0, ui
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t sb = (warp * kStepsPerWarp + s) * kStepWords;
     const uint32_t w0 = sb + lane * kUnitWords;
-    const uint32_t step_valid = len > sb ? min(len - sb, static_cast<uint32_t>(kStepWords)) : 0u;
-    const uint32_t valid = len > w0 ? min(len - w0, static_cast<uint32_t>(kUnitWords)) : 0u;
+    const uint32_t step_valid = step_valid_words(len, sb);
+    if (step_valid == 0) continue;
     uint32_t x[8];
     load_unit(sin, w0, x);
     uint32_t low[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) low[q] = __byte_perm(x[2 * q], x[2 * q + 1], 0x6420);
-    const uint64_t lowd[2] = {low[0] | (static_cast<uint64_t>(low[1]) << 32),
-                              low[2] | (static_cast<uint64_t>(low[3]) << 32)};
-    warp_store<uint64_t, 2>(J.dst + kHeader + t0 + sb, step_valid, lowd, lane);
     uint32_t c[16];
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
-      c[2 * p] = srank[(x[p] >> 8) & 0xFFu];
+      c[2 * p] = srank[__byte_perm(x[p], 0, 0x4441)];
       c[2 * p + 1] = srank[x[p] >> 24];
     }
+    const bool full = step_valid == kStepWords;
+    if (!full) {
+      const uint32_t valid = w0 < len ? min(len - w0, static_cast<uint32_t>(kUnitWords)) : 0u;
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (i >= static_cast<int>(valid)) c[i] = 0;
+      for (int i = 0; i < 16; ++i)
+        if (i >= static_cast<int>(valid)) c[i] = 0;
+    }
+    uint8_t* ldst = J.dst + kHeader + t0 + sb;
+    if (full) {
+      warp_store_words<4, 8>(ldst, low, lane);
+    } else {
+      const uint64_t lowd[2] = {low[0] | (static_cast<uint64_t>(low[1]) << 32),
+                                low[2] | (static_cast<uint64_t>(low[3]) << 32)};
+      warp_store<uint64_t, 2>(ldst, step_valid, lowd, lane);
+    }
     if (kBits == 6) {
-      uint32_t q[3];
-      q[0] = c[0] | (c[1] << 6) | (c[2] << 12) | (c[3] << 18) | (c[4] << 24) | (c[5] << 30);
-      q[1] = (c[5] >> 2) | (c[6] << 4) | (c[7] << 10) | (c[8] << 16) | (c[9] << 22) | (c[10] << 28);
-      q[2] = (c[10] >> 4) | (c[11] << 2) | (c[12] << 8) | (c[13] << 14) | (c[14] << 20) | (c[15] << 26);
-      warp_store<uint32_t, 3>(J.dst + kHeader + J.n + 3 * (t0 + sb) / 4, 3 * ((step_valid + 3) / 4), q,
-                              lane);
+      uint32_t g[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) g[q] = c[4 * q] + c[4 * q + 1] * 64u + c[4 * q + 2] * 4096u + c[4 * q + 3] * 262144u;
+      const uint32_t qw[3] = {g[0] | (g[1] << 24), (g[1] >> 8) | (g[2] << 16), (g[2] >> 16) | (g[3] << 8)};
+      uint8_t* cdst = J.dst + kHeader + J.n + 3 * (t0 + sb) / 4;
+      if (full) warp_store_words<3, 4>(cdst, qw, lane);
+      else warp_store<uint32_t, 3>(cdst, 3 * ((step_valid + 3) / 4), qw, lane);
     } else {
       uint64_t lo = 0;
       uint32_t hi = 0;
@@ -561,44 +782,47 @@ __device__ __forceinline__ void fixed_tile_body(const EncJob& J, uint64_t t0, ui
           hi |= c[i] >> (64 - bit);
         }
       }
-      const uint16_t q[5] = {static_cast<uint16_t>(lo), static_cast<uint16_t>(lo >> 16),
-                             static_cast<uint16_t>(lo >> 32), static_cast<uint16_t>(lo >> 48),
-                             static_cast<uint16_t>(hi)};
-      warp_store<uint16_t, 5>(J.dst + kHeader + J.n + 5 * (t0 + sb) / 8, 5 * ((step_valid + 7) / 8), q,
-                              lane);
+      const uint16_t qh[5] = {static_cast<uint16_t>(lo), static_cast<uint16_t>(lo >> 16),
+                              static_cast<uint16_t>(lo >> 32), static_cast<uint16_t>(lo >> 48),
+                              static_cast<uint16_t>(hi)};
+      uint8_t* cdst = J.dst + kHeader + J.n + 5 * (t0 + sb) / 8;
+      if (full) warp_store_full<uint16_t, 5>(cdst, qh, lane);
+      else warp_store<uint16_t, 5>(cdst, 5 * ((step_valid + 7) / 8), qh, lane);
     }
   }
 }
 
 template <int kMax, int kBits>
-__global__ void __launch_bounds__(kThreads) EncodeFixedKernel(const __grid_constant__ EncBatch<kMax> b) {
+__global__ void __launch_bounds__(kCtaThreads, 3) EncodeFixedKernel(const __grid_constant__ EncBatch<kMax> b) {
   constexpr uint32_t kLimit = kBits == 6 ? 64 : 32;
-  __shared__ __align__(128) uint16_t sin[kTileWords];
-  __shared__ uint32_t srank[256];
-  __shared__ uint32_t sbm[8];
-  __shared__ __align__(8) uint64_t bar;
-  const int tid = threadIdx.x;
-  const int j = find_job<kMax>(b.tile_start, b.jobs, blockIdx.x);
-  const EncJob& J = b.job[j];
-  const uint32_t tile = blockIdx.x - b.tile_start[j];
-  const uint32_t* bitmap = reinterpret_cast<const uint32_t*>(J.scratch);
-  uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 32);
-  if (tid < 8) sbm[tid] = bitmap[tid];
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint8_t srank[256];
+  __shared__ Ring R;
+  __shared__ EncDesc D[kStages];
+  ring_init(R);
   __syncthreads();
-  uint32_t distinct, rank;
-  bool present;
-  palette_ranks(sbm, srank, distinct, present, rank);
-  if (tile == 0) write_fixed_header<kBits>(J.dst, distinct, present, rank, ld_volatile_u32(error) != 0);
-  if (distinct > kLimit) return;  // uniform across the job's CTAs
-  __syncthreads();
-  const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-  const uint32_t len = tile_len(J.n, t0);
-  load_tile_words(J, t0, len, sin, &bar, error);
-  fixed_tile_body<kBits>(J, t0, len, sin, srank);
+  int rank_job = -1;
+  bool skip = false;
+  encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
+                                           const RingPos&) {
+    if (j != rank_job) {  // uniform across the consumers
+      consumer_sync();    // every warp is done with the previous ranks
+      uint32_t distinct, rank;
+      bool present;
+      palette_ranks(reinterpret_cast<const uint32_t*>(J.scratch), srank, distinct, present, rank);
+      uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 32);
+      if (tile == 0) write_fixed_header<kBits>(J.dst, distinct, present, rank, ld_volatile_u32(error) != 0);
+      skip = distinct > kLimit;
+      rank_job = j;
+      consumer_sync();
+    }
+    if (skip) return;  // palette overflow: header only (uniform across the job)
+    const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
+    fixed_tile_body<kBits>(J, t0, tile_len(J.n, t0), sin, srank);
+  });
+  // a job whose tile 0 this CTA did not see still needs its header: the
+  // owner of tile 0 wrote it (tile 0 is always the first tile of some chunk
+  // or preceded by the same job's tiles in the same chunk).
 }
 
 // ------------------------------------------------------------- auto encode
@@ -612,12 +836,17 @@ __device__ __forceinline__ void raw_tile_body(const EncJob& J, uint64_t t0, uint
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t sb = (warp * kStepsPerWarp + s) * kStepWords;
     const uint32_t w0 = sb + lane * kUnitWords;
-    const uint32_t step_valid = len > sb ? min(len - sb, static_cast<uint32_t>(kStepWords)) : 0u;
+    const uint32_t step_valid = step_valid_words(len, sb);
+    if (step_valid == 0) continue;
     uint32_t x[8];
     load_unit(sin, w0, x);
-    const uint64_t d[4] = {x[0] | (static_cast<uint64_t>(x[1]) << 32), x[2] | (static_cast<uint64_t>(x[3]) << 32),
-                           x[4] | (static_cast<uint64_t>(x[5]) << 32), x[6] | (static_cast<uint64_t>(x[7]) << 32)};
-    warp_store<uint64_t, 4>(J.dst + 1 + 2 * (t0 + sb), 2 * step_valid, d, lane);
+    if (step_valid == kStepWords) {
+      warp_store_words<8, 8>(J.dst + 1 + 2 * (t0 + sb), x, lane);
+    } else {
+      const uint64_t d[4] = {x[0] | (static_cast<uint64_t>(x[1]) << 32), x[2] | (static_cast<uint64_t>(x[3]) << 32),
+                             x[4] | (static_cast<uint64_t>(x[5]) << 32), x[6] | (static_cast<uint64_t>(x[7]) << 32)};
+      warp_store<uint64_t, 4>(J.dst + 1 + 2 * (t0 + sb), 2 * step_valid, d, lane);
+    }
   }
 }
 
@@ -628,90 +857,123 @@ __device__ __forceinline__ void raw_tile_body(const EncJob& J, uint64_t t0, uint
 enum AutoKind { kAutoTop16 = 0, kAutoFixed6 = 1, kAutoRaw = 2, kAutoOverflow = 3 };
 
 template <int kMax>
-__global__ void __launch_bounds__(kThreads) EncodeAutoKernel(const __grid_constant__ EncBatch<kMax> b) {
-  __shared__ __align__(128) uint16_t sin[kTileWords];
-  __shared__ uint32_t stbl[512];  // top16 table or fixed ranks
-  __shared__ uint32_t sbm[8];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t s_wtot[2][kWarps];
-  __shared__ uint64_t s_prefix;
+__global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_constant__ EncBatch<kMax> b) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint32_t stbl[512];
+  __shared__ uint8_t srank[256];
+  __shared__ Ring R;
+  __shared__ EncDesc D[kStages];
+  __shared__ uint32_t s_wtot[2][2][kWarps];
+  __shared__ uint64_t s_prefix[2];
   const int tid = threadIdx.x;
-  const int j = find_job<kMax>(b.tile_start, b.jobs, blockIdx.x);
-  const EncJob& J = b.job[j];
-  const uint32_t tile = blockIdx.x - b.tile_start[j];
-  uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 4);
-  if (tid < 8) sbm[tid] = reinterpret_cast<const uint32_t*>(J.scratch + 16)[tid];
-  if (tid == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
+  ring_init(R);
   __syncthreads();
-  const uint64_t escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
-  uint32_t distinct, rank;
-  bool present;
-  palette_ranks(sbm, stbl + 256, distinct, present, rank);
-  const bool err = ld_volatile_u32(error) != 0;
-  const int kind = err ? kAutoOverflow
-                 : escapes <= J.cap ? kAutoTop16
-                 : distinct <= 64 ? kAutoFixed6
-                 : J.raw_ok ? kAutoRaw : kAutoOverflow;
-  const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-  const uint32_t len = tile_len(J.n, t0);
-  if (kind == kAutoOverflow) {
-    if (tile == 0) write_fixed_header<6>(J.dst, distinct > 64 ? distinct : 65, present, rank, true);
-    return;
-  }
-  if (kind == kAutoFixed6) {
-    if (tile == 0) write_fixed_header<6>(J.dst, distinct, present, rank, false);
-    __syncthreads();
-    load_tile_words(J, t0, len, sin, &bar, error);
-    fixed_tile_body<6>(J, t0, len, sin, stbl + 256);
-    return;
-  }
-  if (kind == kAutoRaw) {
-    if (tile == 0 && tid == 0) J.dst[0] = 6;
-    load_tile_words(J, t0, len, sin, &bar, error);
-    raw_tile_body(J, t0, len, sin);
-    return;
-  }
-  // top16 with known per-tile offsets: prefix = complete groups before this
-  // tile's group + this group's earlier tiles (no waiting: the stats pass ran).
-  load_top16_table(J.tables, stbl);
-  if ((tid >> 5) == 0) {
-    const int lane = tid & 31;
-    const uint64_t* groups = reinterpret_cast<const uint64_t*>(J.scratch + 64);
-    const uint32_t* counts = reinterpret_cast<const uint32_t*>(groups + groups_for(J.tiles));
-    const uint32_t g = tile >> 5;
-    uint64_t v = lane < static_cast<int>(tile & 31) ? counts[(g << 5) + lane] : 0;
-    uint64_t prefix = warp_sum(v);
-    for (uint32_t base = 0; base < g; base += 32) {
-      v = base + lane < g ? (groups[base + lane] & 0xFFFFFFFFull) : 0;
-      prefix += warp_sum(v);
+  int setup_job = -1;
+  int kind = kAutoOverflow;
+  uint64_t escapes = 0;
+  encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
+                                           const RingPos& p) {
+    if (j != setup_job) {  // uniform across the consumers
+      consumer_sync();     // every warp is done with the previous ranks/table
+      uint32_t distinct, rank;
+      bool present;
+      palette_ranks(reinterpret_cast<const uint32_t*>(J.scratch + 16), srank, distinct, present, rank);
+      escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
+      const bool err = ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch + 4)) != 0;
+      kind = err ? kAutoOverflow
+           : escapes <= J.cap ? kAutoTop16
+           : distinct <= 64 ? kAutoFixed6
+           : J.raw_ok ? kAutoRaw : kAutoOverflow;
+      if (tile == 0 || setup_job < 0) {
+        // the CTA holding tile 0 writes the header
+        if (tile == 0) {
+          if (kind == kAutoOverflow) write_fixed_header<6>(J.dst, distinct > 64 ? distinct : 65, present, rank, true);
+          else if (kind == kAutoFixed6) write_fixed_header<6>(J.dst, distinct, present, rank, false);
+          else if (kind == kAutoRaw && tid == 0) J.dst[0] = 6;
+          else if (kind == kAutoTop16 && tid == 0) write_top16_header(J.dst, escapes, J.cap, false);
+        }
+      }
+      if (kind == kAutoTop16) load_top16_table(J.tables, stbl);
+      setup_job = j;
+      consumer_sync();
     }
-    if (lane == 0) s_prefix = prefix;
-  }
-  // zero this tile's share of the unused escape slots [escapes, cap)
-  {
-    uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
-    const uint64_t lo = 5 * escapes, hi = 5 * J.cap;
-    const uint64_t share = (hi - lo + J.tiles - 1) / J.tiles;
-    const uint64_t a = lo + share * tile;
-    const uint64_t e = min(hi, a + share);
-    for (uint64_t i = a + tid; i < e; i += kThreads) entries[i] = 0;
-  }
-  load_tile_words(J, t0, len, sin, &bar, error);
-  uint32_t masks[kStepsPerWarp];
-  top16_tile_body(J, t0, len, sin, stbl, masks);
-  uint32_t off[kStepsPerWarp];
-  escape_offsets(masks, s_wtot, off);  // syncs: s_prefix visible after
-  write_escapes(J, t0, sin, masks, off, s_prefix);
-  if (tile == 0 && tid == 0) write_top16_header(J.dst, escapes, J.cap, false);
+    const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
+    const uint32_t len = tile_len(J.n, t0);
+    if (kind == kAutoOverflow) return;
+    if (kind == kAutoFixed6) {
+      fixed_tile_body<6>(J, t0, len, sin, srank);
+      return;
+    }
+    if (kind == kAutoRaw) {
+      raw_tile_body(J, t0, len, sin);
+      return;
+    }
+    // top16 with known per-tile offsets: prefix = complete groups before this
+    // tile's group + this group's earlier tiles (the stats pass finished).
+    if ((tid >> 5) == 0) {
+      const int lane = tid & 31;
+      const uint64_t* groups = reinterpret_cast<const uint64_t*>(J.scratch + 64);
+      const uint32_t* counts = reinterpret_cast<const uint32_t*>(groups + groups_for(J.tiles));
+      const uint32_t g = tile >> 5;
+      uint64_t v = lane < static_cast<int>(tile & 31) ? counts[(g << 5) + lane] : 0;
+      uint64_t prefix = warp_sum(v);
+      for (uint32_t base = 0; base < g; base += 32) {
+        v = base + lane < g ? (groups[base + lane] & 0xFFFFFFFFull) : 0;
+        prefix += warp_sum(v);
+      }
+      if (lane == 0) s_prefix[p.k & 1] = prefix;
+    }
+    {  // zero this tile's share of the unused escape slots [escapes, cap)
+      uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
+      const uint64_t lo = 5 * escapes, hi = 5 * J.cap;
+      const uint64_t share = (hi - lo + J.tiles - 1) / J.tiles;
+      const uint64_t a = lo + share * tile;
+      const uint64_t e = min(hi, a + share);
+      for (uint64_t i = a + tid; i < e; i += kThreads) entries[i] = 0;
+    }
+    uint32_t masks[kStepsPerWarp];
+    top16_tile_body(J, t0, len, sin, stbl, masks);
+    uint32_t off[kStepsPerWarp];
+    escape_offsets(masks, s_wtot[p.k & 1], off);  // syncs: s_prefix visible after
+    write_escapes(J, t0, sin, masks, off, s_prefix[p.k & 1]);
+  });
 }
 
 // ------------------------------------------------------------------ decode
+//
+// Producer warp per tile: reads the job's mode byte (once per job), stages
+// the tile's stream bytes by TMA, resolves the destination of each 512-word
+// step in the paged cache (one block-table load per step, off the
+// consumers' path) and, for top16, gathers the tile's escapes into the
+// stage descriptor.  Consumer warps: codes -> 16 words per lane -> two
+// 16-byte stores per lane at the resolved step address.
 
-// Store the 16 words (8 u32, little-endian pairs) of one lane unit starting
-// at packed index g into the paged cache.
+constexpr uint32_t kStepsPerTile = kTileWords / kStepWords;
+constexpr uint32_t kStageEscapes = 512;  // escapes one tile descriptor holds
+
+// Decode stage descriptor, written by the producer warp.
+struct DecDesc {
+  uint32_t tile;   // global tile index, or kEndTile
+  uint32_t job;
+  uint32_t mode;   // stream mode of the job; 0: leave the tile alone
+  uint32_t pad_x;  // offset of the body / low / raw bytes in the stage
+  uint32_t pad_y;  // offset of the codes in the stage's codes region
+  uint32_t unused;
+  uint16_t* step_dst[kStepsPerTile];   // 16-byte aligned contiguous destination of a step, or null
+  uint32_t esc_bits[kTileWords / 32];  // top16: escaped words of the tile
+  uint16_t esc_rank[kTileWords / 32];  // top16: escapes before each bitmap word
+  uint8_t esc_exp[kStageEscapes];      // top16: exponents in position order
+};
+
+// fixed6 pair table of the consumers' current job: entry (c0 | c1 << 6)
+// holds the high bytes of a word pair whose codes are c0 and c1,
+// pal[c0] << 8 | pal[c1] << 24.
+struct DecodeExtra {
+  uint8_t pal[64];
+  uint32_t pair[4096];
+};
+
+// Destination of the 16-word unit at packed index g (valid words `valid`).
 __device__ __forceinline__ void store_unit(uint16_t* dst, const Layout& L, uint64_t g, uint32_t valid,
                                            const uint32_t (&o)[8], bool vec) {
   if (vec && valid == kUnitWords) {
@@ -725,280 +987,435 @@ __device__ __forceinline__ void store_unit(uint16_t* dst, const Layout& L, uint6
   }
 }
 
+// Store this lane's unit of warp step `step`: two 16-byte stores at the
+// step's resolved address, else through the layout word by word.
+__device__ __forceinline__ void store_step(const DecJob& J, const DecDesc& d, uint64_t t0, uint32_t step,
+                                           uint32_t valid, int lane, const uint32_t (&o)[8]) {
+  uint16_t* q = d.step_dst[step];
+  if (q != nullptr) {
+    uint4* p = reinterpret_cast<uint4*>(q + lane * kUnitWords);
+    p[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    p[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  } else if (valid) {
+    store_unit(J.dst, J.L, t0 + step * kStepWords + lane * kUnitWords, valid, o, J.vec != 0);
+  }
+}
+
 __device__ __forceinline__ uint32_t entry_pos(const uint8_t* entries, uint64_t idx) {
   return load_u32le(entries + idx * 5);
 }
 
-struct Top16DecodeSmem {
-  uint8_t body[kTileWords + 64];
-  uint8_t codes[kTileWords / 2 + 64];
-  uint32_t dtbl[512];
-  uint32_t esc_bits[kTileWords / 32];
-  uint8_t esc_exp[kTileWords];
-};
+// prmt.b32 in its default mode: a selector nibble with bit 3 set replicates
+// the sign bit of the selected byte.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
 
-struct Fixed6DecodeSmem {
-  uint8_t low[kTileWords + 64];
-  uint8_t codes[kTileWords * 3 / 4 + 64];
-  uint32_t pal[64];
-};
+// Exponents of four consecutive words from their four 4-bit codes (`nib16`,
+// first word in the low nibble) and a plane's 16-entry codebook held in four
+// registers: two byte permutes pick book[c & 7] from bytes 0-7 and 8-15, a
+// third turns each code's bit 3 into a byte mask.  No table in memory.
+__device__ __forceinline__ uint32_t book_exps4(const uint32_t (&bk)[4], uint32_t nib16) {
+  const uint32_t sel = nib16 & 0x7777u;
+  const uint32_t lo = prmt(bk[0], bk[1], sel);
+  const uint32_t hi = prmt(bk[2], bk[3], sel);
+  const uint32_t m = prmt(nib16 << 4, nib16, 0xD9C8u);
+  return (lo & ~m) | (hi & m);
+}
 
-struct RawDecodeSmem {
-  uint8_t words[2 * kTileWords + 64];
-};
-
-constexpr size_t kDecodeSmemBytes =
-    sizeof(Top16DecodeSmem) > sizeof(Fixed6DecodeSmem)
-        ? (sizeof(Top16DecodeSmem) > sizeof(RawDecodeSmem) ? sizeof(Top16DecodeSmem) : sizeof(RawDecodeSmem))
-        : (sizeof(Fixed6DecodeSmem) > sizeof(RawDecodeSmem) ? sizeof(Fixed6DecodeSmem) : sizeof(RawDecodeSmem));
-
-__device__ __forceinline__ void decode_top16_tile(const DecJob& J, uint32_t tile, Top16DecodeSmem& S,
-                                                  uint64_t* bar, uint32_t* s_last) {
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const uint64_t count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
-  const uint8_t* books = J.tables + 512;
-  for (int i = tid; i < 512; i += kThreads) {
-    const int plane = i >> 8;
-    const uint32_t cb = i & 255;
-    S.dtbl[i] = (static_cast<uint32_t>(__ldg(books + plane * 16 + (cb & 15))) << 7) |
-                (static_cast<uint32_t>(__ldg(books + plane * 16 + (cb >> 4))) << 23);
+// Producer lane 0: stage one tile's stream bytes into a ring stage (TMA
+// bytes registered on `bar`, no arrive).  Returns the pads of the two regions.
+__device__ __forceinline__ uint2 decode_stage(const DecJob& J, uint32_t mode, uint64_t t0, uint32_t len,
+                                              uint8_t* stage, uint64_t* bar) {
+  uint2 pad{0, 0};
+  if (mode == 5) {
+    pad.x = stage_bytes_one(J.src, J.src_bytes, 5 + t0, len, stage, bar);
+    pad.y = stage_bytes_one(J.src, J.src_bytes, 5 + J.n + t0 / 2, (len + 1) / 2, stage + kDecCodesOffset, bar);
+  } else if (mode == 3) {
+    pad.x = stage_bytes_one(J.src, J.src_bytes, 65 + t0, len, stage, bar);
+    pad.y = stage_bytes_one(J.src, J.src_bytes, 65 + J.n + 3 * t0 / 4, 3 * ((len + 3) / 4),
+                            stage + kDecCodesOffset, bar);
+  } else if (mode == 6) {
+    pad.x = stage_bytes_one(J.src, J.src_bytes, 1 + 2 * t0, 2 * len, stage, bar);
   }
-  S.esc_bits[tid] = 0;
-  __syncthreads();
-  const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-  const uint32_t len = tile_len(J.n, t0);
-  const uint32_t pad_b = stage_bytes(J.src, 5 + t0, len, S.body, bar);
-  const uint32_t pad_c = stage_bytes(J.src, 5 + J.n + t0 / 2, (len + 1) / 2, S.codes, bar);
-  if (tid == 0) mbar_arrive(bar);
+  return pad;
+}
 
-  // this tile's escapes: lower_bound(t0) over the entries assuming ascending
-  // positions (warp 32-ary search), then a forward scan while positions fall
-  // in the tile.  Streams in another order are repaired by the last CTA.
+// First entry index whose position is >= t0, assuming ascending positions
+// (warp-wide 32-ary search).
+__device__ uint64_t escape_lower_bound(const uint8_t* entries, uint64_t count, uint64_t t0) {
+  const int lane = threadIdx.x & 31;
+  uint64_t lo = 0, hi = count;  // answer in [lo, hi]
+  while (hi - lo > 32) {
+    const uint64_t step = (hi - lo + 31) / 32;
+    const uint64_t idx = lo + lane * step;
+    const bool probe = idx < hi;
+    const bool below = probe && entry_pos(entries, idx) < t0;
+    const uint32_t nb = __popc(__ballot_sync(kFull, below));
+    const uint32_t np = __popc(__ballot_sync(kFull, probe));
+    const uint64_t nlo = nb ? lo + (nb - 1) * step + 1 : lo;
+    const uint64_t nhi = nb < np ? lo + nb * step : hi;
+    lo = nlo;
+    hi = nhi;
+  }
+  const uint64_t idx = lo + lane;
+  const bool below = idx < hi && entry_pos(entries, idx) < t0;
+  return lo + __popc(__ballot_sync(kFull, below));
+}
+
+// Producer warp: this tile's escapes into the descriptor (bitmap, ranks,
+// exponents in position order).  Entries are taken from `cursor` (the lower
+// bound of t0 when cursor_ok, else searched) while their positions fall in
+// the tile and strictly increase, up to kStageEscapes.  Returns the entries
+// taken; any other entry (out of position order, >= n, or past a tile's
+// capacity) is left to the job's last tile, which applies every entry when
+// the tiles did not take them all.  cursor_ok says whether the cursor ended
+// on the next tile's lower bound.
+__device__ uint32_t producer_escapes(const DecJob& J, uint64_t count, uint64_t t0, uint32_t len, DecDesc& d,
+                                     uint64_t& cursor, bool& cursor_ok) {
+  const int lane = threadIdx.x & 31;
   const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
-  if (warp == 0 && count > 0) {
-    uint64_t lo = 0, hi = count;  // answer in [lo, hi]
-    while (hi - lo > 32) {
-      const uint64_t step = (hi - lo + 31) / 32;
-      const uint64_t idx = lo + lane * step;
-      const bool probe = idx < hi;
-      const bool below = probe && entry_pos(entries, idx) < t0;
-      const uint32_t nb = __popc(__ballot_sync(kFull, below));
-      const uint32_t np = __popc(__ballot_sync(kFull, probe));
-      const uint64_t nlo = nb ? lo + (nb - 1) * step + 1 : lo;
-      const uint64_t nhi = nb < np ? lo + nb * step : hi;
-      lo = nlo;
-      hi = nhi;
+#pragma unroll
+  for (int w = 0; w < static_cast<int>(kTileWords / 32 / 32); ++w) d.esc_bits[w * 32 + lane] = 0;
+  if (!cursor_ok) cursor = escape_lower_bound(entries, count, t0);
+  __syncwarp();
+  uint32_t taken = 0;
+  int64_t last = -1;
+  bool clean = true;
+  while (cursor < count) {
+    const uint64_t idx = cursor + lane;
+    const bool exists = idx < count;
+    const int64_t pos = exists ? static_cast<int64_t>(entry_pos(entries, idx)) : -2;
+    int64_t prev = __shfl_up_sync(kFull, pos, 1);
+    if (lane == 0) prev = last;
+    const bool ok = exists && pos >= static_cast<int64_t>(t0) && pos < static_cast<int64_t>(t0 + len) &&
+                    pos > prev && taken + lane < kStageEscapes;
+    const uint32_t bad = __ballot_sync(kFull, !ok);
+    const int take = bad ? __ffs(bad) - 1 : 32;
+    if (lane < take) {
+      const uint32_t local = static_cast<uint32_t>(pos - static_cast<int64_t>(t0));
+      atomicOr(&d.esc_bits[local >> 5], 1u << (local & 31));
+      d.esc_exp[taken + lane] = __ldg(entries + idx * 5 + 4);
     }
-    {
-      const uint64_t idx = lo + lane;
-      const bool below = idx < hi && entry_pos(entries, idx) < t0;
-      lo += __popc(__ballot_sync(kFull, below));
+    if (take > 0) last = __shfl_sync(kFull, pos, take - 1);
+    taken += take;
+    cursor += take;
+    if (take < 32) {
+      // the entry that stopped the scan opens a later tile, or the scan ran out
+      clean = __shfl_sync(kFull, !exists || (pos >= static_cast<int64_t>(t0 + len) && pos > prev), take);
+      break;
     }
-    uint64_t cur = lo;
-    uint32_t covered = 0;
-    for (uint64_t guard = 0; guard <= count; guard += 32) {
-      const uint64_t idx = cur + lane;
-      uint32_t p = 0;
-      bool in = false;
-      if (idx < count) {
-        p = entry_pos(entries, idx);
-        in = p >= t0 && p < t0 + len;
-      }
-      const uint32_t out = __ballot_sync(kFull, !in);
-      const int first_out = out ? __ffs(out) - 1 : 32;
-      if (lane < first_out) {
-        const uint32_t local = static_cast<uint32_t>(p - t0);
-        atomicOr(&S.esc_bits[local >> 5], 1u << (local & 31));
-        S.esc_exp[local] = __ldg(entries + idx * 5 + 4);
-      }
-      covered += first_out;
-      if (first_out < 32) break;
-      cur += 32;
-    }
-    if (lane == 0 && covered) atomicAdd(&g_decode_slots[J.slot].covered, covered);
   }
-  const bool ok = mbar_wait(bar, 0);
-  if (__syncthreads_or(!ok)) {
-    if (tid == 0) raise_error(nullptr);
-    mbar_wait(bar, 0);
-    __syncthreads();
+  cursor_ok = clean;
+  __syncwarp();
+  // ranks: lane covers bitmap words 8*lane .. 8*lane+7
+  constexpr int kPer = kTileWords / 32 / 32;
+  uint32_t c[kPer];
+  uint32_t mine = 0;
+#pragma unroll
+  for (int w = 0; w < kPer; ++w) {
+    c[w] = __popc(d.esc_bits[kPer * lane + w]);
+    mine += c[w];
   }
+  uint32_t incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  uint32_t run = incl - mine;
+#pragma unroll
+  for (int w = 0; w < kPer; ++w) {
+    d.esc_rank[kPer * lane + w] = static_cast<uint16_t>(run);
+    run += c[w];
+  }
+  return taken;
+}
 
-  const bool vec = J.vec != 0;
+// Mode of a job's stream, or 0 when this kernel must leave it alone
+// (kMode != 0: the reference writes nothing for another mode; kMode == 0:
+// unknown modes and streams shorter than their mode's length are skipped).
+template <int kMode>
+__device__ __forceinline__ uint32_t job_mode(const DecJob& J) {
+  const uint32_t mode = __ldg(J.src);
+  if (kMode != 0) return mode == static_cast<uint32_t>(kMode) ? mode : 0;
+  uint64_t need = 0;
+  if (mode == 5) need = 5 + J.n + (J.n + 1) / 2 + 5 * J.cap;
+  else if (mode == 3) need = 65 + J.n + 3 * ((J.n + 3) / 4);
+  else if (mode == 6) need = 1 + 2 * J.n;
+  return (need == 0 || need > J.src_bytes) ? 0 : mode;
+}
+
+// Producer warp of DecodeKernel.
+template <int kMax, int kMode>
+__device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t* ring, Ring& R, DecDesc* D) {
+  const int lane = threadIdx.x & 31;
+  const Chunk c = cta_chunk(b.tile_start[b.jobs]);
+  RingPos p;
+  int ji = find_job<kMax>(b.tile_start, b.jobs, c.first);
+  int mode_job = -1;
+  uint32_t mode = 0;
+  uint64_t count = 0;
+  uint64_t cursor = 0;
+  bool cursor_ok = false;
+  for (uint32_t t = c.first;; ++t) {
+    producer_acquire(R, p, nullptr);
+    DecDesc& d = D[p.s];
+    if (t >= c.last) {
+      if (lane == 0) d.tile = kEndTile;
+      producer_commit(R, p);
+      return;
+    }
+    ji = advance_job<kMax>(b.tile_start, ji, t);
+    const DecJob& N = b.job[ji];
+    if (ji != mode_job) {
+      mode = job_mode<kMode>(N);
+      count = mode == 5 ? min(static_cast<uint64_t>(load_u32le(N.src + 1)), N.cap) : 0;
+      cursor_ok = false;
+      mode_job = ji;
+    }
+    const uint64_t t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
+    const uint32_t len = tile_len(N.n, t0);
+    if (lane == 0) {
+      const uint2 pad = decode_stage(N, mode, t0, len, ring + p.s * kDecStageBytes, &R.full[p.s]);
+      d.tile = t;
+      d.job = static_cast<uint32_t>(ji);
+      d.mode = mode;
+      d.pad_x = pad.x;
+      d.pad_y = pad.y;
+    }
+    if (lane < static_cast<int>(kStepsPerTile)) {
+      uint16_t* q = nullptr;
+      const uint32_t sb = lane * kStepWords;
+      if (mode != 0 && N.vec != 0 && sb + kStepWords <= len) {
+        const uint64_t g = t0 + sb;
+        if (layout_run(N.L, g) >= kStepWords) q = N.dst + layout_addr(N.L, g);
+      }
+      d.step_dst[lane] = q;
+    }
+    if (mode == 5 && count > 0) {
+      const uint32_t covered = producer_escapes(N, count, t0, len, d, cursor, cursor_ok);
+      if (lane == 0 && covered) {
+        atomicAdd(&g_decode_slots[N.slot].covered, covered);
+        __threadfence();
+      }
+    }
+    producer_commit(R, p);
+    p.next();
+  }
+}
+
+__device__ __forceinline__ void decode_top16_compute(const DecJob& J, const DecDesc& d, const uint8_t* stage,
+                                                     uint64_t t0, uint32_t len, uint32_t hrel, bool escapes,
+                                                     const uint32_t (&bk0)[4], const uint32_t (&bk1)[4]) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t pad_x = d.pad_x, pad_y = d.pad_y;
 #pragma unroll
   for (int s = 0; s < kStepsPerWarp; ++s) {
-    const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-    if (w0 >= len) continue;
-    const uint32_t valid = min(len - w0, static_cast<uint32_t>(kUnitWords));
+    const uint32_t step = warp * kStepsPerWarp + s;
+    const uint32_t sb = step * kStepWords;
+    if (sb >= len) continue;
+    const uint32_t w0 = sb + lane * kUnitWords;
+    const uint32_t valid = w0 < len ? min(len - w0, static_cast<uint32_t>(kUnitWords)) : 0u;
     uint32_t B[4];
-    smem_read16(S.body, pad_b + w0, B);
+    smem_read16_window(stage, pad_x + w0, B);
     uint32_t C[2];
-    smem_read_words<2>(S.codes, pad_c + w0 / 2, C);
-    const uint64_t g = t0 + w0;
+    smem_read8_window(stage + kDecCodesOffset, pad_y + w0 / 2, C);
+    uint32_t e[4];  // exponents of words 4q..4q+3
+    if (w0 >= hrel || w0 + kUnitWords <= hrel) {
+      const bool p1 = w0 >= hrel;
+      uint32_t bk[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) bk[k] = p1 ? bk1[k] : bk0[k];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) e[q] = book_exps4(bk, (C[q >> 1] >> (16 * (q & 1))) & 0xFFFFu);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t nib = (C[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
+        const uint32_t a = book_exps4(bk0, nib);
+        const uint32_t b = book_exps4(bk1, nib);
+        uint32_t m = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (w0 + 4 * q + k >= hrel) m |= 0xFFu << (8 * k);
+        e[q] = (a & ~m) | (b & m);
+      }
+    }
     uint32_t o[8];
-    const bool uniform = g >= J.half || g + kUnitWords <= J.half;
-    const uint32_t* tb = S.dtbl + (g >= J.half ? 256 : 0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t cb = (C[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-      const uint32_t body2 = __byte_perm(B[i >> 1], 0, (i & 1) ? 0x3322 : 0x1100) & 0x807F807Fu;
-      uint32_t ex;
-      if (uniform) {
-        ex = tb[cb];
-      } else {
-        const uint32_t p0 = (g + 2 * i) >= J.half;
-        const uint32_t p1 = (g + 2 * i + 1) >= J.half;
-        ex = (S.dtbl[(p0 << 8) + cb] & 0xFFFFu) | (S.dtbl[(p1 << 8) + cb] & 0xFFFF0000u);
-      }
-      o[i] = body2 | ex;
+      const uint32_t body2 = __byte_perm(B[i >> 1], 0, (i & 1) ? 0x3322 : 0x1100);
+      const uint32_t ex = __byte_perm(e[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140) << 7;
+      o[i] = (body2 & 0x807F807Fu) | ex;
     }
-    const uint32_t eb = (S.esc_bits[w0 >> 5] >> (w0 & 31)) & 0xFFFFu;
+    // the escape map is written only for streams with escapes
+    const uint32_t word = escapes ? d.esc_bits[w0 >> 5] : 0u;
+    const uint32_t eb = (word >> (w0 & 31)) & 0xFFFFu;
     if (eb) {
+      uint32_t r = d.esc_rank[w0 >> 5] + __popc(word & ((1u << (w0 & 31)) - 1u));
 #pragma unroll
       for (int i = 0; i < kUnitWords; ++i) {
         if ((eb >> i) & 1u) {
-          const uint32_t e = S.esc_exp[w0 + i];
+          const uint32_t ev = d.esc_exp[r++];
           const uint32_t sh = (i & 1) * 16;
-          o[i >> 1] = (o[i >> 1] & ~(0x7F80u << sh)) | ((e << 7) << sh);
+          o[i >> 1] = (o[i >> 1] & ~(0x7F80u << sh)) | ((ev << 7) << sh);
         }
       }
     }
-    store_unit(J.dst, J.L, g, valid, o, vec);
-  }
-
-  // Last CTA of the job: apply every entry if the tiles did not account for
-  // all of them (entries out of position order, or positions >= n).
-  if (count == 0) return;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned int prev = atomicAdd(&g_decode_slots[J.slot].done, 1u);
-    *s_last = prev == J.tiles - 1;
-  }
-  __syncthreads();
-  if (!*s_last) return;
-  __threadfence();
-  const uint32_t covered = ld_volatile_u32(&g_decode_slots[J.slot].covered);
-  if (covered != count) {
-    for (uint64_t i = tid; i < count; i += kThreads) {
-      const uint32_t p = entry_pos(entries, i);
-      if (p >= J.n) continue;
-      uint16_t* w = J.dst + layout_addr(J.L, p);
-      *w = static_cast<uint16_t>((__ldcg(w) & 0x807Fu) |
-                                 (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7));
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    g_decode_slots[J.slot].done = 0;
-    g_decode_slots[J.slot].covered = 0;
+    store_step(J, d, t0, step, valid, lane, o);
   }
 }
 
-__device__ __forceinline__ void decode_fixed6_tile(const DecJob& J, uint32_t tile, Fixed6DecodeSmem& S,
-                                                   uint64_t* bar) {
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  if (tid < 64) S.pal[tid] = static_cast<uint32_t>(__ldg(J.src + 1 + tid)) << 8;
-  __syncthreads();
-  const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-  const uint32_t len = tile_len(J.n, t0);
-  const uint32_t pad_l = stage_bytes(J.src, 65 + t0, len, S.low, bar);
-  const uint32_t pad_c = stage_bytes(J.src, 65 + J.n + 3 * t0 / 4, 3 * ((len + 3) / 4), S.codes, bar);
-  if (tid == 0) mbar_arrive(bar);
-  const bool ok = mbar_wait(bar, 0);
-  if (__syncthreads_or(!ok)) {
-    if (tid == 0) raise_error(nullptr);
-    mbar_wait(bar, 0);
-    __syncthreads();
-  }
-  const bool vec = J.vec != 0;
+__device__ __forceinline__ void decode_fixed6_compute(const DecJob& J, const DecDesc& d, const uint8_t* stage,
+                                                      uint64_t t0, uint32_t len, const DecodeExtra& X) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t pad_x = d.pad_x, pad_y = d.pad_y;
+  const uint8_t* pair = reinterpret_cast<const uint8_t*>(X.pair);
 #pragma unroll
   for (int s = 0; s < kStepsPerWarp; ++s) {
-    const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-    if (w0 >= len) continue;
-    const uint32_t valid = min(len - w0, static_cast<uint32_t>(kUnitWords));
+    const uint32_t step = warp * kStepsPerWarp + s;
+    const uint32_t sb = step * kStepWords;
+    if (sb >= len) continue;
+    const uint32_t w0 = sb + lane * kUnitWords;
+    const uint32_t valid = w0 < len ? min(len - w0, static_cast<uint32_t>(kUnitWords)) : 0u;
     uint32_t Lw[4];
-    smem_read16(S.low, pad_l + w0, Lw);
+    smem_read16_window(stage, pad_x + w0, Lw);
     uint32_t Q[3];
-    smem_read_words<3>(S.codes, pad_c + 3 * w0 / 4, Q);
-    uint32_t c[16];
-    c[0] = Q[0] & 63; c[1] = (Q[0] >> 6) & 63; c[2] = (Q[0] >> 12) & 63; c[3] = (Q[0] >> 18) & 63;
-    c[4] = (Q[0] >> 24) & 63; c[5] = ((Q[0] >> 30) | (Q[1] << 2)) & 63;
-    c[6] = (Q[1] >> 4) & 63; c[7] = (Q[1] >> 10) & 63; c[8] = (Q[1] >> 16) & 63;
-    c[9] = (Q[1] >> 22) & 63; c[10] = ((Q[1] >> 28) | (Q[2] << 4)) & 63;
-    c[11] = (Q[2] >> 2) & 63; c[12] = (Q[2] >> 8) & 63; c[13] = (Q[2] >> 14) & 63;
-    c[14] = (Q[2] >> 20) & 63; c[15] = (Q[2] >> 26) & 63;
+    smem_read_words<3>(stage + kDecCodesOffset, pad_y + 3 * w0 / 4, Q);
+    // byte offsets into the pair table of the 12-bit fields 12i..12i+11
+    uint32_t f[8];
+    f[0] = (Q[0] << 2) & 0x3FFCu;
+    f[1] = (Q[0] >> 10) & 0x3FFCu;
+    f[2] = __funnelshift_r(Q[0], Q[1], 22) & 0x3FFCu;
+    f[3] = (Q[1] >> 2) & 0x3FFCu;
+    f[4] = (Q[1] >> 14) & 0x3FFCu;
+    f[5] = __funnelshift_r(Q[1], Q[2], 26) & 0x3FFCu;
+    f[6] = (Q[2] >> 6) & 0x3FFCu;
+    f[7] = (Q[2] >> 18) & 0x3FFCu;
     uint32_t o[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t l2 = __byte_perm(Lw[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140);
-      o[i] = l2 | S.pal[c[2 * i]] | (S.pal[c[2 * i + 1]] << 16);
-    }
-    store_unit(J.dst, J.L, t0 + w0, valid, o, vec);
+    for (int i = 0; i < 8; ++i)
+      o[i] = __byte_perm(Lw[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140) |
+             *reinterpret_cast<const uint32_t*>(pair + f[i]);
+    store_step(J, d, t0, step, valid, lane, o);
   }
 }
 
-__device__ __forceinline__ void decode_raw_tile(const DecJob& J, uint32_t tile, RawDecodeSmem& S,
-                                                uint64_t* bar) {
+__device__ __forceinline__ void decode_raw_compute(const DecJob& J, const DecDesc& d, const uint8_t* stage,
+                                                   uint64_t t0, uint32_t len) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t pad_x = d.pad_x;
+#pragma unroll
+  for (int s = 0; s < kStepsPerWarp; ++s) {
+    const uint32_t step = warp * kStepsPerWarp + s;
+    const uint32_t sb = step * kStepWords;
+    if (sb >= len) continue;
+    const uint32_t w0 = sb + lane * kUnitWords;
+    const uint32_t valid = w0 < len ? min(len - w0, static_cast<uint32_t>(kUnitWords)) : 0u;
+    uint32_t o[8];
+    smem_read_words<8>(stage, pad_x + 2 * w0, o);
+    store_step(J, d, t0, step, valid, lane, o);
+  }
+}
+
+// kMode: 5 = top16, 3 = fixed6, 0 = dispatch on each stream's mode byte.
+template <int kMax, int kMode>
+__global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_constant__ DecBatch<kMax> b) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ __align__(16) DecodeExtra X;
+  __shared__ __align__(16) DecDesc D[kStages];
+  __shared__ Ring R;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-  const uint32_t len = tile_len(J.n, t0);
-  const uint32_t pad = stage_bytes(J.src, 1 + 2 * t0, 2 * len, S.words, bar);
-  if (tid == 0) mbar_arrive(bar);
-  const bool ok = mbar_wait(bar, 0);
-  if (__syncthreads_or(!ok)) {
-    if (tid == 0) raise_error(nullptr);
-    mbar_wait(bar, 0);
-    __syncthreads();
+  ring_init(R);
+  __syncthreads();
+  if (warp == kProducerWarp) {
+    decode_producer<kMax, kMode>(b, ring, R, D);
+    return;
   }
-  const bool vec = J.vec != 0;
+  int book_job = -1, pair_job = -1;
+  uint64_t job_count = 0;                                 // escape count of book_job's stream
+  uint32_t bk0[4] = {0, 0, 0, 0}, bk1[4] = {0, 0, 0, 0};  // top16 codebooks of book_job
+  RingPos p;
+  for (;;) {
+    consumer_wait(R, p, nullptr);
+    const DecDesc& d = D[p.s];
+    const uint32_t t = d.tile;
+    if (t == kEndTile) break;
+    const uint32_t mode = d.mode;
+    if (mode != 0) {  // uniform across the consumers
+      const int ji = static_cast<int>(d.job);
+      const DecJob& J = b.job[ji];
+      const uint64_t t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
+      const uint32_t len = tile_len(J.n, t0);
+      const uint8_t* stage = ring + p.s * kDecStageBytes;
+      if (mode == 5) {
+        if (ji != book_job) {
+          const uint8_t* books = J.tables + 512;
 #pragma unroll
-  for (int s = 0; s < kStepsPerWarp; ++s) {
-    const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-    if (w0 >= len) continue;
-    const uint32_t valid = min(len - w0, static_cast<uint32_t>(kUnitWords));
-    uint32_t o[8];
-    smem_read_words<8>(S.words, pad + 2 * w0, o);
-    store_unit(J.dst, J.L, t0 + w0, valid, o, vec);
-  }
-}
-
-// kMode: 5 = top16, 3 = fixed6, 0 = dispatch on each stream's mode byte
-// (5, 3 or 6; a stream shorter than its mode's size is skipped).
-template <int kMax, int kMode>
-__global__ void __launch_bounds__(kThreads) DecodeKernel(const __grid_constant__ DecBatch<kMax> b) {
-  __shared__ __align__(128) uint8_t smem[kDecodeSmemBytes];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t s_last;
-  const int j = find_job<kMax>(b.tile_start, b.jobs, blockIdx.x);
-  const DecJob& J = b.job[j];
-  const uint32_t tile = blockIdx.x - b.tile_start[j];
-  const uint32_t mode = __ldg(J.src);
-  if (kMode != 0 && mode != static_cast<uint32_t>(kMode)) return;  // reference: write nothing
-  if (kMode == 0) {
-    uint64_t need = 0;
-    if (mode == 5) need = 5 + J.n + (J.n + 1) / 2 + 5 * J.cap;
-    else if (mode == 3) need = 65 + J.n + 3 * ((J.n + 3) / 4);
-    else if (mode == 6) need = 1 + 2 * J.n;
-    if (need == 0 || need > J.src_bytes) return;
-  }
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
-  if (mode == 5) {
-    decode_top16_tile(J, tile, *reinterpret_cast<Top16DecodeSmem*>(smem), &bar, &s_last);
-  } else if (mode == 3) {
-    decode_fixed6_tile(J, tile, *reinterpret_cast<Fixed6DecodeSmem*>(smem), &bar);
-  } else {
-    __syncthreads();
-    decode_raw_tile(J, tile, *reinterpret_cast<RawDecodeSmem*>(smem), &bar);
+          for (int k = 0; k < 4; ++k) {
+            bk0[k] = load_u32le(books + 4 * k);
+            bk1[k] = load_u32le(books + 16 + 4 * k);
+          }
+          job_count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
+          book_job = ji;
+        }
+        const uint32_t hrel =
+            J.half <= t0 ? 0u : static_cast<uint32_t>(min(J.half - t0, static_cast<uint64_t>(kTileWords)));
+        decode_top16_compute(J, d, stage, t0, len, hrel, job_count > 0, bk0, bk1);
+        if (job_count > 0) {
+          // the job's last tile to finish applies every entry if the tiles
+          // did not take them all (out of position order, or >= n)
+          __threadfence();
+          consumer_sync();
+          if (warp == 0) {
+            uint32_t last = 0;
+            if (lane == 0) last = atomicAdd(&g_decode_slots[J.slot].done, 1u) == J.tiles - 1;
+            if (__shfl_sync(kFull, last, 0)) {
+              __threadfence();
+              const uint32_t covered = ld_volatile_u32(&g_decode_slots[J.slot].covered);
+              if (covered != job_count) {
+                const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
+                for (uint64_t i = lane; i < job_count; i += 32) {
+                  const uint32_t q = entry_pos(entries, i);
+                  if (q >= J.n) continue;
+                  uint16_t* w = J.dst + layout_addr(J.L, q);
+                  *w = static_cast<uint16_t>((__ldcg(w) & 0x807Fu) |
+                                             (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7));
+                }
+              }
+              __syncwarp();
+              if (lane == 0) {
+                g_decode_slots[J.slot].done = 0;
+                g_decode_slots[J.slot].covered = 0;
+              }
+            }
+          }
+        }
+      } else if (mode == 3) {
+        if (ji != pair_job) {
+          consumer_sync();  // every warp is done with the previous table
+          if (tid < 64) X.pal[tid] = __ldg(J.src + 1 + tid);
+          consumer_sync();
+          for (int i = tid; i < 4096; i += kThreads)
+            X.pair[i] = (static_cast<uint32_t>(X.pal[i & 63]) << 8) | (static_cast<uint32_t>(X.pal[i >> 6]) << 24);
+          pair_job = ji;
+          consumer_sync();
+        }
+        decode_fixed6_compute(J, d, stage, t0, len, X);
+      } else {
+        decode_raw_compute(J, d, stage, t0, len);
+      }
+    }
+    consumer_release(R, p);
+    p.next();
   }
 }
 
