@@ -240,3 +240,60 @@ def test_profiler_counts_launches():
     assert prof["DecodeAutoKernel"][1] == 3
     assert prof["ZeroKernel"][1] == 3
     assert all(ms > 0 for ms, _ in prof.values())
+
+
+def test_auto_round_trip_at_every_stream_alignment():
+    """Full tiles coded into stream buffers that start at each byte offset
+    0..15: the warp run stores take every funnel shift (and the aligned
+    path), in all three modes, for encode and decode."""
+    rng = np.random.Generator(np.random.PCG64(7))
+    shape = (16, 8, 128)
+    pool = 8
+    sources = {
+        "top16": make_case(rng, pool, shape, 6, 0.003),
+        "fixed6": make_case(rng, pool, shape, 7, 0.02, escape_choices=3),
+        "raw": (rng.integers(0, 1 << 16, size=(2, pool) + shape, dtype=np.uint16),
+                rng.permutation(pool)[:4].astype(np.int64), tables_np(0)),
+    }
+    n = 2 * 4 * int(np.prod(shape))
+    cap = S.auto_capacity(n)
+    expected = {}
+    for kind, (cache, ids, tab) in sources.items():
+        if kind == "top16":
+            expected[kind] = oracle.encode_top16_blocks(cache, ids, tab)[1]
+        elif kind == "fixed6":
+            expected[kind] = oracle.encode_mode_blocks(cache, ids, bits=6)[1]
+        else:
+            expected[kind] = np.concatenate([[6], cache[:, ids].reshape(-1).view(np.uint8)]).astype(np.uint8)
+    big = torch.zeros(48 * (cap + 64), dtype=torch.uint8, device="cuda")
+    jobs, views, keep, order = [], [], [], []
+    for kind, (cache, ids, tab) in sources.items():
+        kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+        ids_t, tab_t = dev(ids), dev(tab)
+        keep += [kv, ids_t, tab_t]
+        for off in range(16):
+            start = len(views) * (cap + 64) + off
+            view = big[start : start + cap]
+            jobs.append(job_for(kv, ids_t, view, tab_t))
+            views.append(view)
+            order.append((kind, off))
+    assert S.encode_auto_batch(jobs)
+    torch.cuda.synchronize()
+    for (kind, off), view in zip(order, views):
+        want = expected[kind]
+        got = view.cpu().numpy()[: want.size]
+        assert np.array_equal(got, want), (kind, off, int(np.flatnonzero(got != want)[0]))
+    targets, djobs = [], []
+    for (kind, off), view in zip(order, views):
+        cache, ids, tab = sources[kind]
+        out = torch.full(cache.shape, 0x1357, dtype=torch.int16, device="cuda").view(torch.bfloat16)
+        ids_t, tab_t = dev(ids), dev(tab)
+        keep += [ids_t, tab_t]  # the jobs hold raw pointers
+        targets.append((kind, off, out))
+        djobs.append(job_for(out, ids_t, view, tab_t, stream_bytes=expected[kind].size))
+    assert S.decode_auto_batch(djobs)
+    torch.cuda.synchronize()
+    for kind, off, out in targets:
+        cache, ids, _ = sources[kind]
+        got = to_u16(out)
+        assert np.array_equal(got[:, ids], cache[:, ids]), (kind, off)

@@ -384,6 +384,91 @@ __device__ __forceinline__ void smem_read_words(const uint8_t* buf, uint32_t off
   for (int k = 0; k < N; ++k) out[k] = __funnelshift_r(a[k], a[k + 1], sh);
 }
 
+// Store a warp's run of K steps: in step k lane L owns the 4*NW bytes at run
+// offset 4*NW*(32k + L), held in D[k].  Aligned S-byte slots (S = 4 or 8,
+// 4*NW a multiple of S) take the bytes that straddle two lanes, or two steps
+// (lane 31 of step k and lane 0 of step k+1), by one shuffle per word; only
+// the < S bytes at each end of the run go out as single byte stores.
+template <int NW, int S, int K>
+__device__ __forceinline__ void warp_store_run(uint8_t* g, const uint32_t (&D)[K][NW], int lane) {
+  static_assert(S == 4 || S == 8, "slot size");
+  static_assert(NW >= 2 && (4 * NW) % S == 0, "whole slots per lane");
+  constexpr uint32_t kLaneBytes = 4 * NW;
+  constexpr uint32_t kStepBytes = 32 * kLaneBytes;
+  const uintptr_t base = reinterpret_cast<uintptr_t>(g);
+  const uint32_t s = static_cast<uint32_t>(base % S);
+  if (s == 0) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if (S == 8) {
+        uint2* p = reinterpret_cast<uint2*>(base + k * kStepBytes) + lane * (NW / 2);
+#pragma unroll
+        for (int j = 0; j < NW / 2; ++j) p[j] = make_uint2(D[k][2 * j], D[k][2 * j + 1]);
+      } else {
+        uint32_t* p = reinterpret_cast<uint32_t*>(base + k * kStepBytes) + lane * NW;
+#pragma unroll
+        for (int j = 0; j < NW; ++j) p[j] = D[k][j];
+      }
+    }
+    return;
+  }
+  const uint32_t o = S - s;     // run bytes before the first aligned slot
+  const bool q = (o & 4) != 0;  // word offset of that slot in the lane's data
+  const uint32_t r = (o & 3) * 8;
+  const int src = (lane + 1) & 31;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    // the next lane's first two words; lane 31 reads lane 0 of step k+1
+    const bool wrap = lane == 0 && k + 1 < K;
+    const uint32_t n0 = wrap ? D[k + 1 < K ? k + 1 : k][0] : D[k][0];
+    const uint32_t n1 = wrap ? D[k + 1 < K ? k + 1 : k][1] : D[k][1];
+    uint32_t W[NW + 2];
+#pragma unroll
+    for (int j = 0; j < NW; ++j) W[j] = D[k][j];
+    W[NW] = __shfl_sync(kFull, n0, src);
+    W[NW + 1] = __shfl_sync(kFull, n1, src);
+    uint32_t out[NW];
+#pragma unroll
+    for (int j = 0; j < NW; ++j) {
+      const uint32_t a = q ? W[j + 1] : W[j];
+      const uint32_t b = q ? W[j + 2] : W[j + 1];
+      out[j] = __funnelshift_r(a, b, r);
+    }
+    // lane 31's last slot of the last step reaches past the run: the tail
+    // bytes below cover its part
+    const uintptr_t first = base + o + k * kStepBytes + static_cast<uintptr_t>(lane) * kLaneBytes;
+    const bool last_lane = k == K - 1 && lane == 31;
+    if (S == 8) {
+      uint2* p = reinterpret_cast<uint2*>(first);
+#pragma unroll
+      for (int j = 0; j < NW / 2; ++j)
+        if (j < NW / 2 - 1 || !last_lane) p[j] = make_uint2(out[2 * j], out[2 * j + 1]);
+    } else {
+      uint32_t* p = reinterpret_cast<uint32_t*>(first);
+#pragma unroll
+      for (int j = 0; j < NW; ++j)
+        if (j < NW - 1 || !last_lane) p[j] = out[j];
+    }
+  }
+  // head: run bytes [0, o) are lane 0's first bytes of step 0; tail: the
+  // run's last s bytes are lane 31's last bytes of step K-1
+  const uint32_t h0 = __shfl_sync(kFull, D[0][0], 0);
+  const uint32_t h1 = __shfl_sync(kFull, D[0][1], 0);
+  const uint32_t t0 = __shfl_sync(kFull, D[K - 1][NW - 2], 31);
+  const uint32_t t1 = __shfl_sync(kFull, D[K - 1][NW - 1], 31);
+  {
+    const uint32_t word = lane < 4 ? h0 : h1;
+    st_global_u8_if(static_cast<uint32_t>(lane) < o, reinterpret_cast<uint8_t*>(base) + lane,
+                    (word >> (8 * (lane & 3))) & 0xFFu);
+  }
+  {
+    const uint32_t idx = kLaneBytes - s + lane;  // byte of lane 31's data
+    const uint32_t word = (idx >> 2) == static_cast<uint32_t>(NW - 1) ? t1 : t0;
+    st_global_u8_if(static_cast<uint32_t>(lane) < s,
+                    reinterpret_cast<uint8_t*>(base + K * kStepBytes - s) + lane, (word >> (8 * (idx & 3))) & 0xFFu);
+  }
+}
+
 // ---------------------------------------------------------------- staging
 
 // Stage words [t0, t0+len) of a bulk-capable layout (base 16-byte aligned,

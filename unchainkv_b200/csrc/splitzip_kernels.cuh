@@ -27,12 +27,13 @@ namespace ukv {
 constexpr int kMaxBatch = 96;
 constexpr uint64_t kStatusFlag = 1ull << 63;
 constexpr int kDecodeSlots = 1024;
-constexpr int kStages = 3;
+constexpr int kEncStages = 4;  // ring depth of the encode kernels (16 KiB stages)
+constexpr int kDecStages = 3;  // ring depth of the decode kernel (16.1 KiB stages + descriptors)
 constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 16 KiB of words
 constexpr uint32_t kDecStageBytes = 2 * kTileWords + 128;
 constexpr uint32_t kDecCodesOffset = kTileWords + 128;  // top16/fixed6 codes inside a stage
-constexpr uint32_t kEncSmemBytes = kStages * kEncStageBytes;
-constexpr uint32_t kDecSmemBytes = kStages * kDecStageBytes;
+constexpr uint32_t kEncSmemBytes = kEncStages * kEncStageBytes;
+constexpr uint32_t kDecSmemBytes = kDecStages * kDecStageBytes;
 
 struct DecodeSlot {
   unsigned int done;
@@ -173,7 +174,7 @@ __device__ __forceinline__ uint32_t step_valid_words(uint32_t len, uint32_t sb) 
 
 // ------------------------------------------------------- ring pipeline
 //
-// Warp-specialized: warp kProducerWarp stages tiles into a kStages ring of
+// Warp-specialized: warp kProducerWarp stages tiles into a ring of
 // shared-memory buffers (TMA bulk copies issued by its lane 0, plus the
 // per-tile descriptor the consumers need); warps 0..kWarps-1 code the
 // tiles.  full[s] completes when the 32 producer lanes have arrived and the
@@ -186,15 +187,17 @@ constexpr int kCtaThreads = kThreads + 32;
 constexpr int kProducerWarp = kWarps;
 constexpr uint32_t kEndTile = 0xFFFFFFFFu;
 
+template <int S>
 struct Ring {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[S];
+  uint64_t empty[S];
 };
 
-__device__ __forceinline__ void ring_init(Ring& R) {
+template <int S>
+__device__ __forceinline__ void ring_init(Ring<S>& R) {
   if (threadIdx.x == 0) {
 #pragma unroll
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&R.full[s], 32);
       mbar_init(&R.empty[s], kWarps);
     }
@@ -202,14 +205,16 @@ __device__ __forceinline__ void ring_init(Ring& R) {
   }
 }
 
-// Position in the ring: uses so far, stage, parity of the stage's current use.
+// Position in a ring of S stages: uses so far, stage, parity of the stage's
+// current use.
+template <int S>
 struct RingPos {
   uint32_t k = 0;
   int s = 0;
   uint32_t phase = 0;
   __device__ __forceinline__ void next() {
     ++k;
-    if (++s == kStages) {
+    if (++s == S) {
       s = 0;
       phase ^= 1u;
     }
@@ -226,19 +231,25 @@ __device__ __forceinline__ void wait_stage(uint64_t* bar, uint32_t parity, uint3
 }
 
 // Producer: wait until every consumer warp released the stage's previous use.
-__device__ __forceinline__ void producer_acquire(Ring& R, const RingPos& p, uint32_t* error) {
-  if (p.k >= kStages) wait_stage(&R.empty[p.s], p.phase ^ 1u, error);
+template <int S>
+__device__ __forceinline__ void producer_acquire(Ring<S>& R, const RingPos<S>& p, uint32_t* error) {
+  if (p.k >= S) wait_stage(&R.empty[p.s], p.phase ^ 1u, error);
 }
 
 // Producer, every lane: publish the stage (after its descriptor writes).
-__device__ __forceinline__ void producer_commit(Ring& R, const RingPos& p) { mbar_arrive(&R.full[p.s]); }
+template <int S>
+__device__ __forceinline__ void producer_commit(Ring<S>& R, const RingPos<S>& p) {
+  mbar_arrive(&R.full[p.s]);
+}
 
-__device__ __forceinline__ void consumer_wait(Ring& R, const RingPos& p, uint32_t* error) {
+template <int S>
+__device__ __forceinline__ void consumer_wait(Ring<S>& R, const RingPos<S>& p, uint32_t* error) {
   wait_stage(&R.full[p.s], p.phase, error);
 }
 
 // Consumer warp: done with the stage (all lanes' reads precede lane 0's arrive).
-__device__ __forceinline__ void consumer_release(Ring& R, const RingPos& p) {
+template <int S>
+__device__ __forceinline__ void consumer_release(Ring<S>& R, const RingPos<S>& p) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&R.empty[p.s]);
 }
@@ -248,22 +259,36 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
 }
 
-// Encode stage descriptor: global tile index (or kEndTile) and its job.
+using EncRing = Ring<kEncStages>;
+using EncPos = RingPos<kEncStages>;
+using DecRing = Ring<kDecStages>;
+using DecPos = RingPos<kDecStages>;
+
+// Encode stage descriptor: global tile index (or kEndTile), its job and a
+// word the kernel's producer hook computed for it.
 struct EncDesc {
   uint32_t tile;
   uint32_t job;
+  uint32_t aux;
+  uint32_t unused;
+};
+
+// Producer hook that annotates nothing.
+struct NoAux {
+  template <typename Job>
+  __device__ __forceinline__ uint32_t operator()(const Job&) const { return 0; }
 };
 
 // Producer warp of the encode kernels: stages the tiles next_tile() yields
 // (increasing; >= total ends) into the ring.  A bulk-capable layout takes one
 // TMA copy per contiguous run from lane 0; any other is gathered word by word
 // by the 32 lanes.
-template <int kMax, typename Next>
-__device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t* ring, Ring& R, EncDesc* D,
-                                                Next&& next_tile) {
+template <int kMax, typename Next, typename Aux = NoAux>
+__device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R, EncDesc* D,
+                                                Next&& next_tile, Aux aux = Aux()) {
   const int lane = threadIdx.x & 31;
   const uint32_t total = b.tile_start[b.jobs];
-  RingPos p;
+  EncPos p;
   int ji = 0;
   for (;;) {
     producer_acquire(R, p, nullptr);
@@ -281,6 +306,7 @@ __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t
     if (lane == 0) {
       D[p.s].tile = t;
       D[p.s].job = static_cast<uint32_t>(ji);
+      D[p.s].aux = aux(J);
     }
     if (J.bulk != 0) {
       if (lane == 0) stage_words_tma(J.src, J.L, t0, len, sin, &R.full[p.s]);
@@ -301,28 +327,28 @@ struct ChunkTiles {
 // Consumer warps of the encode kernels: fn(job, job_index, tile, words,
 // ring position) for every staged tile until the end descriptor.
 template <int kMax, typename Fn>
-__device__ __forceinline__ void encode_consumer(const EncBatch<kMax>& b, uint8_t* ring, Ring& R,
+__device__ __forceinline__ void encode_consumer(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R,
                                                 const EncDesc* D, Fn&& fn) {
-  RingPos p;
+  EncPos p;
   for (;;) {
     consumer_wait(R, p, nullptr);
     const EncDesc d = D[p.s];
     if (d.tile == kEndTile) return;
     const EncJob& J = b.job[d.job];
     fn(J, static_cast<int>(d.job), d.tile - b.tile_start[d.job],
-       reinterpret_cast<const uint16_t*>(ring + p.s * kEncStageBytes), p);
+       reinterpret_cast<const uint16_t*>(ring + p.s * kEncStageBytes), p, d.aux);
     consumer_release(R, p);
     p.next();
   }
 }
 
 // Chunk-scheduled encode kernel body: producer warp + consumer warps.
-template <int kMax, typename Fn>
-__device__ __forceinline__ void encode_pipeline(const EncBatch<kMax>& b, uint8_t* ring, Ring& R, EncDesc* D,
-                                                Fn&& fn) {
+template <int kMax, typename Fn, typename Aux = NoAux>
+__device__ __forceinline__ void encode_pipeline(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R, EncDesc* D,
+                                                Fn&& fn, Aux aux = Aux()) {
   if ((threadIdx.x >> 5) == kProducerWarp) {
     const Chunk c = cta_chunk(b.tile_start[b.jobs]);
-    encode_producer<kMax>(b, ring, R, D, ChunkTiles{c.first, c.last});
+    encode_producer<kMax>(b, ring, R, D, ChunkTiles{c.first, c.last}, aux);
     return;
   }
   encode_consumer<kMax>(b, ring, R, D, fn);
@@ -381,6 +407,27 @@ __device__ __forceinline__ void top16_tile_body(const EncJob& J, uint64_t t0, ui
                                                 uint32_t (&masks)[kStepsPerWarp]) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  if (len == kTileWords) {  // full tile: the warp's steps form one run per region
+    uint32_t bb[kStepsPerWarp][4];
+    uint32_t cw[kStepsPerWarp][2];
+#pragma unroll
+    for (int s = 0; s < kStepsPerWarp; ++s) {
+      const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
+      uint32_t x[8];
+      load_unit(sin, w0, x);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t lo = __byte_perm(x[2 * q], x[2 * q + 1], 0x6420);
+        const uint32_t hi = __byte_perm(x[2 * q], x[2 * q + 1], 0x7531);
+        bb[s][q] = (lo & 0x7F7F7F7Fu) | (hi & 0x80808080u);
+      }
+      top16_unit_codes(x, stbl, t0 + w0, J.half, cw[s][0], cw[s][1], masks[s]);
+    }
+    const uint64_t r0 = t0 + static_cast<uint64_t>(warp) * kStepsPerWarp * kStepWords;
+    warp_store_run<4, 8, kStepsPerWarp>(J.dst + 5 + r0, bb, lane);
+    warp_store_run<2, 8, kStepsPerWarp>(J.dst + 5 + J.n + r0 / 2, cw, lane);
+    return;
+  }
 #pragma unroll
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t sb = (warp * kStepsPerWarp + s) * kStepWords;
@@ -553,8 +600,8 @@ template <int kMax>
 __global__ void __launch_bounds__(kCtaThreads, 3) EncodeTop16Kernel(const __grid_constant__ EncBatch<kMax> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint32_t stbl[512];
-  __shared__ Ring R;
-  __shared__ EncDesc D[kStages];
+  __shared__ EncRing R;
+  __shared__ EncDesc D[kEncStages];
   __shared__ uint32_t s_wtot[2][2][kWarps];
   __shared__ uint64_t s_prefix[2];
   const int tid = threadIdx.x;
@@ -571,7 +618,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeTop16Kernel(const __grid
   }
   int table_job = -1;
   encode_consumer<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const RingPos& p) {
+                                           const EncPos& p, uint32_t) {
     uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 4);
     if (j != table_job) {  // uniform across the consumers
       consumer_sync();     // every warp is done with the previous table
@@ -603,13 +650,23 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeTop16Kernel(const __grid
 // High-byte presence of every word (-> job bitmap) and, for kStats, the
 // top16 escape count of every tile (-> tile count, group sum, job total; each
 // warp adds its own share, so no CTA barrier is needed for the counts).
+//
+// The presence table holds high byte h at index h ^ (sign << 2), so that a
+// value and its negation (which share every other bit of h) fall in
+// different shared-memory banks.  Word order does not matter here, so each
+// lane reads two 16-byte chunks that are contiguous across the warp
+// (conflict-free).  Once a job's running escape total exceeds its top16
+// capacity the job cannot be top16 and its remaining tiles skip the escape
+// count (the producer reads the total for each tile).
+__device__ __forceinline__ uint32_t presence_index(uint32_t h) { return h ^ ((h >> 5) & 4u); }
+
 template <int kMax, bool kStats>
 __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_constant__ EncBatch<kMax> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint8_t spres[256];
   __shared__ uint8_t sesc[512];  // 1 where the exponent has no top16 code
-  __shared__ Ring R;
-  __shared__ EncDesc D[kStages];
+  __shared__ EncRing R;
+  __shared__ EncDesc D[kEncStages];
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -621,13 +678,17 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
   // (consumers only; every warp is past its last presence store)
   auto flush = [&](const EncJob& P) {
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(P.scratch + (kStats ? 16 : 0));
-    const uint32_t bits = __ballot_sync(kFull, spres[tid] != 0);
+    const uint32_t bits = __ballot_sync(kFull, spres[presence_index(tid)] != 0);
     if (lane == 0 && bits) atomicOr(&bitmap[warp], bits);
     consumer_sync();
     if (tid < 64) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
   };
+  // aux = 1 when the job's escapes already exceed its top16 capacity
+  auto over_cap = [](const EncJob& J) -> uint32_t {
+    return kStats && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap;
+  };
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const RingPos&) {
+                                           const EncPos&, uint32_t skip_escapes) {
     if (j != pres_job || (kStats && j != table_job)) {  // uniform across the consumers
       consumer_sync();
       if (j != pres_job) {
@@ -642,20 +703,27 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     }
     const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
     const uint32_t len = tile_len(J.n, t0);
+    const bool count = kStats && !skip_escapes;
     uint32_t escapes = 0;
     if (len == kTileWords && (t0 >= J.half || t0 + kTileWords <= J.half)) {
       // whole tile in one plane: table offset fixed, no bounds
       const uint32_t poff = t0 >= J.half ? 256u : 0u;
 #pragma unroll
       for (int s = 0; s < kStepsPerWarp; ++s) {
-        const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-        uint32_t x[8];
-        load_unit(sin, w0, x);
+        const uint16_t* w = sin + (warp * kStepsPerWarp + s) * kStepWords + 8 * lane;
+        const uint4 v0 = *reinterpret_cast<const uint4*>(w);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(w + 256);
+        const uint32_t x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
-          spres[__byte_perm(x[p], 0, 0x4441)] = 1;
-          spres[x[p] >> 24] = 1;
-          if (kStats) escapes += sesc[((x[p] >> 7) & 0xFFu) | poff] + sesc[((x[p] >> 23) & 0xFFu) | poff];
+          const uint32_t y = x[p] ^ ((x[p] >> 5) & 0x04000400u);
+          spres[__byte_perm(y, 0, 0x4441)] = 1;
+          spres[y >> 24] = 1;
+        }
+        if (count) {
+#pragma unroll
+          for (int p = 0; p < 8; ++p)
+            escapes += sesc[((x[p] >> 7) & 0xFFu) | poff] + sesc[((x[p] >> 23) & 0xFFu) | poff];
         }
       }
     } else {
@@ -667,12 +735,12 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
         const uint64_t g = t0 + w0;
         for (uint32_t i = 0; i < valid; ++i) {
           const uint32_t w = sin[w0 + i];
-          spres[w >> 8] = 1;
-          if (kStats) escapes += sesc[((g + i) >= J.half ? 256 : 0) + ((w >> 7) & 0xFFu)];
+          spres[presence_index(w >> 8)] = 1;
+          if (count) escapes += sesc[((g + i) >= J.half ? 256 : 0) + ((w >> 7) & 0xFFu)];
         }
       }
     }
-    if (kStats) {
+    if (count) {
       escapes = warp_sum(escapes);
       if (lane == 0 && escapes) {
         uint64_t* groups = reinterpret_cast<uint64_t*>(J.scratch + 64);
@@ -682,7 +750,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
         atomicAdd(reinterpret_cast<uint32_t*>(J.scratch), escapes);
       }
     }
-  });
+  }, over_cap);
   if (warp == kProducerWarp) return;
   consumer_sync();
   if (pres_job >= 0) flush(b.job[pres_job]);
@@ -721,10 +789,47 @@ __device__ __forceinline__ void write_fixed_header(uint8_t* dst, uint32_t distin
   if (tid == 0) dst[0] = (distinct > kLimit || error) ? 255 : (kBits == 6 ? 3 : 4);
 }
 
+// A full fixed6 tile: each warp codes its run of kStepsPerWarp steps, then
+// stores the run's low bytes and its codes as two contiguous runs.
+__device__ __forceinline__ void fixed6_tile_full(const EncJob& J, uint64_t t0, const uint16_t* sin,
+                                                 const uint8_t* srank) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  uint32_t low[kStepsPerWarp][4];
+  uint32_t qw[kStepsPerWarp][3];
+#pragma unroll
+  for (int s = 0; s < kStepsPerWarp; ++s) {
+    const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
+    uint32_t x[8];
+    load_unit(sin, w0, x);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) low[s][q] = __byte_perm(x[2 * q], x[2 * q + 1], 0x6420);
+    uint32_t g[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t c0 = srank[__byte_perm(x[2 * q], 0, 0x4441)];
+      const uint32_t c1 = srank[x[2 * q] >> 24];
+      const uint32_t c2 = srank[__byte_perm(x[2 * q + 1], 0, 0x4441)];
+      const uint32_t c3 = srank[x[2 * q + 1] >> 24];
+      g[q] = c0 | (c1 << 6) | (c2 << 12) | (c3 << 18);
+    }
+    qw[s][0] = g[0] | (g[1] << 24);
+    qw[s][1] = (g[1] >> 8) | (g[2] << 16);
+    qw[s][2] = (g[2] >> 16) | (g[3] << 8);
+  }
+  const uint64_t r0 = t0 + static_cast<uint64_t>(warp) * kStepsPerWarp * kStepWords;
+  warp_store_run<4, 8, kStepsPerWarp>(J.dst + 65 + r0, low, lane);
+  warp_store_run<3, 4, kStepsPerWarp>(J.dst + 65 + J.n + 3 * r0 / 4, qw, lane);
+}
+
 template <int kBits>
 __device__ __forceinline__ void fixed_tile_body(const EncJob& J, uint64_t t0, uint32_t len,
                                                 const uint16_t* sin, const uint8_t* srank) {
   constexpr uint32_t kHeader = kBits == 6 ? 65 : 33;
+  if (kBits == 6 && len == kTileWords) {
+    fixed6_tile_full(J, t0, sin, srank);
+    return;
+  }
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
 #pragma unroll
@@ -797,14 +902,14 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeFixedKernel(const __grid
   constexpr uint32_t kLimit = kBits == 6 ? 64 : 32;
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint8_t srank[256];
-  __shared__ Ring R;
-  __shared__ EncDesc D[kStages];
+  __shared__ EncRing R;
+  __shared__ EncDesc D[kEncStages];
   ring_init(R);
   __syncthreads();
   int rank_job = -1;
   bool skip = false;
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const RingPos&) {
+                                           const EncPos&, uint32_t) {
     if (j != rank_job) {  // uniform across the consumers
       consumer_sync();    // every warp is done with the previous ranks
       uint32_t distinct, rank;
@@ -832,6 +937,15 @@ __device__ __forceinline__ void raw_tile_body(const EncJob& J, uint64_t t0, uint
                                               const uint16_t* sin) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  if (len == kTileWords) {
+    uint32_t x[kStepsPerWarp][8];
+#pragma unroll
+    for (int s = 0; s < kStepsPerWarp; ++s)
+      load_unit(sin, (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords, x[s]);
+    const uint64_t r0 = t0 + static_cast<uint64_t>(warp) * kStepsPerWarp * kStepWords;
+    warp_store_run<8, 8, kStepsPerWarp>(J.dst + 1 + 2 * r0, x, lane);
+    return;
+  }
 #pragma unroll
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t sb = (warp * kStepsPerWarp + s) * kStepWords;
@@ -861,8 +975,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint32_t stbl[512];
   __shared__ uint8_t srank[256];
-  __shared__ Ring R;
-  __shared__ EncDesc D[kStages];
+  __shared__ EncRing R;
+  __shared__ EncDesc D[kEncStages];
   __shared__ uint32_t s_wtot[2][2][kWarps];
   __shared__ uint64_t s_prefix[2];
   const int tid = threadIdx.x;
@@ -872,7 +986,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   int kind = kAutoOverflow;
   uint64_t escapes = 0;
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const RingPos& p) {
+                                           const EncPos& p, uint32_t) {
     if (j != setup_job) {  // uniform across the consumers
       consumer_sync();     // every warp is done with the previous ranks/table
       uint32_t distinct, rank;
@@ -1150,10 +1264,10 @@ __device__ __forceinline__ uint32_t job_mode(const DecJob& J) {
 
 // Producer warp of DecodeKernel.
 template <int kMax, int kMode>
-__device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t* ring, Ring& R, DecDesc* D) {
+__device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t* ring, DecRing& R, DecDesc* D) {
   const int lane = threadIdx.x & 31;
   const Chunk c = cta_chunk(b.tile_start[b.jobs]);
-  RingPos p;
+  DecPos p;
   int ji = find_job<kMax>(b.tile_start, b.jobs, c.first);
   int mode_job = -1;
   uint32_t mode = 0;
@@ -1329,8 +1443,8 @@ template <int kMax, int kMode>
 __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_constant__ DecBatch<kMax> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) DecodeExtra X;
-  __shared__ __align__(16) DecDesc D[kStages];
-  __shared__ Ring R;
+  __shared__ __align__(16) DecDesc D[kDecStages];
+  __shared__ DecRing R;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
@@ -1343,7 +1457,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
   int book_job = -1, pair_job = -1;
   uint64_t job_count = 0;                                 // escape count of book_job's stream
   uint32_t bk0[4] = {0, 0, 0, 0}, bk1[4] = {0, 0, 0, 0};  // top16 codebooks of book_job
-  RingPos p;
+  DecPos p;
   for (;;) {
     consumer_wait(R, p, nullptr);
     const DecDesc& d = D[p.s];
