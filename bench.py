@@ -80,36 +80,81 @@ def cpu_model() -> str:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event reasons of the benchmark's GPUs, sampled every
+    10 ms during the timed region through NVML (read-only queries); falls back
+    to `nvidia-smi -lms 100` where NVML cannot be loaded."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_indices):
-        self.gpus = set(gpu_indices)
-        self.rows = []
-        self.proc = None
+    def __init__(self, gpu_indices, period_s: float = 0.01):
+        self.gpus = list(gpu_indices)
+        self.period = period_s
+        self.rows = []  # (sm_mhz, util_pct, set of reasons)
+        self.max_mhz = None
+        self.stop_flag = threading.Event()
         self.thread = None
+        self.proc = None
 
     def start(self):
         try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.gpus]
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handles[0], pynvml.NVML_CLOCK_SM))
+            masks = [(name, getattr(pynvml, const)) for name, const in self.REASONS]
+        except Exception:  # no NVML: nvidia-smi
+            self._start_smi()
+            return
+
+        def poll():
+            while not self.stop_flag.is_set():
+                for h in handles:
+                    try:
+                        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                        util = float(pynvml.nvmlDeviceGetUtilizationRates(h).gpu)
+                        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    except Exception:
+                        continue
+                    self.rows.append((sm, util, {name for name, m in masks if bits & m}))
+                time.sleep(self.period)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+
+    def _start_smi(self):
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        names = [name for name, _ in self.REASONS]
+
+        def read():
+            for line in self.proc.stdout:
+                r = [x.strip() for x in line.split(",")]
+                if len(r) < 10 or not r[0].isdigit() or int(r[0]) not in self.gpus:
+                    continue
+                try:
+                    sm, util = float(r[1]), float(r[4])
+                    self.max_mhz = float(r[2])
+                except ValueError:
+                    continue
+                self.rows.append((sm, util, {n for n, v in zip(names, r[6:10]) if v.lower() == "active"}))
+
+        self.thread = threading.Thread(target=read, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 10:
-                self.rows.append(parts)
-
     def stop(self):
+        self.stop_flag.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -120,23 +165,14 @@ class ClockSampler:
             self.thread.join(timeout=5)
 
     def summary(self):
-        rows = [r for r in self.rows if r[0].isdigit() and int(r[0]) in self.gpus]
-        loaded = [r for r in rows if r[4].isdigit() and int(r[4]) >= 30] or rows
+        loaded = [r for r in self.rows if r[1] >= 30] or self.rows
         if not loaded:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
-        sm = [float(r[1]) for r in loaded if r[1].replace(".", "").isdigit()]
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"], "samples": 0}
         reasons = set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for r in loaded:
-            for name, value in zip(names, r[6:10]):
-                if value.strip().lower() == "active":
-                    reasons.add(name)
-        return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": float(loaded[0][2]) if loaded[0][2].replace(".", "").isdigit() else None,
-            "reasons": sorted(reasons),
-            "samples": len(loaded),
-        }
+            reasons |= r[2]
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(loaded)}
 
 
 # ------------------------------------------------------------- CPU oracle
@@ -201,6 +237,19 @@ def cpu_pipeline_gbs(cfg, layers: int, repeats: int = 3):
     sec = statistics.median(times)
     raw = 2 * n * layers
     return raw / sec / 1e9, threads, escapes / (n * layers), modes
+
+
+def ncu_traffic(workload: str, kernel: str):
+    """Per-launch DRAM bytes (read + write) of `kernel` on `workload` from the
+    ncu launch list summarised in profiles/dram_traffic.txt, or None."""
+    path = ROOT / "profiles" / "dram_traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 3 and not line.startswith("#") and parts[0] == workload and parts[1] == kernel:
+            return int(parts[2])
+    return None
 
 
 def reference_arm(args):
@@ -449,10 +498,7 @@ def b200_arm(args):
                          "gbs": round(alg[name] / (per * 1e-3) / 1e9, 1) if name in alg else None}
     dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
     dom = kernels[dominant]
-    traffic = None
-    tpath = ROOT / "profiles" / "ncu_traffic.json"
-    if tpath.exists():
-        traffic = json.loads(tpath.read_text()).get(args.workload, {}).get(dominant)
+    traffic = ncu_traffic(args.workload, dominant)
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": round(dom["gbs"] / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                 "alg_bytes_per_launch": dom["alg_bytes_per_launch"]}
