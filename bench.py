@@ -48,7 +48,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("c1", "c2"), default="c1")
+    p.add_argument("--workload", choices=("c1", "c2", "c3"), default="c1",
+                   help="c1: configs[1] (default); c2: configs[2] per-GPU TP shard; c3: configs[3] mixed batch")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -178,65 +179,82 @@ class ClockSampler:
 # ------------------------------------------------------------- CPU oracle
 
 
-def host_layer(cfg, layer, ids, scale_shift=1.0):
+def cpu_jobs(cfg, layers: int):
+    """Host sample of a workload for the CPU legs: (cache, src ids, dst ids,
+    544-byte tables) per call.  c1/c2: `layers` layers of the request;
+    c3: the first `4*layers` requests of layer 0."""
     from unchainkv_b200 import splitzip_cuda, workloads
 
-    cache = workloads.paged_cache_host(cfg, layer, ids, scale_shift)
-    tables = np.frombuffer(splitzip_cuda.build_top16_tables(workloads.layer_codebooks(layer, cfg.kv_heads, cfg.head_dim)),
-                           dtype=np.uint8).copy()
-    return cache, tables
+    def table(books):
+        return np.frombuffer(splitzip_cuda.build_top16_tables(books), dtype=np.uint8).copy()
+
+    if isinstance(cfg, workloads.MixedConfig):
+        cache, tabs, books = workloads.mixed_sample_host(cfg, 0, 4 * layers)
+        pool = cache.shape[1]
+        tabs2 = workloads.request_block_tables(pool, [len(t) for t in tabs], 3001)
+        t544 = table(books)
+        return [(cache, np.ascontiguousarray(a), np.ascontiguousarray(b), t544) for a, b in zip(tabs, tabs2)]
+    pool = cfg.blocks * cfg.pool_factor
+    ids = np.ascontiguousarray(workloads.block_table(pool, cfg.blocks, 3000))
+    ids2 = np.ascontiguousarray(workloads.block_table(pool, cfg.blocks, 3001))
+    return [(workloads.paged_cache_host(cfg, layer, ids), ids, ids2, table(workloads.shard_codebooks(cfg, layer)))
+            for layer in range(layers)]
 
 
 def cpu_pipeline_gbs(cfg, layers: int, repeats: int = 3):
     """The reference path on host cores: top16 attempt -> (overflow) fixed6
-    encode -> decode into a second cache, per layer, all host threads.
-    Returns (GB/s of raw KV, threads, escape rate, mode histogram)."""
+    encode -> decode into a second cache, per call, all host threads.
+    Returns (GB/s of raw KV, threads, escape rate, mode histogram, sample)."""
     from oracle import oracle
-    from unchainkv_b200 import workloads
 
     lib = oracle.lib()
     threads = oracle.max_threads()
-    pool = cfg.blocks * cfg.pool_factor
-    ids = np.ascontiguousarray(workloads.block_table(pool, cfg.blocks, 3000))
-    ids2 = np.ascontiguousarray(workloads.block_table(pool, cfg.blocks, 3001))
-    samples = [host_layer(cfg, layer, ids) for layer in range(layers)]
-    n = cfg.words_per_layer
+    jobs = cpu_jobs(cfg, layers)
     bw = cfg.block_words
-    ps = pool * bw
-    out = np.zeros(2 * n + 4096, dtype=np.uint8)
-    target = np.zeros((2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim), dtype=np.uint16)
+    largest = max(2 * len(ids) * bw for _, ids, _, _ in jobs)
+    out = np.zeros(2 * largest + 4096, dtype=np.uint8)
+    target = np.zeros_like(jobs[0][0])
     modes = {}
     escapes = 0
 
-    def run_layer(cache, tables):
-        nonlocal escapes
-        res = lib.orc_encode_top16_blocks_mt(cache.ctypes.data, ps, bw, bw, ids.ctypes.data, 0, cfg.blocks,
+    def run(cache, ids, ids2, tables):
+        blocks = len(ids)
+        n = 2 * blocks * bw
+        ps = cache.shape[1] * bw
+        res = lib.orc_encode_top16_blocks_mt(cache.ctypes.data, ps, bw, bw, ids.ctypes.data, 0, blocks,
                                              out.ctypes.data, out.size, tables.ctypes.data, threads)
         mode = int(out[0])
         if mode == 255:
-            res = lib.orc_encode_mode_blocks_mt(cache.ctypes.data, ps, bw, bw, ids.ctypes.data, 0, cfg.blocks,
+            res = lib.orc_encode_mode_blocks_mt(cache.ctypes.data, ps, bw, bw, ids.ctypes.data, 0, blocks,
                                                 out.ctypes.data, out.size, 6, threads)
             mode = int(out[0])
-            lib.orc_decode_fixed6_blocks_mt(out.ctypes.data, res, target.ctypes.data, n, cfg.blocks, bw, ps, bw,
+            lib.orc_decode_fixed6_blocks_mt(out.ctypes.data, res, target.ctypes.data, n, blocks, bw, ps, bw,
                                             0, ids2.ctypes.data, threads)
         else:
-            lib.orc_decode_top16_blocks_mt(out.ctypes.data, res, target.ctypes.data, n, cfg.blocks, bw, ps, bw,
+            lib.orc_decode_top16_blocks_mt(out.ctypes.data, res, target.ctypes.data, n, blocks, bw, ps, bw,
                                            0, ids2.ctypes.data, tables.ctypes.data, threads)
         return mode
 
-    for cache, tables in samples:  # warm-up + mode census
-        mode = run_layer(cache, tables)
+    words = 0
+    for cache, ids, ids2, tables in jobs:  # warm-up + mode census
+        mode = run(cache, ids, ids2, tables)
         modes[mode] = modes.get(mode, 0) + 1
         escapes += oracle.escape_count(cache[:, ids].reshape(-1), tables)
+        words += 2 * len(ids) * bw
     times = []
     for _ in range(repeats):
         t = time.perf_counter()
-        for cache, tables in samples:
-            run_layer(cache, tables)
+        for job in jobs:
+            run(*job)
         times.append(time.perf_counter() - t)
     sec = statistics.median(times)
-    raw = 2 * n * layers
-    return raw / sec / 1e9, threads, escapes / (n * layers), modes
+    from unchainkv_b200 import workloads
+
+    if isinstance(cfg, workloads.MixedConfig):
+        sample = f"first {len(jobs)} of {cfg.requests} requests of one layer, host numpy draw of the same distribution"
+    else:
+        sample = f"{len(jobs)} of {cfg.layers} layers, host numpy draw of the same distribution"
+    return 2 * words / sec / 1e9, threads, escapes / words, modes, sample
 
 
 def ncu_traffic(workload: str, kernel: str):
@@ -261,8 +279,8 @@ def reference_arm(args):
     from unchainkv_b200 import workloads
 
     cfg = workloads.CONFIGS[args.workload]
-    gbs, threads, esc, modes = cpu_pipeline_gbs(cfg, max(1, args.cpu_layers), repeats=max(1, args.steps))
-    sample = f"{args.cpu_layers} of {cfg.layers} layers per step ({cfg.tokens} tokens, {cfg.kv_heads}x{cfg.head_dim})"
+    gbs, threads, esc, modes, sample = cpu_pipeline_gbs(cfg, max(1, args.cpu_layers), repeats=max(1, args.steps))
+    sample += " per step"
     line = {
         "impl": "reference",
         "metric": "codec GB/s of raw bf16 KV per GPU (encode, decode) and % HBM peak; ratio",
@@ -276,8 +294,8 @@ def reference_arm(args):
         "vs_baseline": None,
         "dtype": "u16",
         "data": "synthetic (seeded numpy draw of the config distribution)",
-        "config": {"workload": cfg.name, "layers": cfg.layers, "tokens": cfg.tokens,
-                   "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens,
+        "config": {"workload": cfg.name, "layers": cfg.layers, "kv_heads": cfg.kv_heads,
+                   "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens,
                    "pipeline": "top16 attempt -> fixed6 fallback -> decode (host threads)"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample, "cpu": cpu_model(), "escape_rate": esc,
@@ -288,6 +306,66 @@ def reference_arm(args):
 
 
 # ------------------------------------------------------------------ B200
+
+
+def build_plan(cfg, L, device, rank):
+    """Device caches, per-layer tables and the encode/decode jobs of one step.
+    c1/c2: one request per layer; c3: many requests per layer sharing the
+    layer's paged pool.  Streams of all jobs sit in one transfer buffer at
+    16-byte aligned offsets."""
+    import torch
+
+    from unchainkv_b200 import splitzip_cuda as S
+    from unchainkv_b200 import workloads
+
+    mixed = isinstance(cfg, workloads.MixedConfig)
+    if mixed:
+        blocks = workloads.request_blocks(cfg, workloads.request_lengths(cfg))
+        pool = int(sum(blocks) * cfg.pool_factor)
+        src_ids = workloads.request_block_tables(pool, blocks, 3000)
+        dst_ids = workloads.request_block_tables(pool, blocks, 3001)
+    else:
+        blocks = [cfg.blocks]
+        pool = cfg.blocks * cfg.pool_factor
+        src_ids = [workloads.block_table(pool, cfg.blocks, 3000)]
+        dst_ids = [workloads.block_table(pool, cfg.blocks, 3001)]
+    shape = (L, 2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim)
+    src = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    dst = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+    # each rank codes its own shard: its own heads (TP) or its own request
+    if mixed:
+        books = b"".join(workloads.fill_pool_device(src[l], cfg, l, shard=rank) for l in range(L))
+    else:
+        books = b"".join(workloads.fill_layer_device(src[l], cfg, l, src_ids[0], shard=rank) for l in range(L))
+    tables = torch.tensor(
+        np.frombuffer(b"".join(S.build_top16_tables(books[l * 32:(l + 1) * 32]) for l in range(L)), np.uint8)
+        .reshape(L, 544).copy(), device=device)
+    src_t = [torch.as_tensor(x, device=device) for x in src_ids]
+    dst_t = [torch.as_tensor(x, device=device) for x in dst_ids]
+    jobs = []  # (layer, request, n, offset, capacity)
+    offset = 0
+    for l in range(L):
+        for r, nb in enumerate(blocks):
+            n = 2 * nb * cfg.block_words
+            cap = (S.auto_capacity(n) + 15) // 16 * 16
+            jobs.append((l, r, n, offset, cap))
+            offset += cap
+    streams = torch.zeros(offset, dtype=torch.uint8, device=device)
+    enc = S.job_array([S.make_job(src[l], src_t[r], streams[o:o + c], c, tables[l]) for l, r, n, o, c in jobs])
+    dec = S.job_array([S.make_job(dst[l], dst_t[r], streams[o:o + c], c, tables[l]) for l, r, n, o, c in jobs])
+    all_src = torch.cat(src_t)
+    return {"src": src, "dst": dst, "tables": tables, "jobs": jobs, "streams": streams, "enc": enc,
+            "dec": dec, "src_t": src_t, "dst_t": dst_t, "all_src": all_src, "pool": pool, "blocks": blocks,
+            "raw_bytes": 2 * sum(n for _, _, n, _, _ in jobs)}
+
+
+def check_round_trip(P, what):
+    import torch
+
+    for l in range(P["src"].shape[0]):
+        for s_ids, d_ids in zip(P["src_t"], P["dst_t"]):
+            if not torch.equal(P["dst"][l][:, d_ids].view(torch.int16), P["src"][l][:, s_ids].view(torch.int16)):
+                raise RuntimeError(f"{what}: layer {l} round trip differs")
 
 
 def b200_arm(args):
@@ -310,61 +388,43 @@ def b200_arm(args):
         raise RuntimeError(f"splitzip library missing: {S.load_error()}")
 
     cfg = workloads.CONFIGS[args.workload]
-    if args.layers:
-        import dataclasses
-
-        cfg = dataclasses.replace(cfg, layers=args.layers)
-    L = cfg.layers
-    pool = cfg.blocks * cfg.pool_factor
-    n = cfg.words_per_layer
-    ids = workloads.block_table(pool, cfg.blocks, 3000)
-    ids2 = workloads.block_table(pool, cfg.blocks, 3001)
-    shape = (L, 2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim)
-    src = torch.empty(shape, dtype=torch.bfloat16, device=device)
-    dst = torch.zeros(shape, dtype=torch.bfloat16, device=device)
-    books = b"".join(workloads.fill_layer_device(src[l], cfg, l, ids) for l in range(L))
-    tables = torch.tensor(
-        np.frombuffer(b"".join(S.build_top16_tables(books[l * 32:(l + 1) * 32]) for l in range(L)), np.uint8)
-        .reshape(L, 544).copy(), device=device)
-    ids_t = torch.as_tensor(ids, device=device)
-    ids2_t = torch.as_tensor(ids2, device=device)
-    cap = S.auto_capacity(n)
-    streams = torch.zeros((L, cap), dtype=torch.uint8, device=device)
-    enc = S.job_array([S.make_job(src[l], ids_t, streams[l], cap, tables[l]) for l in range(L)])
-    dec = S.job_array([S.make_job(dst[l], ids2_t, streams[l], cap, tables[l]) for l in range(L)])
+    mixed = isinstance(cfg, workloads.MixedConfig)
+    L = args.layers or cfg.layers
+    P = build_plan(cfg, L, device, rank)
+    jobs, streams, enc, dec = P["jobs"], P["streams"], P["enc"], P["dec"]
+    J = len(jobs)
     lib = S._load()
     stream = torch.cuda.current_stream(device)
     sp = stream.cuda_stream
-    raw_bytes = 2 * n * L
+    raw_bytes = P["raw_bytes"]
 
     def encode():
-        if lib.kvq_splitzip_bf16_encode_auto_batch(enc, L, sp) <= 0:
+        if lib.kvq_splitzip_bf16_encode_auto_batch(enc, J, sp) <= 0:
             raise RuntimeError("encode declined: " + lib.kvq_splitzip_last_error().decode())
 
     def decode():
-        if lib.kvq_splitzip_bf16_decode_auto_batch(dec, L, sp) <= 0:
+        if lib.kvq_splitzip_bf16_decode_auto_batch(dec, J, sp) <= 0:
             raise RuntimeError("decode declined: " + lib.kvq_splitzip_last_error().decode())
 
     def step():
         encode()
         decode()
 
-    # correctness of the timed configuration (bitwise, every layer)
+    # correctness of the timed configuration (bitwise, every job)
     step()
     torch.cuda.synchronize()
-    modes = streams[:, 0].cpu().tolist()
-    for l in range(L):
-        if not torch.equal(dst[l][:, ids2_t].view(torch.int16), src[l][:, ids_t].view(torch.int16)):
-            raise RuntimeError(f"layer {l}: round trip differs")
-    sizes = [S.stream_bytes(m, n) for m in modes]
+    offsets = torch.tensor([o for _, _, _, o, _ in jobs], device=device)
+    modes = streams[offsets].cpu().tolist()
+    check_round_trip(P, "first step")
+    sizes = [S.stream_bytes(m, n) for m, (_, _, n, _, _) in zip(modes, jobs)]
     escapes = 0
+    words = 0
     for l in range(L):
-        t = tables[l]
-        w = src[l][:, ids_t].reshape(2, -1).view(torch.int16).to(torch.int32) & 0xFFFF
+        t = P["tables"][l]
+        w = P["src"][l][:, P["all_src"]].reshape(2, -1).view(torch.int16).to(torch.int32) & 0xFFFF
         e = (w >> 7) & 0xFF
-        esc_k = (t[:256][e[0].long()] == 255).sum()
-        esc_v = (t[256:512][e[1].long()] == 255).sum()
-        escapes += int(esc_k + esc_v)
+        escapes += int((t[:256][e[0].long()] == 255).sum() + (t[256:512][e[1].long()] == 255).sum())
+        words += w.numel()
     encoded_total = sum(s for s in sizes if s)
 
     def barrier():
@@ -385,16 +445,11 @@ def b200_arm(args):
         end.synchronize()
         ms = start.elapsed_time(end)
         barrier()
-        if world > 1:
-            t = torch.tensor([ms], device=device, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return workloads.max_over_ranks(ms)
 
     sampler = ClockSampler(range(world)) if rank == 0 else None
     if sampler:
         sampler.start()
-        time.sleep(0.5)
     ms_step = timed(step, args.steps) / args.steps
     if sampler:
         sampler.stop()
@@ -413,38 +468,40 @@ def b200_arm(args):
     # pinned host -> H2D into receive buffers -> decode
     e2e = None
     if not args.skip_e2e:
-        recv = torch.zeros((L, cap), dtype=torch.uint8, device=device)
-        host = torch.empty((L, cap), dtype=torch.uint8, pin_memory=True)
-        mode_host = torch.empty((L,), dtype=torch.uint8, pin_memory=True)
-        dec_recv = S.job_array([S.make_job(dst[l], ids2_t, recv[l], cap, tables[l]) for l in range(L)])
+        recv = torch.zeros_like(streams)
+        host = torch.empty(streams.numel(), dtype=torch.uint8, pin_memory=True)
+        mode_host = torch.empty((J,), dtype=torch.uint8, pin_memory=True)
+        dec_recv = S.job_array([S.make_job(P["dst"][l], P["dst_t"][r], recv[o:o + c], c, P["tables"][l])
+                                for l, r, n, o, c in jobs])
         d2h = torch.cuda.Stream(device)
         h2d = torch.cuda.Stream(device)
-        moved = {"h2d": 0, "d2h": 0}
+        moved = {}
 
         def e2e_step():
-            S.encode_auto_batch(enc)
-            mode_host.copy_(streams[:, 0], non_blocking=True)
+            encode()
+            mode_host.copy_(streams[offsets], non_blocking=True)
             torch.cuda.current_stream().synchronize()
-            lengths = [S.stream_bytes(int(m), n) for m in mode_host.tolist()]
+            lengths = [S.stream_bytes(int(m), n) for m, (_, _, n, _, _) in zip(mode_host.tolist(), jobs)]
             if any(x is None for x in lengths):
-                raise RuntimeError("a layer produced no stream (mode 255)")
+                raise RuntimeError("a job produced no stream (mode 255)")
             ready = torch.cuda.Event()
             ready.record(stream)
             d2h.wait_event(ready)
-            events = []
-            for l in range(L):
+            last = None
+            for (l, r, n, o, c), size in zip(jobs, lengths):
                 with torch.cuda.stream(d2h):
-                    host[l, : lengths[l]].copy_(streams[l, : lengths[l]], non_blocking=True)
+                    host[o:o + size].copy_(streams[o:o + size], non_blocking=True)
                     ev = torch.cuda.Event()
                     ev.record(d2h)
                 h2d.wait_event(ev)
                 with torch.cuda.stream(h2d):
-                    recv[l, : lengths[l]].copy_(host[l, : lengths[l]], non_blocking=True)
-                    events.append(torch.cuda.Event())
-                    events[-1].record(h2d)
-            stream.wait_event(events[-1])
-            S.decode_auto_batch(dec_recv)
-            moved["d2h"] = sum(lengths) + L
+                    recv[o:o + size].copy_(host[o:o + size], non_blocking=True)
+                    last = torch.cuda.Event()
+                    last.record(h2d)
+            stream.wait_event(last)
+            if lib.kvq_splitzip_bf16_decode_auto_batch(dec_recv, J, sp) <= 0:
+                raise RuntimeError("decode declined: " + lib.kvq_splitzip_last_error().decode())
+            moved["d2h"] = sum(lengths) + J
             moved["h2d"] = sum(lengths)
 
         for _ in range(2):
@@ -459,15 +516,9 @@ def b200_arm(args):
             e2e_step()
         end.record(stream)
         end.synchronize()
-        e2e_ms = start.elapsed_time(end) / args.e2e_steps
+        e2e_ms = workloads.max_over_ranks(start.elapsed_time(end) / args.e2e_steps)
         wall_ms = (time.perf_counter() - t0) * 1e3 / args.e2e_steps
-        if world > 1:
-            t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
-        for l in range(L):
-            if not torch.equal(dst[l][:, ids2_t].view(torch.int16), src[l][:, ids_t].view(torch.int16)):
-                raise RuntimeError(f"e2e layer {l}: round trip differs")
+        check_round_trip(P, "e2e")
         e2e = {"value": round(world * raw_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": moved["h2d"], "d2h_bytes_per_step": moved["d2h"],
                "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(wall_ms, 4),
@@ -481,37 +532,41 @@ def b200_arm(args):
         return
 
     peak, peak_kind = peaks()
-    # algorithmic bytes per launch of each kernel of a step
-    mode_bytes = [(m, s) for m, s in zip(modes, sizes)]
-    stream_total = sum(s for _, s in mode_bytes)
-    alg = {
-        "StatsKernel": 2 * n * L,
-        "EncodeAutoKernel": 2 * n * L + stream_total,
-        "DecodeAutoKernel": stream_total + 2 * n * L,
-        "ZeroKernel": 64 * L,
-    }
+    # algorithmic bytes per launch of each kernel of a step: raw words read
+    # (stats), raw read + stream written (encode), stream read + raw written
+    # (decode); a step's launches split a batch of more than 96 jobs
+    stream_total = encoded_total
+    launches = {name: l for name, (_, l) in prof.items()}
+    alg_step = {"StatsKernel": raw_bytes, "EncodeAutoKernel": raw_bytes + stream_total,
+                "DecodeAutoKernel": stream_total + raw_bytes, "ZeroKernel": 64 * J}
     kernels = {}
-    for name, (ms, launches) in prof.items():
-        per = ms / launches
-        kernels[name] = {"launches": launches, "ms_per_launch": round(per, 5),
-                         "alg_bytes_per_launch": alg.get(name),
-                         "gbs": round(alg[name] / (per * 1e-3) / 1e9, 1) if name in alg else None}
+    for name, (ms, nl) in prof.items():
+        per = ms / nl
+        per_launch = alg_step[name] * prof_steps / nl if name in alg_step else None
+        kernels[name] = {"launches": nl, "ms_per_launch": round(per, 5), "alg_bytes_per_launch": per_launch,
+                         "gbs": round(per_launch / (per * 1e-3) / 1e9, 1) if per_launch else None}
     dominant = max(prof.items(), key=lambda kv: kv[1][0])[0]
     dom = kernels[dominant]
     traffic = ncu_traffic(args.workload, dominant)
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": round(dom["gbs"] / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                 "alg_bytes_per_launch": dom["alg_bytes_per_launch"]}
-    launches_per_step = sum(l for _, l in prof.values()) / prof_steps
+    launches_per_step = sum(launches.values()) / prof_steps
 
     cpu = None
     if not args.no_cpu_baseline:
-        gbs, threads, esc, cmodes = cpu_pipeline_gbs(cfg, max(1, args.cpu_layers))
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{args.cpu_layers} of {cfg.layers} layers, host numpy draw of the same distribution",
+        gbs, threads, esc, cmodes, sample = cpu_pipeline_gbs(cfg, max(1, args.cpu_layers))
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
                "cpu": cpu_model(), "escape_rate": round(esc, 5)}
 
+    if mixed:
+        shape_cfg = {"requests": cfg.requests, "tokens_per_layer": int(sum(P["blocks"]) * cfg.block_tokens),
+                     "request_tokens": [cfg.min_tokens, cfg.max_tokens], "scale_shift": cfg.scale_shift,
+                     "model_layers": cfg.model_layers}
+    else:
+        shape_cfg = {"tokens": cfg.tokens}
     value = world * raw_bytes / (ms_step * 1e-3) / 1e9
+    alg_round_trip = sum(alg_step[k] for k in ("StatsKernel", "EncodeAutoKernel", "DecodeAutoKernel"))
     line = {
         "metric": "codec GB/s of raw bf16 KV per GPU (encode, decode) and % HBM peak; ratio",
         "value": round(value, 3),
@@ -526,20 +581,19 @@ def b200_arm(args):
         "dtype": "u16",
         "data": "synthetic (seeded device draw of the config distribution)",
         "config": {
-            "workload": cfg.name, "layers": L, "tokens": cfg.tokens, "kv_heads": cfg.kv_heads,
-            "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens, "pool_blocks": pool,
-            "raw_bytes_per_step": raw_bytes, "encoded_bytes_per_step": encoded_total,
-            "policy": "device-chosen codec per layer (top16 -> fixed6 -> raw)",
+            "workload": cfg.name, "layers": L, **shape_cfg, "kv_heads": cfg.kv_heads,
+            "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens, "pool_blocks": P["pool"],
+            "jobs_per_step": J, "raw_bytes_per_step": raw_bytes, "encoded_bytes_per_step": encoded_total,
+            "policy": "device-chosen codec per job (top16 -> fixed6 -> raw)",
             "l2": "inputs larger than L2 (raw KV per step 512 MiB+)",
             "parallelism": f"independent per-GPU shards x{world} (no collective)",
         },
         "encode_gbs_per_gpu": round(raw_bytes / (ms_enc * 1e-3) / 1e9, 2),
         "decode_gbs_per_gpu": round(raw_bytes / (ms_dec * 1e-3) / 1e9, 2),
         "ratio": round(raw_bytes / encoded_total, 4),
-        "escape_rate": round(escapes / (n * L), 5),
+        "escape_rate": round(escapes / words, 5),
         "modes": {str(m): modes.count(m) for m in sorted(set(modes))},
-        "hbm_frac_round_trip": round(sum(alg[k] for k in ("StatsKernel", "EncodeAutoKernel", "DecodeAutoKernel"))
-                                     / (ms_step * 1e-3) / 1e9 / peak, 4),
+        "hbm_frac_round_trip": round(alg_round_trip / (ms_step * 1e-3) / 1e9 / peak, 4),
         "roofline": roofline,
         "kernels": kernels,
         "gpu_launches": int(round(launches_per_step * args.steps)),

@@ -184,7 +184,7 @@ KVQ_API long long kvq_splitzip_bf16_decode_fixed6_batch(const kvq_splitzip_job* 
  * align16(2n+1) + scratch, else a fixed6 overflow stream (mode 255) for the
  * host to replace with raw.  The stream's length follows from byte 0
  * (5: 5+n+ceil(n/2)+5*ceil(n/200); 3: 65+n+3*ceil(n/4); 6: 2n+1).
- * Scratch: 64 + 8*ceil(tiles/32) + 4*tiles bytes (tiles = ceil(n/8192)) at
+ * Scratch: 64 + align16(8*ceil(tiles/32)) + 16*tiles bytes (tiles = ceil(n/8192)) at
  * the 16-byte aligned end of the largest form.  Returns the sum over jobs of
  * the largest form each job may produce. */
 KVQ_API long long kvq_splitzip_bf16_encode_auto_batch(const kvq_splitzip_job* jobs,

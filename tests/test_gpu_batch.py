@@ -297,3 +297,55 @@ def test_auto_round_trip_at_every_stream_alignment():
         cache, ids, _ = sources[kind]
         got = to_u16(out)
         assert np.array_equal(got[:, ids], cache[:, ids]), (kind, off)
+
+
+def test_mixed_context_batch_like_config3():
+    """configs[3] in small: many requests of one layer with log-uniform
+    lengths (whole blocks, partial tails holding stale values) in one shared
+    pool, values shifted so ~5% of exponents escape the palette.  Every job's
+    stream equals the reference chain's result (top16 overflows -> fixed6),
+    and the batch round-trips into a second pool."""
+    from unchainkv_b200 import workloads as W
+
+    cfg = W.MixedConfig("c3_small", layers=1, model_layers=1, requests=20, min_tokens=16, max_tokens=2048,
+                        scale_shift=5.5, kv_heads=2)
+    blocks = W.request_blocks(cfg, W.request_lengths(cfg))
+    pool = sum(blocks) + 7
+    src_ids = W.request_block_tables(pool, blocks, 3000)
+    dst_ids = W.request_block_tables(pool, blocks, 3001)
+    scales = W.shard_scales(cfg, 0)
+    cache = W.draw_tokens(77, scales, pool * cfg.block_tokens, cfg.scale_shift)
+    cache = cache.reshape(2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim)
+    tab = np.frombuffer(S.build_top16_tables(W.top16_codebooks_from_words(W.draw_tokens(78, scales, 4096))),
+                        np.uint8).copy()
+    kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+    out = torch.zeros_like(kv)
+    tab_t = dev(tab)
+    keep, jobs, djobs, views, expect = [kv, out, tab_t], [], [], [], []
+    caps = [S.auto_capacity(2 * b * cfg.block_words) for b in blocks]
+    buf = torch.zeros(sum((c + 15) // 16 * 16 for c in caps), dtype=torch.uint8, device="cuda")
+    at = 0
+    for b, ids, ids2, cap in zip(blocks, src_ids, dst_ids, caps):
+        view = buf[at : at + cap]
+        at += (cap + 15) // 16 * 16
+        a, d = dev(ids), dev(ids2)
+        keep += [a, d]
+        jobs.append(job_for(kv, a, view, tab_t))
+        res, stream = oracle.encode_top16_blocks(cache, ids, tab)
+        if stream[0] == 255:
+            res, stream = oracle.encode_mode_blocks(cache, ids, bits=6)
+        expect.append(stream[:res])
+        djobs.append(job_for(out, d, view, tab_t, stream_bytes=res))
+        views.append(view)
+    escapes = sum(oracle.escape_count(cache[:, ids].reshape(-1), tab) for ids in src_ids)
+    words = sum(2 * b * cfg.block_words for b in blocks)
+    assert 0.03 < escapes / words < 0.08
+    assert S.encode_auto_batch(jobs)
+    torch.cuda.synchronize()
+    for i, (view, want) in enumerate(zip(views, expect)):
+        assert np.array_equal(view.cpu().numpy()[: want.size], want), i
+    assert S.decode_auto_batch(djobs)
+    torch.cuda.synchronize()
+    got = to_u16(out)
+    for ids, ids2 in zip(src_ids, dst_ids):
+        assert np.array_equal(got[:, ids2], cache[:, ids])

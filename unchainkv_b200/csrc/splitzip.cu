@@ -407,7 +407,19 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
   b.tile_start[count] = tiles;
   const char* name =
       kMode == 5 ? "DecodeTop16Kernel" : kMode == 3 ? "DecodeFixed6Kernel" : "DecodeAutoKernel";
-  return launch_persistent(DecodeKernel<kMax, kMode>, name, kDecSmemBytes, b, tiles, stream);
+  const long long rc = launch_persistent(DecodeKernel<kMax, kMode>, name, kDecSmemBytes, b, tiles, stream);
+  if constexpr (kMode == 3) {
+    return rc;
+  } else {
+    if (rc < 0) return rc;
+    // top16 streams whose entries the tiles could not all take (unsorted
+    // streams from other encoders) are finished by one CTA per job
+    const long long prof = prof_begin(stream);
+    RepairKernel<kMax, kMode><<<static_cast<unsigned>(count), kThreads, 0, stream>>>(b);
+    prof_end(prof, "RepairKernel", stream);
+    const cudaError_t st = cudaGetLastError();
+    return st == cudaSuccess ? 0 : Fail("RepairKernel", st);
+  }
 }
 
 template <int kMode>

@@ -473,23 +473,39 @@ __device__ __forceinline__ void warp_store_run(uint8_t* g, const uint32_t (&D)[K
 
 // Stage words [t0, t0+len) of a bulk-capable layout (base 16-byte aligned,
 // every run a multiple of 8 words at an 8-word aligned offset) into shared
-// memory, sin[j] = word t0+j, by the calling thread alone: one TMA bulk copy
-// per contiguous run with its bytes registered on `bar`; a ragged flat tail
-// of < 8 words by plain loads.  Does not arrive on `bar`.
+// memory, sin[j] = word t0+j, with the 32 lanes of one warp: lane k copies
+// the k-th contiguous run of the tile (k, k+32, ... for layouts with more
+// runs), so the block-table loads of all runs are in flight together.  Each
+// lane registers its own bytes on `bar`; a ragged flat tail of < 8 words
+// goes by lane 0's plain loads.  Does not arrive on `bar`.
 __device__ __forceinline__ void stage_words_tma(const uint16_t* __restrict__ base, const Layout& L, uint64_t t0,
                                                 uint32_t len, uint16_t* sin, uint64_t* bar) {
-  const uint32_t aligned_len = L.block_words == 0 ? (len & ~7u) : len;
-  uint64_t i = t0;
-  const uint64_t end = t0 + aligned_len;
-  while (i < end) {
-    uint64_t run = layout_run(L, i);
-    if (run > end - i) run = end - i;
-    const uint32_t bytes = static_cast<uint32_t>(run * 2);
-    mbar_expect_tx(bar, bytes);
-    bulk_g2s(sin + (i - t0), base + layout_addr(L, i), bytes, bar);
-    i += run;
+  const uint32_t lane = threadIdx.x & 31;
+  if (L.block_words == 0) {  // flat: one run
+    const uint32_t aligned_len = len & ~7u;
+    if (lane == 0) {
+      if (aligned_len) {
+        mbar_expect_tx(bar, aligned_len * 2);
+        bulk_g2s(sin, base + t0, aligned_len * 2, bar);
+      }
+      for (uint32_t j = aligned_len; j < len; ++j) sin[j] = base[t0 + j];
+    }
+    return;
   }
-  for (uint32_t j = aligned_len; j < len; ++j) sin[j] = base[t0 + j];
+  // runs are the intersections of the tile with cache blocks (the plane
+  // boundary is a block boundary)
+  const uint64_t bw = L.block_words;
+  const uint64_t first_block = t0 / bw;
+  const uint64_t end = t0 + len;
+  for (uint64_t k = lane;; k += 32) {
+    const uint64_t b0 = (first_block + k) * bw;
+    const uint64_t s0 = b0 > t0 ? b0 : t0;
+    if (s0 >= end) break;
+    const uint64_t e0 = b0 + bw < end ? b0 + bw : end;
+    const uint32_t bytes = static_cast<uint32_t>((e0 - s0) * 2);
+    mbar_expect_tx(bar, bytes);
+    bulk_g2s(sin + (s0 - t0), base + layout_addr(L, s0), bytes, bar);
+  }
 }
 
 // Stage words of any layout word by word with the 32 lanes of one warp.

@@ -35,10 +35,11 @@ constexpr uint32_t kDecCodesOffset = kTileWords + 128;  // top16/fixed6 codes in
 constexpr uint32_t kEncSmemBytes = kEncStages * kEncStageBytes;
 constexpr uint32_t kDecSmemBytes = kDecStages * kDecStageBytes;
 
+// Per-call decode state: escape entries the tiles of a top16 stream took
+// (compared with the stream's count by RepairKernel, which resets it).
 struct DecodeSlot {
-  unsigned int done;
   unsigned int covered;
-  unsigned int pad[2];
+  unsigned int pad[3];
 };
 
 // ------------------------------------------------------------------ jobs
@@ -110,9 +111,12 @@ __device__ __forceinline__ int find_job(const uint32_t* start, uint32_t jobs, ui
 // Tiles are visited in increasing order, so the job index only moves forward.
 template <int kMax>
 __device__ __forceinline__ int advance_job(const uint32_t* start, int j, uint32_t t) {
-  if (kMax == 1) return 0;
-  while (t >= start[j + 1]) ++j;
-  return j;
+  if constexpr (kMax == 1) {
+    return 0;
+  } else {
+    while (t >= start[j + 1]) ++j;
+    return j;
+  }
 }
 
 struct Chunk {
@@ -132,13 +136,17 @@ __device__ __forceinline__ Chunk cta_chunk(uint32_t total) {
 //     [16+8G, 16+8G+8T) tile status words (flag | escapes).
 //   fixed encode: [0,32) high-byte bitmap, [32,36) error flag.
 //   auto encode:  [0,4) escape total, [4,8) error flag, [16,48) bitmap,
-//     [64, 64+8G) group words, [64+8G, 64+8G+4T) tile escape counts.
+//     [64, 64+8G) group words (escapes of 32 tiles), then from the next
+//     16-byte boundary 16T bytes of escape counts per (tile, warp) as u16.
 __host__ __device__ constexpr uint64_t groups_for(uint64_t tiles) { return (tiles + 31) / 32; }
 __host__ __device__ constexpr uint64_t top16_scratch_bytes(uint64_t tiles) {
   return 16 + 8 * groups_for(tiles) + 8 * tiles;
 }
+__host__ __device__ constexpr uint64_t auto_counts_offset(uint64_t tiles) {
+  return 64 + (8 * groups_for(tiles) + 15) / 16 * 16;
+}
 __host__ __device__ constexpr uint64_t auto_scratch_bytes(uint64_t tiles) {
-  return 64 + 8 * groups_for(tiles) + 4 * tiles;
+  return auto_counts_offset(tiles) + 2 * kWarps * tiles;
 }
 constexpr uint64_t kFixedScratchBytes = 36;
 
@@ -264,25 +272,30 @@ using EncPos = RingPos<kEncStages>;
 using DecRing = Ring<kDecStages>;
 using DecPos = RingPos<kDecStages>;
 
-// Encode stage descriptor: global tile index (or kEndTile), its job and a
-// word the kernel's producer hook computed for it.
+// Encode stage descriptor: global tile index (or kEndTile), its job, and
+// what the kernel's producer hook computed for the tile.
 struct EncDesc {
   uint32_t tile;
   uint32_t job;
   uint32_t aux;
   uint32_t unused;
+  uint64_t prefix;        // auto top16: escapes of the job before this tile
+  uint64_t zero_lo;       // auto top16: this tile's share [zero_lo, zero_hi) of the
+  uint64_t zero_hi;       //   unused escape-slot bytes to clear
+  uint32_t wpre[kWarps];  // auto top16: escapes of the tile before each warp's run
 };
 
-// Producer hook that annotates nothing.
+// Producer hook (run by all 32 producer lanes once the tile is staged; lane
+// 0 writes the descriptor) that annotates nothing.
 struct NoAux {
   template <typename Job>
-  __device__ __forceinline__ uint32_t operator()(const Job&) const { return 0; }
+  __device__ __forceinline__ void operator()(const Job&, uint32_t, EncDesc&) const {}
 };
 
 // Producer warp of the encode kernels: stages the tiles next_tile() yields
 // (increasing; >= total ends) into the ring.  A bulk-capable layout takes one
-// TMA copy per contiguous run from lane 0; any other is gathered word by word
-// by the 32 lanes.
+// TMA copy per contiguous run, the runs spread over the 32 lanes; any other
+// is gathered word by word by the 32 lanes.
 template <int kMax, typename Next, typename Aux = NoAux>
 __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R, EncDesc* D,
                                                 Next&& next_tile, Aux aux = Aux()) {
@@ -306,13 +319,13 @@ __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t
     if (lane == 0) {
       D[p.s].tile = t;
       D[p.s].job = static_cast<uint32_t>(ji);
-      D[p.s].aux = aux(J);
     }
     if (J.bulk != 0) {
-      if (lane == 0) stage_words_tma(J.src, J.L, t0, len, sin, &R.full[p.s]);
+      stage_words_tma(J.src, J.L, t0, len, sin, &R.full[p.s]);
     } else {
       gather_words_warp(J.src, J.L, t0, len, sin);
     }
+    aux(J, t - b.tile_start[ji], D[p.s]);
     producer_commit(R, p);
     p.next();
   }
@@ -325,18 +338,18 @@ struct ChunkTiles {
 };
 
 // Consumer warps of the encode kernels: fn(job, job_index, tile, words,
-// ring position) for every staged tile until the end descriptor.
+// ring position, descriptor) for every staged tile until the end descriptor.
 template <int kMax, typename Fn>
 __device__ __forceinline__ void encode_consumer(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R,
                                                 const EncDesc* D, Fn&& fn) {
   EncPos p;
   for (;;) {
     consumer_wait(R, p, nullptr);
-    const EncDesc d = D[p.s];
+    const EncDesc& d = D[p.s];  // read in place; the stage is released after fn
     if (d.tile == kEndTile) return;
     const EncJob& J = b.job[d.job];
     fn(J, static_cast<int>(d.job), d.tile - b.tile_start[d.job],
-       reinterpret_cast<const uint16_t*>(ring + p.s * kEncStageBytes), p, d.aux);
+       reinterpret_cast<const uint16_t*>(ring + p.s * kEncStageBytes), p, d);
     consumer_release(R, p);
     p.next();
   }
@@ -378,11 +391,13 @@ __device__ __forceinline__ void top16_unit_codes(const uint32_t (&x)[8], const u
                                                  uint32_t& c1, uint32_t& esc) {
   uint32_t u[8];
   if (g >= half || g + kUnitWords <= half) {
-    const uint8_t* t = reinterpret_cast<const uint8_t*>(tbl + (g >= half ? 256 : 0));
+    // byte offset of a word's entry: exponent * 4, plus 1 KiB for plane 1
+    const uint32_t plane = g >= half ? 1024u : 0u;
+    const uint8_t* t = reinterpret_cast<const uint8_t*>(tbl);
 #pragma unroll
     for (int p = 0; p < 8; ++p)
-      u[p] = merge_pair(*reinterpret_cast<const uint32_t*>(t + ((x[p] >> 5) & 0x3FCu)),
-                        *reinterpret_cast<const uint32_t*>(t + ((x[p] >> 21) & 0x3FCu)));
+      u[p] = merge_pair(*reinterpret_cast<const uint32_t*>(t + (((x[p] >> 5) & 0x3FCu) | plane)),
+                        *reinterpret_cast<const uint32_t*>(t + (((x[p] >> 21) & 0x3FCu) | plane)));
   } else {
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
@@ -393,12 +408,13 @@ __device__ __forceinline__ void top16_unit_codes(const uint32_t (&x)[8], const u
   }
   c0 = __byte_perm(__byte_perm(u[0], u[1], 0x0040), __byte_perm(u[2], u[3], 0x0040), 0x5410);
   c1 = __byte_perm(__byte_perm(u[4], u[5], 0x0040), __byte_perm(u[6], u[7], 0x0040), 0x5410);
-  const uint32_t any = (u[0] | u[1] | u[2] | u[3] | u[4] | u[5] | u[6] | u[7]) & 0x30000u;
-  esc = 0;
-  if (any) {
-#pragma unroll
-    for (int p = 0; p < 8; ++p) esc |= ((u[p] >> 16) & 3u) << (2 * p);
-  }
+  // escape flags (bits 16-17 of each u[p]) -> bits 2p, 2p+1, branch-free:
+  // gather byte 2 of every u[p], then pack the 2-bit fields of 4 bytes
+  const uint32_t f0 = __byte_perm(__byte_perm(u[0], u[1], 0x0062), __byte_perm(u[2], u[3], 0x0062), 0x5410);
+  const uint32_t f1 = __byte_perm(__byte_perm(u[4], u[5], 0x0062), __byte_perm(u[6], u[7], 0x0062), 0x5410);
+  const uint32_t a0 = f0 | (f0 >> 6);  // pairs 0,1 at bits 0-3; pairs 2,3 at bits 16-19
+  const uint32_t a1 = f1 | (f1 >> 6);
+  esc = (a0 & 0xFu) | ((a0 >> 12) & 0xF0u) | ((a1 & 0xFu) << 8) | ((a1 >> 4) & 0xF000u);
 }
 
 // Body + codes of one tile; returns this lane's escape masks per step.
@@ -503,6 +519,25 @@ __device__ __forceinline__ uint32_t escape_offsets(const uint32_t (&masks)[kStep
   off[0] = before + (excl & 0xFFFFu);
   off[1] = before + s_wtot[0][warp] + (excl >> 16);
   return total;
+}
+
+// Offsets of this lane's escapes inside its warp's run (step 0's lanes,
+// then step 1's), from the per-step masks; no cross-warp exchange.
+__device__ __forceinline__ void warp_escape_offsets(const uint32_t (&masks)[kStepsPerWarp],
+                                                    uint32_t (&off)[kStepsPerWarp]) {
+  static_assert(kStepsPerWarp == 2, "two steps per warp");
+  const int lane = threadIdx.x & 31;
+  const uint32_t mine = __popc(masks[0]) | (__popc(masks[1]) << 16);
+  uint32_t incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const uint32_t excl = incl - mine;
+  const uint32_t total0 = __shfl_sync(kFull, incl, 31) & 0xFFFFu;
+  off[0] = excl & 0xFFFFu;
+  off[1] = total0 + (excl >> 16);
 }
 
 __device__ __forceinline__ void write_escapes(const EncJob& J, uint64_t t0, const uint16_t* sin,
@@ -618,7 +653,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeTop16Kernel(const __grid
   }
   int table_job = -1;
   encode_consumer<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos& p, uint32_t) {
+                                           const EncPos& p, const EncDesc&) {
     uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 4);
     if (j != table_job) {  // uniform across the consumers
       consumer_sync();     // every warp is done with the previous table
@@ -684,11 +719,13 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     if (tid < 64) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
   };
   // aux = 1 when the job's escapes already exceed its top16 capacity
-  auto over_cap = [](const EncJob& J) -> uint32_t {
-    return kStats && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap;
+  auto over_cap = [](const EncJob& J, uint32_t, EncDesc& d) {
+    const bool over = kStats && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap;
+    if ((threadIdx.x & 31) == 0) d.aux = over;
   };
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos&, uint32_t skip_escapes) {
+                                           const EncPos&, const EncDesc& desc) {
+    const uint32_t skip_escapes = desc.aux;
     if (j != pres_job || (kStats && j != table_job)) {  // uniform across the consumers
       consumer_sync();
       if (j != pres_job) {
@@ -744,8 +781,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
       escapes = warp_sum(escapes);
       if (lane == 0 && escapes) {
         uint64_t* groups = reinterpret_cast<uint64_t*>(J.scratch + 64);
-        uint32_t* counts = reinterpret_cast<uint32_t*>(groups + groups_for(J.tiles));
-        atomicAdd(&counts[tile], escapes);
+        uint16_t* counts = reinterpret_cast<uint16_t*>(J.scratch + auto_counts_offset(J.tiles));
+        counts[tile * kWarps + warp] = static_cast<uint16_t>(escapes);
         atomicAdd(reinterpret_cast<unsigned long long*>(&groups[tile >> 5]), static_cast<unsigned long long>(escapes));
         atomicAdd(reinterpret_cast<uint32_t*>(J.scratch), escapes);
       }
@@ -909,7 +946,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeFixedKernel(const __grid
   int rank_job = -1;
   bool skip = false;
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos&, uint32_t) {
+                                           const EncPos&, const EncDesc&) {
     if (j != rank_job) {  // uniform across the consumers
       consumer_sync();    // every warp is done with the previous ranks
       uint32_t distinct, rank;
@@ -977,16 +1014,62 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   __shared__ uint8_t srank[256];
   __shared__ EncRing R;
   __shared__ EncDesc D[kEncStages];
-  __shared__ uint32_t s_wtot[2][2][kWarps];
-  __shared__ uint64_t s_prefix[2];
   const int tid = threadIdx.x;
   ring_init(R);
   __syncthreads();
   int setup_job = -1;
   int kind = kAutoOverflow;
   uint64_t escapes = 0;
+  // top16 escape offsets from the stats pass, summed by the producer warp so
+  // that the consumers neither wait nor synchronise for them: the tile's
+  // offset (complete groups of 32 tiles before its group + the group's
+  // earlier tiles) and each warp's offset inside the tile
+  auto prefix_hook = [](const EncJob& J, uint32_t tile, EncDesc& d) {
+    const int lane = threadIdx.x & 31;
+    uint64_t prefix = 0;
+    uint32_t wpre = 0;
+    if (*reinterpret_cast<const uint32_t*>(J.scratch) <= J.cap) {
+      const uint64_t* groups = reinterpret_cast<const uint64_t*>(J.scratch + 64);
+      const uint16_t* counts = reinterpret_cast<const uint16_t*>(J.scratch + auto_counts_offset(J.tiles));
+      const uint32_t g = tile >> 5;
+      uint64_t v = 0;
+      if (lane < static_cast<int>(tile & 31)) {
+        const uint4 c = *reinterpret_cast<const uint4*>(counts + ((g << 5) + lane) * kWarps);
+        const uint32_t pairs = (c.x + c.y) + (c.z + c.w);  // two u16 sums per word, < 2^16 each
+        v = (pairs & 0xFFFFu) + (pairs >> 16);
+      }
+      prefix = warp_sum(v);
+      for (uint32_t base = 0; base < g; base += 32) {
+        v = base + lane < g ? (groups[base + lane] & 0xFFFFFFFFull) : 0;
+        prefix += warp_sum(v);
+      }
+      const uint32_t mine = lane < kWarps ? counts[tile * kWarps + lane] : 0u;
+      uint32_t incl = mine;
+#pragma unroll
+      for (int o = 1; o < kWarps; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+      }
+      wpre = incl - mine;
+    }
+    // this tile's share of the unused escape slots [escapes, cap) to zero
+    uint64_t zlo = 0, zhi = 0;
+    const uint64_t escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
+    if (lane == 0 && escapes < J.cap) {
+      const uint64_t lo = 5 * escapes, hi = 5 * J.cap;
+      const uint64_t share = (hi - lo + J.tiles - 1) / J.tiles;
+      zlo = min(hi, lo + share * tile);
+      zhi = min(hi, zlo + share);
+    }
+    if (lane == 0) {
+      d.prefix = prefix;
+      d.zero_lo = zlo;
+      d.zero_hi = zhi;
+    }
+    if (lane < kWarps) d.wpre[lane] = wpre;
+  };
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos& p, uint32_t) {
+                                           const EncPos& p, const EncDesc& desc) {
     if (j != setup_job) {  // uniform across the consumers
       consumer_sync();     // every warp is done with the previous ranks/table
       uint32_t distinct, rank;
@@ -1022,35 +1105,17 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
       raw_tile_body(J, t0, len, sin);
       return;
     }
-    // top16 with known per-tile offsets: prefix = complete groups before this
-    // tile's group + this group's earlier tiles (the stats pass finished).
-    if ((tid >> 5) == 0) {
-      const int lane = tid & 31;
-      const uint64_t* groups = reinterpret_cast<const uint64_t*>(J.scratch + 64);
-      const uint32_t* counts = reinterpret_cast<const uint32_t*>(groups + groups_for(J.tiles));
-      const uint32_t g = tile >> 5;
-      uint64_t v = lane < static_cast<int>(tile & 31) ? counts[(g << 5) + lane] : 0;
-      uint64_t prefix = warp_sum(v);
-      for (uint32_t base = 0; base < g; base += 32) {
-        v = base + lane < g ? (groups[base + lane] & 0xFFFFFFFFull) : 0;
-        prefix += warp_sum(v);
-      }
-      if (lane == 0) s_prefix[p.k & 1] = prefix;
-    }
-    {  // zero this tile's share of the unused escape slots [escapes, cap)
+    // top16: this tile's escapes start at desc.prefix (from the stats pass)
+    {  // zero this tile's share of the unused escape slots (from the producer)
       uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
-      const uint64_t lo = 5 * escapes, hi = 5 * J.cap;
-      const uint64_t share = (hi - lo + J.tiles - 1) / J.tiles;
-      const uint64_t a = lo + share * tile;
-      const uint64_t e = min(hi, a + share);
-      for (uint64_t i = a + tid; i < e; i += kThreads) entries[i] = 0;
+      for (uint64_t i = desc.zero_lo + tid; i < desc.zero_hi; i += kThreads) entries[i] = 0;
     }
     uint32_t masks[kStepsPerWarp];
     top16_tile_body(J, t0, len, sin, stbl, masks);
     uint32_t off[kStepsPerWarp];
-    escape_offsets(masks, s_wtot[p.k & 1], off);  // syncs: s_prefix visible after
-    write_escapes(J, t0, sin, masks, off, s_prefix[p.k & 1]);
-  });
+    warp_escape_offsets(masks, off);
+    write_escapes(J, t0, sin, masks, off, desc.prefix + desc.wpre[tid >> 5]);
+  }, prefix_hook);
 }
 
 // ------------------------------------------------------------------ decode
@@ -1179,48 +1244,103 @@ __device__ uint64_t escape_lower_bound(const uint8_t* entries, uint64_t count, u
   return lo + __popc(__ballot_sync(kFull, below));
 }
 
+// 128 consecutive escape entries held in the producer warp's registers:
+// entry base + 32*j + lane in slot j of each lane (position -2 past the end).
+struct EscWindow {
+  static constexpr int kPerLane = 4;
+  uint64_t base = ~0ull;
+  int64_t pos[kPerLane];
+  uint32_t exps[kPerLane];
+};
+
+// Issue the loads of the window at `base` (the registers are first read at
+// the next scan, so the loads stay in flight meanwhile).
+__device__ __forceinline__ void load_window(EscWindow& w, const uint8_t* entries, uint64_t count, uint64_t base) {
+  const int lane = threadIdx.x & 31;
+  w.base = base;
+#pragma unroll
+  for (int j = 0; j < EscWindow::kPerLane; ++j) {
+    const uint64_t idx = base + 32 * j + lane;
+    const bool exists = idx < count;
+    w.pos[j] = exists ? static_cast<int64_t>(entry_pos(entries, idx)) : -2;
+    w.exps[j] = exists ? __ldg(entries + idx * 5 + 4) : 0u;
+  }
+}
+
 // Producer warp: this tile's escapes into the descriptor (bitmap, ranks,
 // exponents in position order).  Entries are taken from `cursor` (the lower
 // bound of t0 when cursor_ok, else searched) while their positions fall in
-// the tile and strictly increase, up to kStageEscapes.  Returns the entries
-// taken; any other entry (out of position order, >= n, or past a tile's
-// capacity) is left to the job's last tile, which applies every entry when
-// the tiles did not take them all.  cursor_ok says whether the cursor ended
-// on the next tile's lower bound.
-__device__ uint32_t producer_escapes(const DecJob& J, uint64_t count, uint64_t t0, uint32_t len, DecDesc& d,
-                                     uint64_t& cursor, bool& cursor_ok) {
+// the tile and strictly increase, up to kStageEscapes.  They are read from
+// the register window `win`, which the previous tile prefetched at the
+// cursor; the window for the next tile is prefetched on return.  Returns the
+// entries taken; any other entry (out of position order, >= n, or past a
+// tile's capacity) is left to RepairKernel, which applies every entry of a
+// stream whose tiles did not take them all.  cursor_ok says whether the
+// cursor ended on the next tile's lower bound.
+__device__ __forceinline__ uint32_t producer_escapes(const DecJob& J, uint64_t count, uint64_t t0, uint32_t len,
+                                                     DecDesc& d, uint64_t& cursor, bool& cursor_ok,
+                                                     EscWindow& win) {
+  constexpr int kPerLane = EscWindow::kPerLane;
   const int lane = threadIdx.x & 31;
   const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
+  const int64_t lo = static_cast<int64_t>(t0), hi = static_cast<int64_t>(t0 + len);
 #pragma unroll
   for (int w = 0; w < static_cast<int>(kTileWords / 32 / 32); ++w) d.esc_bits[w * 32 + lane] = 0;
   if (!cursor_ok) cursor = escape_lower_bound(entries, count, t0);
+  if (win.base != cursor) load_window(win, entries, count, cursor);
   __syncwarp();
   uint32_t taken = 0;
   int64_t last = -1;
   bool clean = true;
   while (cursor < count) {
-    const uint64_t idx = cursor + lane;
-    const bool exists = idx < count;
-    const int64_t pos = exists ? static_cast<int64_t>(entry_pos(entries, idx)) : -2;
-    int64_t prev = __shfl_up_sync(kFull, pos, 1);
-    if (lane == 0) prev = last;
-    const bool ok = exists && pos >= static_cast<int64_t>(t0) && pos < static_cast<int64_t>(t0 + len) &&
-                    pos > prev && taken + lane < kStageEscapes;
-    const uint32_t bad = __ballot_sync(kFull, !ok);
-    const int take = bad ? __ffs(bad) - 1 : 32;
-    if (lane < take) {
-      const uint32_t local = static_cast<uint32_t>(pos - static_cast<int64_t>(t0));
-      atomicOr(&d.esc_bits[local >> 5], 1u << (local & 31));
-      d.esc_exp[taken + lane] = __ldg(entries + idx * 5 + 4);
+    // take = number of leading window entries that belong to this tile, in order
+    bool next_tile[kPerLane];  // entry opens a later tile in order (or there is none)
+    uint32_t bad[kPerLane];
+    int64_t group_last = last;
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const bool exists = win.base + 32 * j + lane < count;
+      const int64_t pos = win.pos[j];
+      int64_t prev = __shfl_up_sync(kFull, pos, 1);
+      if (lane == 0) prev = group_last;
+      const bool ok = exists && pos >= lo && pos < hi && pos > prev && taken + 32 * j + lane < kStageEscapes;
+      next_tile[j] = !exists || (pos >= hi && pos > prev);
+      bad[j] = __ballot_sync(kFull, !ok);
+      group_last = __shfl_sync(kFull, pos, 31);
     }
-    if (take > 0) last = __shfl_sync(kFull, pos, take - 1);
+    uint32_t take = 32 * kPerLane;
+    bool stop_clean = false;
+#pragma unroll
+    for (int j = kPerLane - 1; j >= 0; --j) {
+      if (bad[j]) {  // uniform; the lowest group with a bad entry wins
+        const int first = __ffs(bad[j]) - 1;
+        take = 32 * j + first;
+        stop_clean = __shfl_sync(kFull, next_tile[j], first);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const uint32_t k = 32 * j + lane;
+      if (k < take) {
+        const uint32_t local = static_cast<uint32_t>(win.pos[j] - lo);
+        atomicOr(&d.esc_bits[local >> 5], 1u << (local & 31));
+        d.esc_exp[taken + k] = static_cast<uint8_t>(win.exps[j]);
+      }
+    }
+    if (take > 0) {
+      const uint32_t j = (take - 1) >> 5;
+      int64_t v = win.pos[0];
+#pragma unroll
+      for (int i = 1; i < kPerLane; ++i) v = (static_cast<uint32_t>(i) == j) ? win.pos[i] : v;
+      last = __shfl_sync(kFull, v, static_cast<int>((take - 1) & 31));
+    }
     taken += take;
     cursor += take;
-    if (take < 32) {
-      // the entry that stopped the scan opens a later tile, or the scan ran out
-      clean = __shfl_sync(kFull, !exists || (pos >= static_cast<int64_t>(t0 + len) && pos > prev), take);
+    if (take < 32 * kPerLane) {
+      clean = stop_clean;
       break;
     }
+    load_window(win, entries, count, cursor);  // more than a window in this tile
   }
   cursor_ok = clean;
   __syncwarp();
@@ -1245,6 +1365,8 @@ __device__ uint32_t producer_escapes(const DecJob& J, uint64_t count, uint64_t t
     d.esc_rank[kPer * lane + w] = static_cast<uint16_t>(run);
     run += c[w];
   }
+  // prefetch the window of the next tile
+  if (cursor_ok && cursor < count && win.base != cursor) load_window(win, entries, count, cursor);
   return taken;
 }
 
@@ -1274,6 +1396,7 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
   uint64_t count = 0;
   uint64_t cursor = 0;
   bool cursor_ok = false;
+  EscWindow win;
   for (uint32_t t = c.first;; ++t) {
     producer_acquire(R, p, nullptr);
     DecDesc& d = D[p.s];
@@ -1288,6 +1411,7 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
       mode = job_mode<kMode>(N);
       count = mode == 5 ? min(static_cast<uint64_t>(load_u32le(N.src + 1)), N.cap) : 0;
       cursor_ok = false;
+      win.base = ~0ull;
       mode_job = ji;
     }
     const uint64_t t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
@@ -1300,22 +1424,21 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
       d.pad_x = pad.x;
       d.pad_y = pad.y;
     }
+    // destination of each 512-word step (its block-table load stays in
+    // flight across the escape scan; the result is stored last)
+    uint16_t* q = nullptr;
     if (lane < static_cast<int>(kStepsPerTile)) {
-      uint16_t* q = nullptr;
       const uint32_t sb = lane * kStepWords;
       if (mode != 0 && N.vec != 0 && sb + kStepWords <= len) {
         const uint64_t g = t0 + sb;
         if (layout_run(N.L, g) >= kStepWords) q = N.dst + layout_addr(N.L, g);
       }
-      d.step_dst[lane] = q;
     }
     if (mode == 5 && count > 0) {
-      const uint32_t covered = producer_escapes(N, count, t0, len, d, cursor, cursor_ok);
-      if (lane == 0 && covered) {
-        atomicAdd(&g_decode_slots[N.slot].covered, covered);
-        __threadfence();
-      }
+      const uint32_t covered = producer_escapes(N, count, t0, len, d, cursor, cursor_ok, win);
+      if (lane == 0 && covered) atomicAdd(&g_decode_slots[N.slot].covered, covered);
     }
+    if (lane < static_cast<int>(kStepsPerTile)) d.step_dst[lane] = q;
     producer_commit(R, p);
     p.next();
   }
@@ -1446,7 +1569,6 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
   __shared__ __align__(16) DecDesc D[kDecStages];
   __shared__ DecRing R;
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
   const int warp = tid >> 5;
   ring_init(R);
   __syncthreads();
@@ -1484,35 +1606,6 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
         const uint32_t hrel =
             J.half <= t0 ? 0u : static_cast<uint32_t>(min(J.half - t0, static_cast<uint64_t>(kTileWords)));
         decode_top16_compute(J, d, stage, t0, len, hrel, job_count > 0, bk0, bk1);
-        if (job_count > 0) {
-          // the job's last tile to finish applies every entry if the tiles
-          // did not take them all (out of position order, or >= n)
-          __threadfence();
-          consumer_sync();
-          if (warp == 0) {
-            uint32_t last = 0;
-            if (lane == 0) last = atomicAdd(&g_decode_slots[J.slot].done, 1u) == J.tiles - 1;
-            if (__shfl_sync(kFull, last, 0)) {
-              __threadfence();
-              const uint32_t covered = ld_volatile_u32(&g_decode_slots[J.slot].covered);
-              if (covered != job_count) {
-                const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
-                for (uint64_t i = lane; i < job_count; i += 32) {
-                  const uint32_t q = entry_pos(entries, i);
-                  if (q >= J.n) continue;
-                  uint16_t* w = J.dst + layout_addr(J.L, q);
-                  *w = static_cast<uint16_t>((__ldcg(w) & 0x807Fu) |
-                                             (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7));
-                }
-              }
-              __syncwarp();
-              if (lane == 0) {
-                g_decode_slots[J.slot].done = 0;
-                g_decode_slots[J.slot].covered = 0;
-              }
-            }
-          }
-        }
       } else if (mode == 3) {
         if (ji != pair_job) {
           consumer_sync();  // every warp is done with the previous table
@@ -1530,6 +1623,32 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
     }
     consumer_release(R, p);
     p.next();
+  }
+}
+
+// Runs after DecodeKernel in stream order, one CTA per job: a top16 stream
+// whose tiles did not take every escape entry (entries out of position
+// order, or at positions >= n) gets all its entries applied, in entry order
+// per thread; then the job's slot is reset for the next call.  Streams with
+// sorted entries (every stream this library writes) skip the work.
+template <int kMax, int kMode>
+__global__ void __launch_bounds__(kThreads) RepairKernel(const __grid_constant__ DecBatch<kMax> b) {
+  for (uint32_t j = blockIdx.x; j < b.jobs; j += gridDim.x) {
+    const DecJob& J = b.job[j];
+    if (job_mode<kMode>(J) != 5) continue;  // uniform across the CTA
+    const uint64_t count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
+    const uint32_t covered = ld_volatile_u32(&g_decode_slots[J.slot].covered);
+    if (covered != count) {
+      const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
+      for (uint64_t i = threadIdx.x; i < count; i += kThreads) {
+        const uint32_t q = entry_pos(entries, i);
+        if (q >= J.n) continue;
+        uint16_t* w = J.dst + layout_addr(J.L, q);
+        *w = static_cast<uint16_t>((*w & 0x807Fu) | (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7));
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) g_decode_slots[J.slot].covered = 0;
   }
 }
 

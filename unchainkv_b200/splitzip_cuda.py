@@ -547,7 +547,7 @@ def auto_capacity(n: int, raw: bool = True) -> int:
     """Stream-buffer bytes for encode_auto_batch: room for the largest form
     (raw mode 6 when ``raw``) plus the statistics scratch."""
     tiles = (n + 8191) // 8192
-    scratch = 64 + 8 * ((tiles + 31) // 32) + 4 * tiles
+    scratch = 64 + (8 * ((tiles + 31) // 32) + 15) // 16 * 16 + 16 * tiles
     largest = 1 + 2 * n if raw else max(top16_stream_bytes(n), fixed6_stream_bytes(n))
     return ((largest + 15) // 16) * 16 + scratch + 16
 
