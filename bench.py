@@ -383,6 +383,8 @@ def b200_arm(args):
     if world > 1:
         import datetime
 
+        # rank 0's stdout carries exactly one JSON line: keep NCCL's banner off it
+        os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     if not S.available():
         raise RuntimeError(f"splitzip library missing: {S.load_error()}")

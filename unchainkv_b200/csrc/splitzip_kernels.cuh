@@ -1020,51 +1020,73 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   int setup_job = -1;
   int kind = kAutoOverflow;
   uint64_t escapes = 0;
-  // top16 escape offsets from the stats pass, summed by the producer warp so
-  // that the consumers neither wait nor synchronise for them: the tile's
-  // offset (complete groups of 32 tiles before its group + the group's
-  // earlier tiles) and each warp's offset inside the tile
-  auto prefix_hook = [](const EncJob& J, uint32_t tile, EncDesc& d) {
+  // top16 escape offsets from the stats pass, prepared by the producer warp
+  // so that the consumers neither wait nor synchronise for them: the tile's
+  // offset in the job and each warp's offset inside the tile.  Job-level
+  // values are read once per job; consecutive tiles keep a running prefix
+  // and a register window of 32 tiles' per-warp counts (one load round per
+  // 32 tiles).  The tile's share of the unused escape slots to zero comes
+  // with it.
+  const EncJob* hook_job = nullptr;
+  uint32_t hook_next = 0, win_first = 0;
+  bool hook_top16 = false;
+  uint64_t running = 0, zlo0 = 0, zhi = 0, zshare = 0;
+  uint4 win = make_uint4(0, 0, 0, 0);
+  auto prefix_hook = [&](const EncJob& J, uint32_t tile, EncDesc& d) {
     const int lane = threadIdx.x & 31;
-    uint64_t prefix = 0;
+    const uint16_t* counts = reinterpret_cast<const uint16_t*>(J.scratch + auto_counts_offset(J.tiles));
+    auto load_win = [&](uint32_t first) {
+      win_first = first;
+      const uint32_t t = first + lane;
+      win = t < J.tiles ? *reinterpret_cast<const uint4*>(counts + static_cast<uint64_t>(t) * kWarps)
+                        : make_uint4(0, 0, 0, 0);
+    };
+    if (&J != hook_job || tile != hook_next) {
+      hook_job = &J;
+      const uint64_t escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
+      hook_top16 = escapes <= J.cap;
+      zlo0 = 5 * escapes;
+      zhi = 5 * J.cap;
+      zshare = zlo0 < zhi ? (zhi - zlo0 + J.tiles - 1) / J.tiles : 0;
+      running = 0;
+      if (hook_top16) {
+        const uint64_t* groups = reinterpret_cast<const uint64_t*>(J.scratch + 64);
+        const uint32_t g = tile >> 5;
+        uint64_t v = 0;
+        if (lane < static_cast<int>(tile & 31)) {
+          const uint4 c = *reinterpret_cast<const uint4*>(counts + ((g << 5) + lane) * kWarps);
+          const uint32_t pairs = (c.x + c.y) + (c.z + c.w);  // two u16 sums per word, each < 2^16
+          v = (pairs & 0xFFFFu) + (pairs >> 16);
+        }
+        running = warp_sum(v);
+        for (uint32_t base = 0; base < g; base += 32) {
+          v = base + lane < g ? (groups[base + lane] & 0xFFFFFFFFull) : 0;
+          running += warp_sum(v);
+        }
+        load_win(tile);
+      }
+    }
     uint32_t wpre = 0;
-    if (*reinterpret_cast<const uint32_t*>(J.scratch) <= J.cap) {
-      const uint64_t* groups = reinterpret_cast<const uint64_t*>(J.scratch + 64);
-      const uint16_t* counts = reinterpret_cast<const uint16_t*>(J.scratch + auto_counts_offset(J.tiles));
-      const uint32_t g = tile >> 5;
-      uint64_t v = 0;
-      if (lane < static_cast<int>(tile & 31)) {
-        const uint4 c = *reinterpret_cast<const uint4*>(counts + ((g << 5) + lane) * kWarps);
-        const uint32_t pairs = (c.x + c.y) + (c.z + c.w);  // two u16 sums per word, < 2^16 each
-        v = (pairs & 0xFFFFu) + (pairs >> 16);
-      }
-      prefix = warp_sum(v);
-      for (uint32_t base = 0; base < g; base += 32) {
-        v = base + lane < g ? (groups[base + lane] & 0xFFFFFFFFull) : 0;
-        prefix += warp_sum(v);
-      }
-      const uint32_t mine = lane < kWarps ? counts[tile * kWarps + lane] : 0u;
-      uint32_t incl = mine;
+    uint64_t prefix = running;
+    if (hook_top16) {
+      if (tile - win_first >= 32) load_win(tile);
+      const int k = static_cast<int>(tile - win_first);
+      const uint32_t c[4] = {__shfl_sync(kFull, win.x, k), __shfl_sync(kFull, win.y, k),
+                             __shfl_sync(kFull, win.z, k), __shfl_sync(kFull, win.w, k)};
+      uint32_t total = 0;
 #pragma unroll
-      for (int o = 1; o < kWarps; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += t;
+      for (int w = 0; w < kWarps; ++w) {
+        if (w == lane) wpre = total;
+        total += (c[w >> 1] >> (16 * (w & 1))) & 0xFFFFu;
       }
-      wpre = incl - mine;
+      running += total;
     }
-    // this tile's share of the unused escape slots [escapes, cap) to zero
-    uint64_t zlo = 0, zhi = 0;
-    const uint64_t escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
-    if (lane == 0 && escapes < J.cap) {
-      const uint64_t lo = 5 * escapes, hi = 5 * J.cap;
-      const uint64_t share = (hi - lo + J.tiles - 1) / J.tiles;
-      zlo = min(hi, lo + share * tile);
-      zhi = min(hi, zlo + share);
-    }
+    hook_next = tile + 1;
     if (lane == 0) {
       d.prefix = prefix;
-      d.zero_lo = zlo;
-      d.zero_hi = zhi;
+      const uint64_t a = min(zhi, zlo0 + zshare * tile);
+      d.zero_lo = a;
+      d.zero_hi = min(zhi, a + zshare);
     }
     if (lane < kWarps) d.wpre[lane] = wpre;
   };
