@@ -225,6 +225,42 @@ KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned long long src_
                                                          unsigned long long tables_ptr,
                                                          unsigned long long stream_ptr);
 
+/* ---- codec-aware decode attention (extension) ---------------------------
+ * The reference's receiver decodes each transfer stream into its paged cache
+ * and runs attention on the bf16 copy (scripts/bench_codec_attention.py:
+ * 155-157).  This attends over the streams directly.
+ *
+ * One request of a decode-attention batch: its transfer stream of one layer
+ * (the codec's output for the request's `blocks` paged blocks, K plane then
+ * V plane, of shape [16 tokens, 8 kv heads, 128 dims] per block: fixed6
+ * mode 3 or raw mode 6), the number of valid tokens (the last block may be
+ * partial), and its query and output, bf16 [8 * group][128] (q head
+ * kv_head * group + i attends with kv head kv_head). */
+typedef struct kvq_splitzip_attn_request {
+  unsigned long long stream_ptr;
+  unsigned long long stream_bytes;
+  unsigned long long blocks;
+  unsigned long long ctx_tokens;
+  unsigned long long q_ptr;
+  unsigned long long out_ptr;
+} kvq_splitzip_attn_request;
+
+/* Device workspace bytes kvq_splitzip_attention_decode needs for this batch
+ * on the current device (0 if the batch would be declined). */
+KVQ_API long long kvq_splitzip_attention_workspace_bytes(const kvq_splitzip_attn_request* reqs,
+                                                         unsigned long long count,
+                                                         unsigned long long group);
+
+/* out = softmax(q K^T / sqrt(128)) V for every q head of every request, K
+ * and V read from the streams, fp32 accumulation, bf16 output.  group: q
+ * heads per kv head, 1..16; count: 1..64 requests.  Returns count, 0 if
+ * declined (shape, sizes or workspace too small), -1 on a CUDA error.  A
+ * stream whose mode byte is not 3 or 6 yields zeros for its request and
+ * counts one device error. */
+KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_attn_request* reqs, unsigned long long count,
+                                                unsigned long long group, unsigned long long workspace_ptr,
+                                                unsigned long long workspace_bytes, unsigned long long stream_ptr);
+
 /* Kernel profiler (extension; the device-side analogue of the reference's
  * UNCHAIN_KV_TRACE_CUDA event pairs, src/unchain_kv/vllm_connector.py:
  * 3100-3124).  enable(1) clears the record and brackets every later kernel

@@ -16,7 +16,8 @@
 //     distinct high bytes in ascending order (zero padded), low-byte plane n
 //     bytes, 6-bit codes 4->3 bytes LE / 5-bit codes 8->5 bytes LE.
 //   raw (mode 6): [6] + the n words little endian.
-// Kernels are in splitzip_kernels.cuh.
+// Kernels are in splitzip_kernels.cuh (codec) and splitzip_attention.cuh
+// (decode attention over streams).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -27,6 +28,7 @@
 #include <string>
 #include <vector>
 
+#include "splitzip_attention.cuh"
 #include "splitzip_kernels.cuh"
 #include "unchain_kv_splitzip.h"
 
@@ -660,6 +662,107 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_split
                                                                  unsigned long long count,
                                                                  unsigned long long stream_ptr) {
   return decode_batch<0>(jobs, count, reinterpret_cast<cudaStream_t>(stream_ptr));
+}
+
+// ---------------------------------------------------------------- attention
+
+namespace {
+
+using AttnLaunch = AttnBatch<kAttnMaxReqs, kAttnMaxItems>;
+
+// The blocks of all requests, in order, split evenly over the resident CTAs
+// of the attention kernel; an item is one CTA's run of blocks of one
+// request.  The batch is declined when a request is malformed.
+bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint64_t group, AttnLaunch& b,
+                    uint64_t* workspace) {
+  if (reqs == nullptr || count == 0 || count > kAttnMaxReqs || group == 0 || group > kAttnMaxGroup) return false;
+  uint64_t total = 0;
+  for (uint64_t r = 0; r < count; ++r) {
+    const kvq_splitzip_attn_request& q = reqs[r];
+    if (q.stream_ptr == 0 || q.q_ptr == 0 || q.out_ptr == 0 || q.blocks == 0 || q.blocks > (1u << 24)) return false;
+    if (q.ctx_tokens == 0 || q.ctx_tokens > q.blocks * kAttnBlockTokens ||
+        q.ctx_tokens <= (q.blocks - 1) * kAttnBlockTokens)
+      return false;
+    if (q.q_ptr % 4 || q.out_ptr % 8) return false;
+    total += q.blocks;
+  }
+  unsigned grid = 0;
+  if (grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems>, kAttnSmemBytes, kAttnMaxCtas, &grid) < 0) return false;
+  const uint64_t ctas = std::min<uint64_t>(std::min<uint64_t>(grid, total), kAttnMaxCtas);
+  b = AttnLaunch{};
+  for (uint64_t r = 0; r < count; ++r) {
+    const kvq_splitzip_attn_request& q = reqs[r];
+    AttnReq& a = b.req[r];
+    a.stream = reinterpret_cast<const uint8_t*>(q.stream_ptr);
+    a.stream_bytes = q.stream_bytes;
+    a.n = 2 * q.blocks * kAttnBlockWords;
+    a.q = reinterpret_cast<const uint16_t*>(q.q_ptr);
+    a.out = reinterpret_cast<uint16_t*>(q.out_ptr);
+    a.ctx = static_cast<uint32_t>(q.ctx_tokens);
+  }
+  uint32_t items = 0;
+  uint64_t r = 0, req_first = 0;  // request holding global block `at`, and its first global block
+  for (uint64_t c = 0; c < ctas; ++c) {
+    b.cta_item[c] = static_cast<uint16_t>(items);
+    uint64_t at = total * c / ctas;
+    const uint64_t end = total * (c + 1) / ctas;
+    while (at < end) {
+      while (at >= req_first + reqs[r].blocks) req_first += reqs[r++].blocks;
+      const uint64_t stop = std::min<uint64_t>(end, req_first + reqs[r].blocks);
+      if (items >= kAttnMaxItems) return false;
+      b.item[items].req = static_cast<uint32_t>(r);
+      b.item[items].block0 = static_cast<uint32_t>(at - req_first);
+      b.item[items].blocks = static_cast<uint32_t>(stop - at);
+      if (b.req[r].items == 0) b.req[r].first_item = items;
+      ++b.req[r].items;
+      ++items;
+      at = stop;
+    }
+  }
+  b.cta_item[ctas] = static_cast<uint16_t>(items);
+  b.ctas = static_cast<uint32_t>(ctas);
+  b.reqs = static_cast<uint32_t>(count);
+  b.items = items;
+  b.group = static_cast<uint32_t>(group);
+  b.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kAttnHeadDim));
+  *workspace = 16 + static_cast<uint64_t>(items) * kAttnKvHeads * group * kAttnRecord * sizeof(float);
+  return true;
+}
+
+}  // namespace
+
+extern "C" KVQ_API long long kvq_splitzip_attention_workspace_bytes(const kvq_splitzip_attn_request* reqs,
+                                                                    unsigned long long count,
+                                                                    unsigned long long group) {
+  static thread_local AttnLaunch b;
+  uint64_t ws = 0;
+  return plan_attention(reqs, count, group, b, &ws) ? static_cast<long long>(ws) : 0;
+}
+
+extern "C" KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_attn_request* reqs,
+                                                           unsigned long long count, unsigned long long group,
+                                                           unsigned long long workspace_ptr,
+                                                           unsigned long long workspace_bytes,
+                                                           unsigned long long stream_ptr) {
+  static thread_local AttnLaunch b;
+  uint64_t ws = 0;
+  if (!plan_attention(reqs, count, group, b, &ws) || workspace_ptr == 0 || workspace_ptr % 16 ||
+      workspace_bytes < ws)
+    return 0;
+  const cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  b.partials = reinterpret_cast<float*>(workspace_ptr + 16);
+  long long prof = prof_begin(stream);
+  AttnKernel<kAttnMaxReqs, kAttnMaxItems><<<b.ctas, kCtaThreads, kAttnSmemBytes, stream>>>(b);
+  prof_end(prof, "AttnKernel", stream);
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return Fail("AttnKernel", st);
+  const uint64_t warps = static_cast<uint64_t>(b.reqs) * kAttnKvHeads * b.group;
+  prof = prof_begin(stream);
+  AttnCombineKernel<kAttnMaxReqs, kAttnMaxItems><<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(b);
+  prof_end(prof, "AttnCombineKernel", stream);
+  st = cudaGetLastError();
+  if (st != cudaSuccess) return Fail("AttnCombineKernel", st);
+  return static_cast<long long>(count);
 }
 
 extern "C" KVQ_API long long kvq_splitzip_device_errors() {

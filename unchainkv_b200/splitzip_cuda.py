@@ -95,6 +95,16 @@ class KvqJob(ctypes.Structure):
     ]
 
 
+class KvqAttnRequest(ctypes.Structure):
+    """``kvq_splitzip_attn_request`` of include/unchain_kv_splitzip.h: one
+    request of a decode-attention batch."""
+
+    _fields_ = [
+        (name, ctypes.c_ulonglong)
+        for name in ("stream_ptr", "stream_bytes", "blocks", "ctx_tokens", "q_ptr", "out_ptr")
+    ]
+
+
 def library_path() -> Path:
     """The in-tree build of the sm_100a library."""
     return Path(__file__).resolve().parent / "lib" / "libunchain_kv_splitzip_cuda.so"
@@ -129,6 +139,10 @@ def _load():
                 fn = getattr(lib, name)
                 fn.argtypes = [ctypes.POINTER(KvqJob), _U64, _U64] + ([extra] if extra else [])
                 fn.restype = ctypes.c_longlong
+            lib.kvq_splitzip_attention_workspace_bytes.argtypes = [ctypes.POINTER(KvqAttnRequest), _U64, _U64]
+            lib.kvq_splitzip_attention_workspace_bytes.restype = ctypes.c_longlong
+            lib.kvq_splitzip_attention_decode.argtypes = [ctypes.POINTER(KvqAttnRequest)] + [_U64] * 5
+            lib.kvq_splitzip_attention_decode.restype = ctypes.c_longlong
             lib.kvq_splitzip_last_error.argtypes = []
             lib.kvq_splitzip_last_error.restype = ctypes.c_char_p
             lib.kvq_splitzip_profile_enable.argtypes = [ctypes.c_int]
@@ -517,6 +531,65 @@ def device_errors() -> int:
     if value < 0:
         _raise_last(lib, "splitzip device error query failed")
     return int(value)
+
+
+# ------------------------------------------------------ decode attention
+
+ATTN_KV_HEADS = 8
+ATTN_HEAD_DIM = 128
+ATTN_BLOCK_TOKENS = 16
+
+
+def attention_requests(q, streams, ctx_tokens, out):
+    """The ``kvq_splitzip_attn_request`` array of a batch (see attention_decode)."""
+    reqs = (KvqAttnRequest * len(streams))()
+    for i, (stream, ctx) in enumerate(zip(streams, ctx_tokens)):
+        r = reqs[i]
+        r.stream_ptr = stream.data_ptr()
+        r.stream_bytes = stream.numel() * stream.element_size()
+        r.ctx_tokens = int(ctx)
+        r.blocks = (int(ctx) + ATTN_BLOCK_TOKENS - 1) // ATTN_BLOCK_TOKENS
+        r.q_ptr = q[i].data_ptr()
+        r.out_ptr = out[i].data_ptr()
+    return reqs
+
+
+def attention_decode(q, streams, ctx_tokens, out, workspace=None, stream=None) -> int | None:
+    """Decode attention straight over splitzip streams (extension: the
+    reference decodes each stream into its paged cache and attends over the
+    bf16 copy, scripts/bench_codec_attention.py:155-157).
+
+    ``q`` and ``out``: bf16 CUDA tensors [requests, 8 * group, 128] (q head
+    ``kv_head * group + i`` uses kv head ``kv_head``).  ``streams``: per
+    request a uint8 CUDA tensor holding that request's layer stream (fixed6
+    mode 3 or raw mode 6) of ceil(ctx/16) paged blocks of [16, 8, 128].
+    ``ctx_tokens``: valid tokens per request.  ``out[r, h]`` =
+    softmax(q[r, h] K^T / sqrt(128)) V, fp32 accumulation.  Returns the number
+    of requests, or None when the batch is declined."""
+    import torch
+
+    lib = _require_lib()
+    heads = q.shape[1]
+    if q.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or heads % ATTN_KV_HEADS:
+        return None
+    if not (q.is_contiguous() and out.is_contiguous()) or q.shape != out.shape or q.shape[2] != ATTN_HEAD_DIM:
+        return None
+    if len(streams) != q.shape[0] or len(ctx_tokens) != q.shape[0]:
+        return None
+    group = heads // ATTN_KV_HEADS
+    reqs = attention_requests(q, streams, ctx_tokens, out)
+    need = lib.kvq_splitzip_attention_workspace_bytes(reqs, len(streams), group)
+    if need <= 0:
+        return None
+    s = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        if stream is not None:  # keep it from the allocator until that stream is done
+            workspace.record_stream(torch.cuda.ExternalStream(stream, device=q.device))
+    res = lib.kvq_splitzip_attention_decode(reqs, len(streams), group, workspace.data_ptr(), workspace.numel(), s)
+    if res < 0:
+        _raise_last(lib, "splitzip attention failed")
+    return int(res) if res else None
 
 
 # --------------------------------------------------------------- batches
