@@ -60,13 +60,23 @@ def reference(q, words, ctx, group):
     return out.reshape(HEADS * group, DIM)
 
 
-def run(ctxs, modes, group=4, seed=0):
+def place(stream, aligned):
+    """Upload a stream at an address 15 mod 16 (planes on 16-byte
+    boundaries) or at a 16-byte aligned one (planes 1 byte past them)."""
+    if aligned:
+        buf = S.attention_stream_buffer(stream.size, "cuda")
+        buf.copy_(torch.from_numpy(stream.copy()))
+        return buf
+    return torch.from_numpy(stream.copy()).cuda()
+
+
+def run(ctxs, modes, group=4, seed=0, aligned=False):
     rng = np.random.Generator(np.random.PCG64(seed))
     reqs = [request(seed * 1000 + i, c, i % 4, m) for i, (c, m) in enumerate(zip(ctxs, modes))]
     q = W.bf16_bits(rng.standard_normal((len(ctxs), HEADS * group, DIM)).astype(np.float32))
     q_t = torch.from_numpy(q.view(np.int16)).cuda().view(torch.bfloat16)
     out = torch.full_like(q_t, float("nan"))
-    streams = [torch.from_numpy(s.copy()).cuda() for _, s in reqs]
+    streams = [place(s, aligned) for _, s in reqs]
     assert S.attention_decode(q_t, streams, ctxs, out) == len(ctxs)
     torch.cuda.synchronize()
     got = bf16_to_f32(out.view(torch.int16).cpu().numpy().view(np.uint16))
@@ -83,6 +93,12 @@ def test_fixed6_streams_ragged_contexts():
 
 def test_raw_and_fixed6_streams_in_one_batch():
     run([100, 1000, 64, 7], [6, 3, 6, 3], seed=1)
+
+
+@pytest.mark.parametrize("modes", [[3, 3, 3], [6, 3, 6]])
+def test_streams_placed_on_plane_boundaries(modes):
+    """Streams at addresses 15 mod 16 take the plain 16-byte load path."""
+    run([17, 513, 4096], modes, seed=5, aligned=True)
 
 
 def test_group_sizes():

@@ -113,7 +113,7 @@ std::mutex g_geometry_mu;
 std::map<GeometryKey, int> g_geometry;  // resident CTAs per device
 
 template <typename Kernel>
-long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* grid) {
+long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* grid, int threads = kCtaThreads) {
   int device = 0;
   cudaError_t st = cudaGetDevice(&device);
   if (st != cudaSuccess) return Fail("cudaGetDevice", st);
@@ -128,7 +128,7 @@ long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* gri
     st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn_smem));
     if (st != cudaSuccess) return Fail("cudaFuncSetAttribute", st);
     int per_sm = 0, sms = 0;
-    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kCtaThreads, dyn_smem);
+    st = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, dyn_smem);
     if (st != cudaSuccess) return Fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", st);
     st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
@@ -687,7 +687,8 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
     total += q.blocks;
   }
   unsigned grid = 0;
-  if (grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems>, kAttnSmemBytes, kAttnMaxCtas, &grid) < 0) return false;
+  if (grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems>, kAttnSmemBytes, kAttnMaxCtas, &grid, kAttnThreads) < 0)
+    return false;
   const uint64_t ctas = std::min<uint64_t>(std::min<uint64_t>(grid, total), kAttnMaxCtas);
   b = AttnLaunch{};
   for (uint64_t r = 0; r < count; ++r) {
@@ -725,7 +726,7 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
   b.items = items;
   b.group = static_cast<uint32_t>(group);
   b.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kAttnHeadDim));
-  *workspace = 16 + static_cast<uint64_t>(items) * kAttnKvHeads * group * kAttnRecord * sizeof(float);
+  *workspace = 16 + static_cast<uint64_t>(items) * 2 * kAttnKvHeads * group * kAttnRecord * sizeof(float);
   return true;
 }
 
@@ -752,7 +753,7 @@ extern "C" KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_at
   const cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   b.partials = reinterpret_cast<float*>(workspace_ptr + 16);
   long long prof = prof_begin(stream);
-  AttnKernel<kAttnMaxReqs, kAttnMaxItems><<<b.ctas, kCtaThreads, kAttnSmemBytes, stream>>>(b);
+  AttnKernel<kAttnMaxReqs, kAttnMaxItems><<<b.ctas, kAttnThreads, kAttnSmemBytes, stream>>>(b);
   prof_end(prof, "AttnKernel", stream);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return Fail("AttnKernel", st);

@@ -16,15 +16,19 @@
 //     8 heads x 128 dims), then the V plane block, into a ring of shared
 //     memory stages by TMA (the stream regions of that block's words: the
 //     low-byte plane and 6-bit codes for fixed6, the words for raw);
-//   - consumer warp h (kv head h): decodes its head's 16 x 128 slice into a
-//     swizzled bf16 tile in shared memory, loads tensor-core fragments with
-//     ldmatrix, S = Q K^T on m16n8k16 bf16 MMAs (the g q heads of the group
-//     as rows), online softmax in fp32 (base 2), O += P V on MMAs with P
-//     kept in registers as two bf16 parts (hi + lo);
-//   - the item's partial (m, l, O) per q head goes to a workspace and
-//     AttnCombineKernel merges the items of each request.
-// The QK/PV tiles have g useful rows (4 for the benchmark), so they run on
-// warp-level MMAs (16 rows); the kernel is bound by the HBM read of the
+//   - 16 consumer warps: warp (h, e) serves kv head h on the item's blocks
+//     of parity e, so two blocks are in work at a time.  It decodes its
+//     head's 16 x 128 slice of the block into a swizzled bf16 tile in shared
+//     memory, computes S^T = K Q^T (16 tokens x g q heads) on one m16n8k16
+//     bf16 MMA per 16 dims with K fragments from ldmatrix, keeps an online
+//     softmax per q head in fp32 (base 2), turns P^T into the PV operand in
+//     registers (movmatrix), and accumulates O^T += V^T P^T (128 dims x g)
+//     with V^T fragments from ldmatrix.trans; P is split into two bf16 parts
+//     (hi + lo) so that large V values do not amplify its rounding;
+//   - every (item, parity) writes a partial (m, l, O) per q head to a
+//     workspace and AttnCombineKernel merges them per request.
+// The tiles have g useful columns of 8 (g = 4 for the benchmark), so they
+// run on warp-level MMAs; the kernel is bound by the HBM read of the
 // compressed K/V.
 #pragma once
 
@@ -34,18 +38,21 @@ namespace ukv {
 
 constexpr int kAttnHeadDim = 128;
 constexpr int kAttnBlockTokens = 16;
-constexpr int kAttnKvHeads = kWarps;  // one consumer warp per kv head
+constexpr int kAttnKvHeads = kWarps;  // consumer warps of one block parity
+constexpr int kAttnConsumerWarps = 2 * kAttnKvHeads;  // (kv head, block parity)
+constexpr int kAttnConsumers = 32 * kAttnConsumerWarps;
+constexpr int kAttnThreads = kAttnConsumers + 32;     // + the producer warp
 constexpr uint32_t kAttnBlockWords = kAttnBlockTokens * kAttnKvHeads * kAttnHeadDim;  // per plane
 constexpr int kAttnStages = 4;
 constexpr uint32_t kAttnStageBytes = 2 * kAttnBlockWords + 64;  // raw words of one plane block + pads
 constexpr uint32_t kAttnCodesOffset = kAttnBlockWords + 32;     // fixed6 codes inside a stage
 constexpr uint32_t kAttnTileBytes = kAttnBlockTokens * kAttnHeadDim * 2;  // one warp's bf16 tile
 // dynamic shared memory: the ring stages, then one tile per consumer warp
-constexpr uint32_t kAttnSmemBytes = kAttnStages * kAttnStageBytes + kAttnKvHeads * kAttnTileBytes;
+constexpr uint32_t kAttnSmemBytes = kAttnStages * kAttnStageBytes + kAttnConsumerWarps * kAttnTileBytes;
 constexpr int kAttnMaxReqs = 64;
 constexpr int kAttnMaxItems = 1024;
 constexpr int kAttnMaxCtas = 320;
-constexpr int kAttnMaxGroup = 16;
+constexpr int kAttnMaxGroup = 8;
 constexpr uint32_t kAttnRecord = kAttnHeadDim + 4;  // floats per (item, q head): o, m, l, 2 pad (16-byte records)
 
 struct AttnReq {
@@ -73,7 +80,7 @@ struct AttnBatch {
   uint32_t items;
   uint32_t group;      // q heads per kv head
   float scale_log2;    // softmax scale * log2(e)
-  float* partials;     // [items][kv_heads * group][kAttnRecord] (o, then m, l)
+  float* partials;     // [items][2 parities][kv_heads * group][kAttnRecord] (o, then m, l)
   uint32_t ctas;
   uint16_t cta_item[kAttnMaxCtas + 1];  // items of CTA c: [cta_item[c], cta_item[c + 1])
   AttnReq req[kMaxR];
@@ -122,6 +129,18 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
                : "r"(smem_addr(p)));
 }
 
+// Transpose an 8x8 bf16 matrix held in MMA fragment layout across the warp.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+
+// Barrier of the attention kernel's consumer warps (named barrier 1).
+__device__ __forceinline__ void attn_consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kAttnConsumers) : "memory");
+}
+
 // A warp's 16-token x 128-dim bf16 tile: rows of 16 chunks of 16 bytes, chunk
 // c of row t stored at chunk c ^ (t & 7) (ldmatrix reads 8 rows of one logical
 // chunk without bank conflicts).
@@ -133,6 +152,7 @@ __device__ __forceinline__ uint8_t* tile_chunk(uint8_t* tile, uint32_t t, uint32
 // units of 16 words (token t = u / 8, dims 16 * (u % 8)), 4 per lane.
 __device__ __forceinline__ void attn_decode_tile(const AttnDesc& d, const uint8_t* stage, const uint8_t* pair,
                                                  uint8_t* tile, int head, int lane) {
+  const bool aligned = (d.pad_x | d.pad_y) == 0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const uint32_t u = lane + 32 * k;
@@ -141,9 +161,17 @@ __device__ __forceinline__ void attn_decode_tile(const AttnDesc& d, const uint8_
     uint32_t o[8];
     if (d.mode == 3) {
       uint32_t Lw[4];
-      smem_read16_window(stage, d.pad_x + w0, Lw);
-      uint32_t Q[3];
-      smem_read_words<3>(stage + kAttnCodesOffset, d.pad_y + 3 * w0 / 4, Q);
+      uint32_t Q[4];  // 12 code bytes
+      if (aligned) {  // uniform: the stream regions start on 16-byte boundaries
+        const uint4 l4 = *reinterpret_cast<const uint4*>(stage + w0);
+        Lw[0] = l4.x; Lw[1] = l4.y; Lw[2] = l4.z; Lw[3] = l4.w;
+        const uint32_t* c = reinterpret_cast<const uint32_t*>(stage + kAttnCodesOffset + 3 * w0 / 4);
+        Q[0] = c[0]; Q[1] = c[1]; Q[2] = c[2]; Q[3] = 0;
+      } else {
+        smem_read16_window(stage, d.pad_x + w0, Lw);
+        // 16-byte window reads keep each quarter warp on one row's banks
+        smem_read16_window(stage + kAttnCodesOffset, d.pad_y + 3 * w0 / 4, Q);
+      }
       uint32_t f[8];
       f[0] = (Q[0] << 2) & 0x3FFCu;
       f[1] = (Q[0] >> 10) & 0x3FFCu;
@@ -158,7 +186,14 @@ __device__ __forceinline__ void attn_decode_tile(const AttnDesc& d, const uint8_
         o[i] = __byte_perm(Lw[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140) |
                *reinterpret_cast<const uint32_t*>(pair + f[i]);
     } else if (d.mode == 6) {  // raw
-      smem_read_words<8>(stage, d.pad_x + 2 * w0, o);
+      if (aligned) {
+        const uint4* r = reinterpret_cast<const uint4*>(stage + 2 * w0);
+        const uint4 a = r[0], b2 = r[1];
+        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+        o[4] = b2.x; o[5] = b2.y; o[6] = b2.z; o[7] = b2.w;
+      } else {
+        smem_read_words<8>(stage, d.pad_x + 2 * w0, o);
+      }
     } else {  // a stream this kernel does not read: zeros (the producer raised an error)
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = 0u;
@@ -168,26 +203,28 @@ __device__ __forceinline__ void attn_decode_tile(const AttnDesc& d, const uint8_
   }
 }
 
+// 17 warps, one CTA per SM: a sub-partition hosting 5 of them allows 96
+// registers per thread.
 template <int kMaxR, int kMaxI>
-__global__ void __launch_bounds__(kCtaThreads, 1) AttnKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
+__global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint32_t pair[4096];
   __shared__ __align__(16) AttnDesc D[kAttnStages];
-  __shared__ AttnRing R;
+  __shared__ AttnRing R;  // empty barriers count the kWarps == kAttnKvHeads warps of one parity
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   ring_init(R);
   __syncthreads();
+  const uint32_t i_begin = blockIdx.x < b.ctas ? b.cta_item[blockIdx.x] : 0u;
+  const uint32_t i_end = blockIdx.x < b.ctas ? b.cta_item[blockIdx.x + 1] : 0u;
 
-  if (warp == kProducerWarp) {
+  if (warp == kAttnConsumerWarps) {
     // ------------------------------------------------------------ producer
     // K then V of each block of each item of this CTA; the mode byte and the
     // palette of the item's stream are read once per item
     AttnPos p;
-    const uint32_t i_end = blockIdx.x < b.ctas ? b.cta_item[blockIdx.x + 1] : 0u;
-    uint32_t item = blockIdx.x < b.ctas ? b.cta_item[blockIdx.x] : 0u;
-    for (; item < i_end; ++item) {
+    for (uint32_t item = i_begin; item < i_end; ++item) {
       const AttnItem& I = b.item[item];
       const AttnReq& Q = b.req[I.req];
       uint32_t mode = __ldg(Q.stream);
@@ -228,145 +265,150 @@ __global__ void __launch_bounds__(kCtaThreads, 1) AttnKernel(const __grid_consta
         p.next();
       }
     }
-    producer_acquire(R, p, nullptr);
-    if (lane == 0) D[p.s].item = kEndTile;
-    producer_commit(R, p);
     return;
   }
 
   // -------------------------------------------------------------- consumers
-  const int head = warp;
+  const int head = warp & (kAttnKvHeads - 1);
+  const uint32_t parity = static_cast<uint32_t>(warp >> 3);
   const uint32_t group = b.group;
-  const uint32_t row = lane >> 2;     // MMA row = q head of the group (rows >= group are zero)
-  const uint32_t quad = lane & 3;
-  uint8_t* tile = ring + kAttnStages * kAttnStageBytes + head * kAttnTileBytes;
+  const uint32_t gid = lane >> 2;  // MMA group: token gid (+8) of S^T, dim 16m + gid (+8) of O^T
+  const uint32_t tig = lane & 3;   // q heads 2*tig, 2*tig + 1 of the group (valid below `group`)
+  uint8_t* tile = ring + kAttnStages * kAttnStageBytes + warp * kAttnTileBytes;
   int pair_req = -1;
-  uint32_t cur = kEndTile;  // current item
-  uint32_t qa[8][2];        // Q fragments (a0, a2) per 16-dim step
-  float o[16][4];           // O accumulators per 8-dim step (c0, c1 = row; c2, c3 = row + 8, unused)
-  float m = -INFINITY, l = 0.f;
-  // P of the current block as A fragments, split in two bf16 parts
-  // (P = hi + lo, relative error ~2^-16) so that large V values do not
-  // amplify the rounding of P
-  uint32_t pa0 = 0, pa2 = 0, pb0 = 0, pb2 = 0;
-
-  auto flush = [&]() {
-    if (cur == kEndTile) return;
-    if (row < group) {
-      const uint32_t hq = head * group + row;
-      float* dst = b.partials + (static_cast<uint64_t>(cur) * (kAttnKvHeads * group) + hq) * kAttnRecord;
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        *reinterpret_cast<float2*>(dst + 8 * j + 2 * quad) = make_float2(o[j][0], o[j][1]);
-      if (quad == 0) {
-        dst[kAttnHeadDim] = m;
-        dst[kAttnHeadDim + 1] = l;
-      }
-    }
-  };
-
   AttnPos p;
-  for (;;) {
-    consumer_wait(R, p, nullptr);
-    const AttnDesc& d = D[p.s];
-    const uint32_t item = d.item;
-    if (item == kEndTile) break;
-    const int req = static_cast<int>(b.item[item].req);
-    if (item != cur) {  // uniform across the consumers
-      flush();
-      cur = item;
-      const uint16_t* qh = b.req[req].q + static_cast<uint64_t>(head * group + row) * kAttnHeadDim;
+  for (uint32_t item = i_begin; item < i_end; ++item) {
+    const AttnItem& I = b.item[item];
+    const int req = static_cast<int>(I.req);
+    // Q^T fragments (B operand of S^T = K Q^T): Q[q head gid][dims 16k + 2*tig (+8)]
+    uint32_t qb[8][2];
+    {
+      const uint16_t* qh = b.req[req].q + static_cast<uint64_t>(head * group + gid) * kAttnHeadDim;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        qa[k][0] = row < group ? *reinterpret_cast<const uint32_t*>(qh + 16 * k + 2 * quad) : 0u;
-        qa[k][1] = row < group ? *reinterpret_cast<const uint32_t*>(qh + 16 * k + 8 + 2 * quad) : 0u;
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-      m = -INFINITY;
-      l = 0.f;
-      if (d.mode == 3 && req != pair_req) {
-        consumer_sync();  // every warp is done with the previous table
-        for (int i = tid; i < 4096; i += kThreads)
-          pair[i] = (static_cast<uint32_t>(d.pal[i & 63]) << 8) | (static_cast<uint32_t>(d.pal[i >> 6]) << 24);
-        pair_req = req;
-        consumer_sync();
+        qb[k][0] = gid < group ? *reinterpret_cast<const uint32_t*>(qh + 16 * k + 2 * tig) : 0u;
+        qb[k][1] = gid < group ? *reinterpret_cast<const uint32_t*>(qh + 16 * k + 8 + 2 * tig) : 0u;
       }
     }
-    const uint8_t* stage = ring + p.s * kAttnStageBytes;
-    __syncwarp();  // the tile's previous contents were read by every lane
-    attn_decode_tile(d, stage, reinterpret_cast<const uint8_t*>(pair), tile, head, lane);
-    __syncwarp();
-    const uint32_t valid = d.valid;
-    if (d.plane == 0) {
-      // S = Q K^T over the block's 16 tokens: two n-tiles of 8 tokens
-      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    float o[8][4];  // O^T per 16 dims: (dim 16m+gid, head 2tig), (.., 2tig+1), (dim +8, 2tig), (dim +8, 2tig+1)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-#pragma unroll
-        for (int k = 0; k < 8; k += 2) {
-          // matrices: dims 16k, 16k+8, 16(k+1), 16(k+1)+8 of tokens 8j..8j+7
-          uint32_t r[4];
-          const uint32_t t = 8 * j + (lane & 7);
-          ldmatrix_x4(r, tile_chunk(tile, t, 2 * k + (lane >> 3)));
-          mma_bf16(s[j], qa[k][0], 0u, qa[k][1], 0u, r[0], r[1]);
-          mma_bf16(s[j], qa[k + 1][0], 0u, qa[k + 1][1], 0u, r[2], r[3]);
-        }
+    for (int m = 0; m < 8; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
+    float mx[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
+    uint32_t ph0 = 0, ph1 = 0, pl0 = 0, pl1 = 0;  // P^T as B fragments (hi, lo parts)
+    if (req != pair_req) {
+      // the request's fixed6 pair table, built by all consumers: every warp
+      // is past its stages of the previous item, then all read the palette
+      // from the item's first stage (waiting on it without releasing it: its
+      // parity-0 warps release it only after the second barrier)
+      attn_consumer_sync();
+      consumer_wait(R, p, nullptr);
+      const uint8_t* pal = D[p.s].pal;
+      for (int i = tid; i < 4096; i += kAttnConsumers)
+        pair[i] = (static_cast<uint32_t>(pal[i & 63]) << 8) | (static_cast<uint32_t>(pal[i >> 6]) << 24);
+      pair_req = req;
+      attn_consumer_sync();
+    }
+    for (uint32_t k = 0; k < 2 * I.blocks; ++k) {
+      if (((k >> 1) & 1u) != parity) {
+        p.next();
+        continue;
       }
-      // online softmax (base 2) of row `row` over tokens 8j + 2*quad + e
-      float x[4];
-      float bmax = -INFINITY;
+      consumer_wait(R, p, nullptr);
+      const AttnDesc& d = D[p.s];
+      const uint8_t* stage = ring + p.s * kAttnStageBytes;
+      const uint32_t valid = d.valid;
+      __syncwarp();  // the tile's previous contents were read by every lane
+      attn_decode_tile(d, stage, reinterpret_cast<const uint8_t*>(pair), tile, head, lane);
+      // the stage is decoded into the tile: hand it back to the producer now,
+      // so that it refills while this warp runs the MMAs and the softmax
+      consumer_release(R, p);
+      p.next();
+      __syncwarp();
+      if ((k & 1) == 0) {
+        // S^T = K Q^T: 16 tokens x 8 head slots, 8 steps of 16 dims
+        float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd steps
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+        for (int kk = 0; kk < 8; ++kk) {
+          // matrices: tokens 0-7 / 8-15 of dims 16kk..+7, then of dims 16kk+8..+15
+          uint32_t a[4];
+          ldmatrix_x4(a, tile_chunk(tile, (lane & 7) + ((lane >> 3) & 1) * 8, 2 * kk + (lane >> 4)));
+          mma_bf16((kk & 1) ? sd : sc, a[0], a[1], a[2], a[3], qb[kk][0], qb[kk][1]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[i] += sd[i];
+        // online softmax per q head (column) over tokens gid, gid + 8 of all lanes with this tig
+        float x[4];
+        x[0] = gid < valid ? sc[0] * b.scale_log2 : -INFINITY;
+        x[1] = gid < valid ? sc[1] * b.scale_log2 : -INFINITY;
+        x[2] = gid + 8 < valid ? sc[2] * b.scale_log2 : -INFINITY;
+        x[3] = gid + 8 < valid ? sc[3] * b.scale_log2 : -INFINITY;
+        float pe[4], alpha[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const uint32_t tok = 8 * j + 2 * quad + e;
-          const float v = tok < valid ? s[j][e] * b.scale_log2 : -INFINITY;
-          x[2 * j + e] = v;
-          bmax = fmaxf(bmax, v);
+          float bm = fmaxf(x[e], x[2 + e]);
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 4));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 8));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
+          const float m_new = fmaxf(mx[e], bm);
+          alpha[e] = exp2f(mx[e] - m_new);  // 0 on the first block (mx = -inf)
+          pe[e] = exp2f(x[e] - m_new);
+          pe[2 + e] = exp2f(x[2 + e] - m_new);
+          float bs = pe[e] + pe[2 + e];
+          bs += __shfl_xor_sync(kFull, bs, 4);
+          bs += __shfl_xor_sync(kFull, bs, 8);
+          bs += __shfl_xor_sync(kFull, bs, 16);
+          lsum[e] = lsum[e] * alpha[e] + bs;
+          mx[e] = m_new;
         }
-      bmax = fmaxf(bmax, __shfl_xor_sync(kFull, bmax, 1));
-      bmax = fmaxf(bmax, __shfl_xor_sync(kFull, bmax, 2));
-      const float m_new = fmaxf(m, bmax);
-      const float alpha = exp2f(m - m_new);  // 0 on the first block (m = -inf)
-      float pe[4];
-      float bsum = 0.f;
+        if (!__all_sync(kFull, alpha[0] == 1.f && alpha[1] == 1.f)) {  // a running max moved
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        pe[i] = exp2f(x[i] - m_new);
-        bsum += pe[i];
-      }
-      bsum += __shfl_xor_sync(kFull, bsum, 1);
-      bsum += __shfl_xor_sync(kFull, bsum, 2);
-      l = l * alpha + bsum;
-      m = m_new;
+          for (int m = 0; m < 8; ++m) {
+            o[m][0] *= alpha[0];
+            o[m][1] *= alpha[1];
+            o[m][2] *= alpha[0];
+            o[m][3] *= alpha[1];
+          }
+        }
+        // P^T rows (tokens gid, gid+8) x head pairs -> B fragments of V^T P^T
+        const uint32_t h0 = pack_bf16(pe[0], pe[1]), h1 = pack_bf16(pe[2], pe[3]);
+        const uint32_t l0 = pack_bf16(pe[0] - __uint_as_float(h0 << 16), pe[1] - __uint_as_float(h0 & 0xFFFF0000u));
+        const uint32_t l1 = pack_bf16(pe[2] - __uint_as_float(h1 << 16), pe[3] - __uint_as_float(h1 & 0xFFFF0000u));
+        ph0 = movmatrix_trans(h0);
+        ph1 = movmatrix_trans(h1);
+        pl0 = movmatrix_trans(l0);
+        pl1 = movmatrix_trans(l1);
+      } else {
+        // O^T += V^T P^T: 8 steps of 16 dims, k = the block's 16 tokens
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        o[j][0] *= alpha;
-        o[j][1] *= alpha;
-      }
-      pa0 = pack_bf16(pe[0], pe[1]);
-      pa2 = pack_bf16(pe[2], pe[3]);
-      pb0 = pack_bf16(pe[0] - __uint_as_float(pa0 << 16), pe[1] - __uint_as_float(pa0 & 0xFFFF0000u));
-      pb2 = pack_bf16(pe[2] - __uint_as_float(pa2 << 16), pe[3] - __uint_as_float(pa2 & 0xFFFF0000u));
-    } else {
-      // O += P V: 16 n-tiles of 8 dims, k = the block's 16 tokens
-#pragma unroll
-      for (int j = 0; j < 16; j += 2) {
-        // matrices: tokens 0-7 / 8-15 of dims 8j, then of dims 8(j+1)
-        uint32_t r[4];
-        const uint32_t t = (lane & 7) + ((lane >> 3) & 1) * 8;
-        ldmatrix_x4_trans(r, tile_chunk(tile, t, j + (lane >> 4)));
-        mma_bf16(o[j], pa0, 0u, pa2, 0u, r[0], r[1]);
-        mma_bf16(o[j], pb0, 0u, pb2, 0u, r[0], r[1]);
-        mma_bf16(o[j + 1], pa0, 0u, pa2, 0u, r[2], r[3]);
-        mma_bf16(o[j + 1], pb0, 0u, pb2, 0u, r[2], r[3]);
+        for (int m = 0; m < 8; ++m) {
+          // matrices: tokens 0-7 of dims 16m / 16m+8, then tokens 8-15 of dims 16m / 16m+8
+          uint32_t a[4];
+          ldmatrix_x4_trans(a, tile_chunk(tile, (lane & 7) + (lane >> 4) * 8, 2 * m + ((lane >> 3) & 1)));
+          mma_bf16(o[m], a[0], a[1], a[2], a[3], ph0, ph1);
+          mma_bf16(o[m], a[0], a[1], a[2], a[3], pl0, pl1);
+        }
       }
     }
-    consumer_release(R, p);
-    p.next();
+    // partial of (item, parity): O^T columns of the group's heads, m and l
+    const uint32_t heads = kAttnKvHeads * group;
+    float* base = b.partials + (static_cast<uint64_t>(item) * 2 + parity) * heads * kAttnRecord;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const uint32_t hcol = 2 * tig + e;
+      if (hcol < group) {
+        float* dst = base + static_cast<uint64_t>(head * group + hcol) * kAttnRecord;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          dst[16 * m + gid] = o[m][e];
+          dst[16 * m + gid + 8] = o[m][2 + e];
+        }
+        if (gid == 0) {
+          dst[kAttnHeadDim] = mx[e];
+          dst[kAttnHeadDim + 1] = lsum[e];
+        }
+      }
+    }
   }
-  flush();
 }
 
 // Merge the items of every request: out = sum_i 2^(m_i - M) o_i / sum_i 2^(m_i - M) l_i.
@@ -380,26 +422,34 @@ __global__ void __launch_bounds__(256) AttnCombineKernel(const __grid_constant__
   if (wid >= b.reqs * heads) return;
   const AttnReq& Q = b.req[wid / heads];
   const uint32_t hq = wid % heads;
+  // records of the request: (item, parity) pairs
   auto rec = [&](uint32_t i) {
-    return b.partials + (static_cast<uint64_t>(Q.first_item + i) * heads + hq) * kAttnRecord;
+    return b.partials + (static_cast<uint64_t>(2 * Q.first_item + i) * heads + hq) * kAttnRecord;
   };
+  const uint32_t records = 2 * Q.items;
   float M = -INFINITY;
-  for (uint32_t i = lane; i < Q.items; i += 32) M = fmaxf(M, rec(i)[kAttnHeadDim]);
+  for (uint32_t i = lane; i < records; i += 32) M = fmaxf(M, rec(i)[kAttnHeadDim]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, o));
   float L = 0.f;
-  for (uint32_t i = lane; i < Q.items; i += 32) L += exp2f(rec(i)[kAttnHeadDim] - M) * rec(i)[kAttnHeadDim + 1];
-  L = warp_sum(L);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (uint32_t i = 0; i < Q.items; ++i) {
-    const float* src = rec(i);
-    const float w = exp2f(src[kAttnHeadDim] - M);
-    const float4 v = *reinterpret_cast<const float4*>(src + 4 * lane);
-    acc[0] += w * v.x;
-    acc[1] += w * v.y;
-    acc[2] += w * v.z;
-    acc[3] += w * v.w;
+  for (uint32_t i0 = 0; i0 < records; i0 += 32) {
+    // weights of 32 records across the lanes, then their O rows accumulated
+    const uint32_t mine = i0 + lane;
+    const float w_l = mine < records ? exp2f(rec(mine)[kAttnHeadDim] - M) : 0.f;
+    L += mine < records ? w_l * rec(mine)[kAttnHeadDim + 1] : 0.f;
+    const uint32_t n = min(32u, records - i0);
+#pragma unroll 4
+    for (uint32_t j = 0; j < n; ++j) {
+      const float w = __shfl_sync(kFull, w_l, j);
+      const float4 v = *reinterpret_cast<const float4*>(rec(i0 + j) + 4 * lane);
+      acc[0] += w * v.x;
+      acc[1] += w * v.y;
+      acc[2] += w * v.z;
+      acc[3] += w * v.w;
+    }
   }
+  L = warp_sum(L);
   const float inv = 1.f / L;
   uint16_t* dst = Q.out + static_cast<uint64_t>(hq) * kAttnHeadDim + 4 * lane;
   *reinterpret_cast<uint2*>(dst) =

@@ -540,6 +540,17 @@ ATTN_HEAD_DIM = 128
 ATTN_BLOCK_TOKENS = 16
 
 
+def attention_stream_buffer(nbytes: int, device):
+    """A uint8 CUDA buffer of ``nbytes`` whose first byte sits at an address
+    15 mod 16: a fixed6 or raw stream placed there has its planes on 16-byte
+    boundaries, so attention_decode reads them with plain 16-byte loads."""
+    import torch
+
+    raw = torch.empty(nbytes + 32, dtype=torch.uint8, device=device)
+    start = (15 - raw.data_ptr()) % 16
+    return raw[start : start + nbytes]
+
+
 def attention_requests(q, streams, ctx_tokens, out):
     """The ``kvq_splitzip_attn_request`` array of a batch (see attention_decode)."""
     reqs = (KvqAttnRequest * len(streams))()
