@@ -48,8 +48,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("c1", "c2", "c3"), default="c1",
-                   help="c1: configs[1] (default); c2: configs[2] per-GPU TP shard; c3: configs[3] mixed batch")
+    p.add_argument("--workload", choices=("c1", "c2", "c3", "c4"), default="c1",
+                   help="c1: configs[1] (default); c2: configs[2] per-GPU TP shard; c3: configs[3] mixed batch; "
+                        "c4: configs[4] decode attention over compressed KV")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -279,6 +280,20 @@ def reference_arm(args):
     from unchainkv_b200 import workloads
 
     cfg = workloads.CONFIGS[args.workload]
+    if args.workload == "c4":
+        gbs, threads, sample = attention_cpu_gbs(cfg, repeats=max(1, args.steps))
+        print(json.dumps({
+            "impl": "reference",
+            "metric": "decode attention over compressed KV: GB/s of raw bf16 KV attended per GPU",
+            "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic (seeded numpy draw of the configs[0] distribution)",
+            "config": {"workload": cfg.name, "pipeline": "oracle fixed6 decode -> numpy fp32 attention"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample + " per step", "cpu": cpu_model()},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
     gbs, threads, esc, modes, sample = cpu_pipeline_gbs(cfg, max(1, args.cpu_layers), repeats=max(1, args.steps))
     sample += " per step"
     line = {
@@ -608,10 +623,258 @@ def b200_arm(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------- attention
+
+
+def attention_inputs(cfg, device, shard):
+    """per request a fixed6 stream of its one-layer K/V (device
+    draw of the configs[0] distribution, encoded by the library) placed on a
+    plane boundary, contexts and a bf16 N(0,1) query batch."""
+    import torch
+
+    from unchainkv_b200 import splitzip_cuda as S
+    from unchainkv_b200 import workloads as W
+
+    ctxs = W.attention_contexts(cfg)
+    zero_tables = torch.zeros(544, dtype=torch.uint8, device=device)
+    streams = []
+    for r, ctx in enumerate(ctxs):
+        blocks = -(-ctx // cfg.block_tokens)
+        scales = W.channel_scales(r % 32, cfg.kv_heads, cfg.head_dim)
+        kv = W.draw_tokens_device(2000 + r + 100000 * shard, scales, blocks * cfg.block_tokens, device)
+        kv = kv.view(2, blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim).contiguous()
+        n = kv.numel()
+        buf = torch.zeros(S.auto_capacity(n), dtype=torch.uint8, device=device)
+        job = S.make_job(kv, None, buf, None, zero_tables, block_start=0, block_count=blocks)
+        if not S.encode_bf16_batch([job], 6):
+            raise RuntimeError("fixed6 encode declined: " + S._load().kvq_splitzip_last_error().decode())
+        torch.cuda.synchronize()
+        if int(buf[0].item()) != 3:
+            raise RuntimeError("configs[4] data did not give a fixed6 stream")
+        size = S.stream_bytes(3, n)
+        stream = S.attention_stream_buffer(size, device)
+        stream.copy_(buf[:size])
+        streams.append(stream)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4005 + shard)
+    q = torch.randn((cfg.requests, cfg.kv_heads * cfg.group, cfg.head_dim), generator=gen, device=device)
+    return ctxs, streams, q.to(torch.bfloat16)
+
+
+def attention_check(cfg, ctxs, streams, q, out, r=0):
+    """Request r against fp32 attention over its stream decoded by the codec."""
+    import torch
+
+    from unchainkv_b200 import splitzip_cuda as S
+
+    blocks = -(-ctxs[r] // cfg.block_tokens)
+    kv = torch.zeros((2, blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim), dtype=torch.bfloat16,
+                     device=q.device)
+    job = S.make_job(kv, None, streams[r], streams[r].numel(), torch.zeros(544, dtype=torch.uint8, device=q.device),
+                     block_start=0, block_count=blocks)
+    if not S.decode_auto_batch([job]):
+        raise RuntimeError("reference decode declined")
+    k = kv[0].reshape(-1, cfg.kv_heads, cfg.head_dim)[: ctxs[r]].float()
+    v = kv[1].reshape(-1, cfg.kv_heads, cfg.head_dim)[: ctxs[r]].float()
+    qf = q[r].float().view(cfg.kv_heads, cfg.group, cfg.head_dim)
+    s = torch.einsum("hgd,thd->hgt", qf, k) / cfg.head_dim ** 0.5
+    ref = torch.einsum("hgt,thd->hgd", torch.softmax(s, dim=-1), v).reshape(-1, cfg.head_dim)
+    got = out[r].float()
+    bad = (got - ref).abs() > 1e-3 + 2e-2 * ref.abs()
+    if bool(bad.any()):
+        raise RuntimeError(f"attention differs from fp32 decompress-then-attend at {int(bad.sum())} values")
+
+
+def attention_cpu_gbs(cfg, requests: int = 2, repeats: int = 3):
+    """Decompress-then-attend on host cores: the CPU oracle decodes each
+    request's fixed6 stream, numpy attends in fp32.  Returns (GB/s of raw KV
+    attended, threads, sample)."""
+    from oracle import oracle
+    from unchainkv_b200 import workloads as W
+
+    ctxs = W.attention_contexts(cfg)[:requests]
+    jobs = []
+    for r, ctx in enumerate(ctxs):
+        blocks = -(-ctx // cfg.block_tokens)
+        words = W.draw_tokens(2000 + r, W.channel_scales(r % 32, cfg.kv_heads, cfg.head_dim), blocks * cfg.block_tokens)
+        res, stream = oracle.encode_mode(words.reshape(-1), bits=6)
+        jobs.append((ctx, blocks, stream[:res]))
+    rng = np.random.Generator(np.random.PCG64(4005))
+    q = rng.standard_normal((requests, cfg.kv_heads, cfg.group, cfg.head_dim)).astype(np.float32)
+    ids = None
+
+    def run():
+        for r, (ctx, blocks, stream) in enumerate(jobs):
+            cache = np.zeros((2, blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim), np.uint16)
+            oracle.decode_fixed6_blocks(stream, cache, np.arange(blocks, dtype=np.int64))
+            kv = (cache.astype(np.uint32) << 16).view(np.float32).reshape(2, -1, cfg.kv_heads, cfg.head_dim)[:, :ctx]
+            s = np.einsum("hgd,thd->hgt", q[r], kv[0]) / np.sqrt(cfg.head_dim)
+            s -= s.max(axis=-1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(axis=-1, keepdims=True)
+            np.einsum("hgt,thd->hgd", p, kv[1])
+
+    run()
+    times = []
+    for _ in range(repeats):
+        t = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t)
+    raw = sum(4 * ctx * cfg.kv_heads * cfg.head_dim for ctx, _, _ in jobs)
+    del ids
+    return raw / statistics.median(times) / 1e9, oracle.max_threads(), f"first {requests} of {cfg.requests} requests"
+
+
+def attention_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    from unchainkv_b200 import splitzip_cuda as S
+    from unchainkv_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        os.environ["NCCL_DEBUG"] = "WARN"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if not S.available():
+        raise RuntimeError(f"splitzip library missing: {S.load_error()}")
+    cfg = W.CONFIGS["c4"]
+    ctxs, streams, q = attention_inputs(cfg, device, rank)
+    out = torch.empty_like(q)
+    lib = S._load()
+    reqs = S.attention_requests(q, streams, ctxs, out)
+    ws = torch.empty(lib.kvq_splitzip_attention_workspace_bytes(reqs, len(ctxs), cfg.group), dtype=torch.uint8,
+                     device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        if S.attention_decode(q, streams, ctxs, out, workspace=ws) != len(ctxs):
+            raise RuntimeError("attention declined: " + lib.kvq_splitzip_last_error().decode())
+
+    step()
+    torch.cuda.synchronize()
+    attention_check(cfg, ctxs, streams, q, out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end)
+        barrier()
+        return W.max_over_ranks(ms)
+
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms_step = timed(step, args.steps) / args.steps
+    if sampler:
+        sampler.stop()
+    prof_steps = max(1, min(args.steps, 200))
+    S.profile_enable(True)
+    for _ in range(prof_steps):
+        step()
+    prof = S.profile_collect()
+    S.profile_enable(False)
+
+    e2e = None
+    if not args.skip_e2e:
+        q_host = q.cpu().pin_memory()
+        out_host = torch.empty_like(q_host).pin_memory()
+
+        def e2e_step():
+            q.copy_(q_host, non_blocking=True)
+            step()
+            out_host.copy_(out, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        e2e_ms = timed(e2e_step, args.e2e_steps) / args.e2e_steps
+        raw = sum(4 * c * cfg.kv_heads * cfg.head_dim for c in ctxs)
+        e2e = {"value": round(world * raw / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+               "ms_per_step": round(e2e_ms, 4), "path": "pinned q -> attention_decode -> pinned out"}
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = peaks()
+    raw = sum(4 * c * cfg.kv_heads * cfg.head_dim for c in ctxs)
+    stream_bytes = sum(x.numel() for x in streams)
+    qo = 2 * q.numel() * 2
+    alg = {"AttnKernel": stream_bytes + qo}
+    kernels = {}
+    for name, (ms, nl) in prof.items():
+        per = ms / nl
+        kernels[name] = {"launches": nl, "ms_per_launch": round(per, 5), "alg_bytes_per_launch": alg.get(name),
+                         "gbs": round(alg[name] / (per * 1e-3) / 1e9, 1) if name in alg else None}
+    dom = kernels["AttnKernel"]
+    roofline = {"bound": "hbm", "kernel": "AttnKernel", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": round(dom["gbs"] / peak, 4), "peak_kind": peak_kind,
+                "traffic": ncu_traffic(args.workload, "AttnKernel"), "alg_bytes_per_launch": dom["alg_bytes_per_launch"]}
+    cpu = None
+    if not args.no_cpu_baseline:
+        gbs, threads, sample = attention_cpu_gbs(cfg)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": sample + ", oracle fixed6 decode then numpy fp32 attention", "cpu": cpu_model()}
+    line = {
+        "metric": "decode attention over compressed KV: GB/s of raw bf16 KV attended per GPU",
+        "value": round(world * raw / (ms_step * 1e-3) / 1e9, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 (fp32 accumulation)",
+        "data": "synthetic (seeded device draw of the configs[0] distribution, fixed6 streams)",
+        "config": {"workload": cfg.name, "requests": cfg.requests, "q_heads": cfg.kv_heads * cfg.group,
+                   "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens,
+                   "context_tokens": [cfg.min_tokens, cfg.max_tokens], "tokens_per_step": sum(ctxs),
+                   "stream_bytes_per_step": stream_bytes, "raw_kv_bytes_per_step": raw,
+                   "l2": "compressed KV per step larger than L2",
+                   "parallelism": f"independent per-GPU batches x{world} (no collective)"},
+        "roofline": roofline,
+        "kernels": kernels,
+        "gpu_launches": int(round(sum(nl for _, nl in prof.values()) / prof_steps * args.steps)),
+        "clocks": sampler.summary() if sampler else None,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         reference_arm(args)
+    elif args.workload == "c4":
+        attention_arm(args)
     else:
         b200_arm(args)
 

@@ -98,6 +98,39 @@ CONFIG3 = MixedConfig("c3_mixed_context_64req_escape5", layers=8, model_layers=3
 CONFIGS = {"c0": CONFIG0, "c1": CONFIG1, "c2": CONFIG2, "c3": CONFIG3}
 
 
+@dataclass(frozen=True)
+class AttentionConfig:
+    """decode attention of `requests` queries (32 q
+    heads over 8 kv heads, head dim 128) over K/V held as fixed6 streams of
+    16-token paged blocks drawn from the configs[0] distribution, contexts
+    log-uniform in [min_tokens, max_tokens] (seed 4004)."""
+
+    name: str
+    requests: int = 32
+    min_tokens: int = 1024
+    max_tokens: int = 8192
+    group: int = 4
+    kv_heads: int = KV_HEADS
+    head_dim: int = HEAD_DIM
+    block_tokens: int = BLOCK_TOKENS
+    model_kv_heads: int = KV_HEADS
+    layers: int = 1
+
+    @property
+    def block_words(self) -> int:
+        return self.block_tokens * self.kv_heads * self.head_dim
+
+
+CONFIG4 = AttentionConfig("c4_codec_decode_attention_32req")
+CONFIGS["c4"] = CONFIG4
+
+
+def attention_contexts(cfg: AttentionConfig) -> list[int]:
+    rng = np.random.Generator(np.random.PCG64(4004))
+    lo, hi = np.log(cfg.min_tokens), np.log(cfg.max_tokens)
+    return [int(x) for x in np.floor(np.exp(rng.uniform(lo, hi, size=cfg.requests)))]
+
+
 def request_lengths(cfg: MixedConfig) -> np.ndarray:
     """Seeded log-uniform request lengths in tokens (seed 4000)."""
     rng = np.random.Generator(np.random.PCG64(4000))
