@@ -726,7 +726,7 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
   b.items = items;
   b.group = static_cast<uint32_t>(group);
   b.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kAttnHeadDim));
-  *workspace = 16 + static_cast<uint64_t>(items) * 2 * kAttnKvHeads * group * kAttnRecord * sizeof(float);
+  *workspace = 16 + static_cast<uint64_t>(items) * kAttnKvHeads * group * kAttnRecord * sizeof(float);
   return true;
 }
 

@@ -16,17 +16,19 @@
 //     8 heads x 128 dims), then the V plane block, into a ring of shared
 //     memory stages by TMA (the stream regions of that block's words: the
 //     low-byte plane and 6-bit codes for fixed6, the words for raw);
-//   - 16 consumer warps: warp (h, e) serves kv head h on the item's blocks
-//     of parity e, so two blocks are in work at a time.  It decodes its
-//     head's 16 x 128 slice of the block into a swizzled bf16 tile in shared
-//     memory, computes S^T = K Q^T (16 tokens x g q heads) on one m16n8k16
-//     bf16 MMA per 16 dims with K fragments from ldmatrix, keeps an online
-//     softmax per q head in fp32 (base 2), turns P^T into the PV operand in
-//     registers (movmatrix), and accumulates O^T += V^T P^T (128 dims x g)
-//     with V^T fragments from ldmatrix.trans; P is split into two bf16 parts
-//     (hi + lo) so that large V values do not amplify its rounding;
-//   - every (item, parity) writes a partial (m, l, O) per q head to a
-//     workspace and AttnCombineKernel merges them per request.
+//   - decoder warp h (kv head h): decodes its head's 16 x 128 slice of every
+//     staged plane block into a swizzled bf16 tile in shared memory (a K
+//     slot and a V slot per head) and releases the stage;
+//   - MMA warp h: computes S^T = K Q^T (16 tokens x g q heads) on one
+//     m16n8k16 bf16 MMA per 16 dims with K fragments from ldmatrix, keeps an
+//     online softmax per q head in fp32 (base 2), turns P^T into the PV
+//     operand in registers (movmatrix), and accumulates O^T += V^T P^T
+//     (128 dims x g) with V^T fragments from ldmatrix.trans; P is split into
+//     two bf16 parts (hi + lo) so that large V values do not amplify its
+//     rounding.  Decoder and MMA warp of a head hand the slots over with
+//     full/empty mbarriers, so decoding and MMAs overlap;
+//   - every item writes a partial (m, l, O) per q head to a workspace and
+//     AttnCombineKernel merges them per request.
 // The tiles have g useful columns of 8 (g = 4 for the benchmark), so they
 // run on warp-level MMAs; the kernel is bound by the HBM read of the
 // compressed K/V.
@@ -39,9 +41,10 @@ namespace ukv {
 constexpr int kAttnHeadDim = 128;
 constexpr int kAttnBlockTokens = 16;
 constexpr int kAttnKvHeads = kWarps;  // consumer warps of one block parity
-constexpr int kAttnConsumerWarps = 2 * kAttnKvHeads;  // (kv head, block parity)
+constexpr int kAttnConsumerWarps = 2 * kAttnKvHeads;  // a decoder and an MMA warp per kv head
 constexpr int kAttnConsumers = 32 * kAttnConsumerWarps;
 constexpr int kAttnThreads = kAttnConsumers + 32;     // + the producer warp
+constexpr int kAttnDecoders = 32 * kAttnKvHeads;      // threads of the decoder warps
 constexpr uint32_t kAttnBlockWords = kAttnBlockTokens * kAttnKvHeads * kAttnHeadDim;  // per plane
 constexpr int kAttnStages = 4;
 constexpr uint32_t kAttnStageBytes = 2 * kAttnBlockWords + 64;  // raw words of one plane block + pads
@@ -80,7 +83,7 @@ struct AttnBatch {
   uint32_t items;
   uint32_t group;      // q heads per kv head
   float scale_log2;    // softmax scale * log2(e)
-  float* partials;     // [items][2 parities][kv_heads * group][kAttnRecord] (o, then m, l)
+  float* partials;     // [items][kv_heads * group][kAttnRecord] (o, then m, l)
   uint32_t ctas;
   uint16_t cta_item[kAttnMaxCtas + 1];  // items of CTA c: [cta_item[c], cta_item[c + 1])
   AttnReq req[kMaxR];
@@ -136,10 +139,20 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return r;
 }
 
-// Barrier of the attention kernel's consumer warps (named barrier 1).
-__device__ __forceinline__ void attn_consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kAttnConsumers) : "memory");
+// Barrier of the attention kernel's decoder warps (named barrier 1).
+__device__ __forceinline__ void attn_decoder_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kAttnDecoders) : "memory");
 }
+
+// Tile hand-over between the decoder and the MMA warp of a head: slot 0
+// holds K tiles, slot 1 V tiles; full[slot] when decoded, empty[slot] when
+// the MMA warp is done with it.  `valid` carries the block's valid tokens.
+struct AttnHandoff {
+  uint64_t full[2];
+  uint64_t empty[2];
+  uint32_t valid[2];
+  uint32_t pad[2];
+};
 
 // A warp's 16-token x 128-dim bf16 tile: rows of 16 chunks of 16 bytes, chunk
 // c of row t stored at chunk c ^ (t & 7) (ldmatrix reads 8 rows of one logical
@@ -203,18 +216,24 @@ __device__ __forceinline__ void attn_decode_tile(const AttnDesc& d, const uint8_
   }
 }
 
-// 17 warps, one CTA per SM: a sub-partition hosting 5 of them allows 96
-// registers per thread.
 template <int kMaxR, int kMaxI>
 __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint32_t pair[4096];
   __shared__ __align__(16) AttnDesc D[kAttnStages];
-  __shared__ AttnRing R;  // empty barriers count the kWarps == kAttnKvHeads warps of one parity
+  __shared__ AttnRing R;  // empty barriers count the kWarps == kAttnKvHeads decoder warps
+  __shared__ __align__(8) AttnHandoff hand[kAttnKvHeads];
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   ring_init(R);
+  if (tid < kAttnKvHeads) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&hand[tid].full[i], 1);
+      mbar_init(&hand[tid].empty[i], 1);
+    }
+    fence_mbar_init();
+  }
   __syncthreads();
   const uint32_t i_begin = blockIdx.x < b.ctas ? b.cta_item[blockIdx.x] : 0u;
   const uint32_t i_end = blockIdx.x < b.ctas ? b.cta_item[blockIdx.x + 1] : 0u;
@@ -268,22 +287,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
     return;
   }
 
-  // -------------------------------------------------------------- consumers
+  // ---------------------------------------------------------- decoder warps
   const int head = warp & (kAttnKvHeads - 1);
-  const uint32_t parity = static_cast<uint32_t>(warp >> 3);
+  uint8_t* tiles = ring + kAttnStages * kAttnStageBytes + head * 2 * kAttnTileBytes;  // K slot, V slot
+  AttnHandoff& H = hand[head];
+  if (warp < kAttnKvHeads) {
+    int pair_req = -1;
+    uint32_t fills = 0;  // tiles decoded into each slot so far (same for both)
+    AttnPos p;
+    for (uint32_t item = i_begin; item < i_end; ++item) {
+      const AttnItem& I = b.item[item];
+      const int req = static_cast<int>(I.req);
+      if (req != pair_req) {
+        // the request's fixed6 pair table, built by the decoder warps: all
+        // are past their stages of the previous item; the palette comes from
+        // the item's first stage
+        attn_decoder_sync();
+        consumer_wait(R, p, nullptr);
+        const uint8_t* pal = D[p.s].pal;
+        for (int i = tid; i < 4096; i += kAttnDecoders)
+          pair[i] = (static_cast<uint32_t>(pal[i & 63]) << 8) | (static_cast<uint32_t>(pal[i >> 6]) << 24);
+        pair_req = req;
+        attn_decoder_sync();
+      }
+      for (uint32_t k = 0; k < 2 * I.blocks; ++k) {
+        const uint32_t slot = k & 1;
+        consumer_wait(R, p, nullptr);
+        const AttnDesc& d = D[p.s];
+        if (fills > 0) wait_stage(&H.empty[slot], (fills - 1) & 1, nullptr);  // the MMA warp is done with it
+        attn_decode_tile(d, ring + p.s * kAttnStageBytes, reinterpret_cast<const uint8_t*>(pair),
+                         tiles + slot * kAttnTileBytes, head, lane);
+        if (lane == 0) H.valid[slot] = d.valid;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&H.full[slot]);
+        consumer_release(R, p);
+        p.next();
+        if (slot == 1) ++fills;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- MMA warps
   const uint32_t group = b.group;
   const uint32_t gid = lane >> 2;  // MMA group: token gid (+8) of S^T, dim 16m + gid (+8) of O^T
   const uint32_t tig = lane & 3;   // q heads 2*tig, 2*tig + 1 of the group (valid below `group`)
-  uint8_t* tile = ring + kAttnStages * kAttnStageBytes + warp * kAttnTileBytes;
-  int pair_req = -1;
-  AttnPos p;
+  const uint8_t* tileK = tiles;
+  const uint8_t* tileV = tiles + kAttnTileBytes;
+  uint32_t uses = 0;  // tiles consumed from each slot so far
   for (uint32_t item = i_begin; item < i_end; ++item) {
     const AttnItem& I = b.item[item];
-    const int req = static_cast<int>(I.req);
     // Q^T fragments (B operand of S^T = K Q^T): Q[q head gid][dims 16k + 2*tig (+8)]
     uint32_t qb[8][2];
     {
-      const uint16_t* qh = b.req[req].q + static_cast<uint64_t>(head * group + gid) * kAttnHeadDim;
+      const uint16_t* qh = b.req[I.req].q + static_cast<uint64_t>(head * group + gid) * kAttnHeadDim;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         qb[k][0] = gid < group ? *reinterpret_cast<const uint32_t*>(qh + 16 * k + 2 * tig) : 0u;
@@ -294,104 +351,78 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
 #pragma unroll
     for (int m = 0; m < 8; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
     float mx[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
-    uint32_t ph0 = 0, ph1 = 0, pl0 = 0, pl1 = 0;  // P^T as B fragments (hi, lo parts)
-    if (req != pair_req) {
-      // the request's fixed6 pair table, built by all consumers: every warp
-      // is past its stages of the previous item, then all read the palette
-      // from the item's first stage (waiting on it without releasing it: its
-      // parity-0 warps release it only after the second barrier)
-      attn_consumer_sync();
-      consumer_wait(R, p, nullptr);
-      const uint8_t* pal = D[p.s].pal;
-      for (int i = tid; i < 4096; i += kAttnConsumers)
-        pair[i] = (static_cast<uint32_t>(pal[i & 63]) << 8) | (static_cast<uint32_t>(pal[i >> 6]) << 24);
-      pair_req = req;
-      attn_consumer_sync();
-    }
-    for (uint32_t k = 0; k < 2 * I.blocks; ++k) {
-      if (((k >> 1) & 1u) != parity) {
-        p.next();
-        continue;
+    for (uint32_t blk = 0; blk < I.blocks; ++blk, ++uses) {
+      // ---- S^T = K Q^T: 16 tokens x 8 head slots, 8 steps of 16 dims
+      wait_stage(&H.full[0], uses & 1, nullptr);
+      const uint32_t valid = H.valid[0];
+      float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd steps
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        // matrices: tokens 0-7 / 8-15 of dims 16kk..+7, then of dims 16kk+8..+15
+        uint32_t a[4];
+        ldmatrix_x4(a, tile_chunk(const_cast<uint8_t*>(tileK), (lane & 7) + ((lane >> 3) & 1) * 8,
+                                  2 * kk + (lane >> 4)));
+        mma_bf16((kk & 1) ? sd : sc, a[0], a[1], a[2], a[3], qb[kk][0], qb[kk][1]);
       }
-      consumer_wait(R, p, nullptr);
-      const AttnDesc& d = D[p.s];
-      const uint8_t* stage = ring + p.s * kAttnStageBytes;
-      const uint32_t valid = d.valid;
-      __syncwarp();  // the tile's previous contents were read by every lane
-      attn_decode_tile(d, stage, reinterpret_cast<const uint8_t*>(pair), tile, head, lane);
-      // the stage is decoded into the tile: hand it back to the producer now,
-      // so that it refills while this warp runs the MMAs and the softmax
-      consumer_release(R, p);
-      p.next();
       __syncwarp();
-      if ((k & 1) == 0) {
-        // S^T = K Q^T: 16 tokens x 8 head slots, 8 steps of 16 dims
-        float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd steps
+      if (lane == 0) mbar_arrive(&H.empty[0]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // matrices: tokens 0-7 / 8-15 of dims 16kk..+7, then of dims 16kk+8..+15
-          uint32_t a[4];
-          ldmatrix_x4(a, tile_chunk(tile, (lane & 7) + ((lane >> 3) & 1) * 8, 2 * kk + (lane >> 4)));
-          mma_bf16((kk & 1) ? sd : sc, a[0], a[1], a[2], a[3], qb[kk][0], qb[kk][1]);
-        }
+      for (int i = 0; i < 4; ++i) sc[i] += sd[i];
+      // ---- online softmax per q head (column) over tokens gid, gid + 8 of all lanes with this tig
+      float x[4];
+      x[0] = gid < valid ? sc[0] * b.scale_log2 : -INFINITY;
+      x[1] = gid < valid ? sc[1] * b.scale_log2 : -INFINITY;
+      x[2] = gid + 8 < valid ? sc[2] * b.scale_log2 : -INFINITY;
+      x[3] = gid + 8 < valid ? sc[3] * b.scale_log2 : -INFINITY;
+      float pe[4], alpha[2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i] += sd[i];
-        // online softmax per q head (column) over tokens gid, gid + 8 of all lanes with this tig
-        float x[4];
-        x[0] = gid < valid ? sc[0] * b.scale_log2 : -INFINITY;
-        x[1] = gid < valid ? sc[1] * b.scale_log2 : -INFINITY;
-        x[2] = gid + 8 < valid ? sc[2] * b.scale_log2 : -INFINITY;
-        x[3] = gid + 8 < valid ? sc[3] * b.scale_log2 : -INFINITY;
-        float pe[4], alpha[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float bm = fmaxf(x[e], x[2 + e]);
-          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 4));
-          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 8));
-          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
-          const float m_new = fmaxf(mx[e], bm);
-          alpha[e] = exp2f(mx[e] - m_new);  // 0 on the first block (mx = -inf)
-          pe[e] = exp2f(x[e] - m_new);
-          pe[2 + e] = exp2f(x[2 + e] - m_new);
-          float bs = pe[e] + pe[2 + e];
-          bs += __shfl_xor_sync(kFull, bs, 4);
-          bs += __shfl_xor_sync(kFull, bs, 8);
-          bs += __shfl_xor_sync(kFull, bs, 16);
-          lsum[e] = lsum[e] * alpha[e] + bs;
-          mx[e] = m_new;
-        }
-        if (!__all_sync(kFull, alpha[0] == 1.f && alpha[1] == 1.f)) {  // a running max moved
-#pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            o[m][0] *= alpha[0];
-            o[m][1] *= alpha[1];
-            o[m][2] *= alpha[0];
-            o[m][3] *= alpha[1];
-          }
-        }
-        // P^T rows (tokens gid, gid+8) x head pairs -> B fragments of V^T P^T
-        const uint32_t h0 = pack_bf16(pe[0], pe[1]), h1 = pack_bf16(pe[2], pe[3]);
-        const uint32_t l0 = pack_bf16(pe[0] - __uint_as_float(h0 << 16), pe[1] - __uint_as_float(h0 & 0xFFFF0000u));
-        const uint32_t l1 = pack_bf16(pe[2] - __uint_as_float(h1 << 16), pe[3] - __uint_as_float(h1 & 0xFFFF0000u));
-        ph0 = movmatrix_trans(h0);
-        ph1 = movmatrix_trans(h1);
-        pl0 = movmatrix_trans(l0);
-        pl1 = movmatrix_trans(l1);
-      } else {
-        // O^T += V^T P^T: 8 steps of 16 dims, k = the block's 16 tokens
+      for (int e = 0; e < 2; ++e) {
+        float bm = fmaxf(x[e], x[2 + e]);
+        bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 4));
+        bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 8));
+        bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
+        const float m_new = fmaxf(mx[e], bm);
+        alpha[e] = exp2f(mx[e] - m_new);  // 0 on the first block (mx = -inf)
+        pe[e] = exp2f(x[e] - m_new);
+        pe[2 + e] = exp2f(x[2 + e] - m_new);
+        float bs = pe[e] + pe[2 + e];
+        bs += __shfl_xor_sync(kFull, bs, 4);
+        bs += __shfl_xor_sync(kFull, bs, 8);
+        bs += __shfl_xor_sync(kFull, bs, 16);
+        lsum[e] = lsum[e] * alpha[e] + bs;
+        mx[e] = m_new;
+      }
+      if (!__all_sync(kFull, alpha[0] == 1.f && alpha[1] == 1.f)) {  // a running max moved
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
-          // matrices: tokens 0-7 of dims 16m / 16m+8, then tokens 8-15 of dims 16m / 16m+8
-          uint32_t a[4];
-          ldmatrix_x4_trans(a, tile_chunk(tile, (lane & 7) + (lane >> 4) * 8, 2 * m + ((lane >> 3) & 1)));
-          mma_bf16(o[m], a[0], a[1], a[2], a[3], ph0, ph1);
-          mma_bf16(o[m], a[0], a[1], a[2], a[3], pl0, pl1);
+          o[m][0] *= alpha[0];
+          o[m][1] *= alpha[1];
+          o[m][2] *= alpha[0];
+          o[m][3] *= alpha[1];
         }
       }
+      // P^T rows (tokens gid, gid+8) x head pairs -> B fragments of V^T P^T
+      const uint32_t h0 = pack_bf16(pe[0], pe[1]), h1 = pack_bf16(pe[2], pe[3]);
+      const uint32_t l0 = pack_bf16(pe[0] - __uint_as_float(h0 << 16), pe[1] - __uint_as_float(h0 & 0xFFFF0000u));
+      const uint32_t l1 = pack_bf16(pe[2] - __uint_as_float(h1 << 16), pe[3] - __uint_as_float(h1 & 0xFFFF0000u));
+      const uint32_t ph0 = movmatrix_trans(h0), ph1 = movmatrix_trans(h1);
+      const uint32_t pl0 = movmatrix_trans(l0), pl1 = movmatrix_trans(l1);
+      // ---- O^T += V^T P^T: 8 steps of 16 dims, k = the block's 16 tokens
+      wait_stage(&H.full[1], uses & 1, nullptr);
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        // matrices: tokens 0-7 of dims 16m / 16m+8, then tokens 8-15 of dims 16m / 16m+8
+        uint32_t a[4];
+        ldmatrix_x4_trans(a, tile_chunk(const_cast<uint8_t*>(tileV), (lane & 7) + (lane >> 4) * 8,
+                                        2 * m + ((lane >> 3) & 1)));
+        mma_bf16(o[m], a[0], a[1], a[2], a[3], ph0, ph1);
+        mma_bf16(o[m], a[0], a[1], a[2], a[3], pl0, pl1);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&H.empty[1]);
     }
-    // partial of (item, parity): O^T columns of the group's heads, m and l
-    const uint32_t heads = kAttnKvHeads * group;
-    float* base = b.partials + (static_cast<uint64_t>(item) * 2 + parity) * heads * kAttnRecord;
+    // partial of the item: O^T columns of the group's heads, m and l
+    float* base = b.partials + static_cast<uint64_t>(item) * kAttnKvHeads * group * kAttnRecord;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const uint32_t hcol = 2 * tig + e;
@@ -422,11 +453,11 @@ __global__ void __launch_bounds__(256) AttnCombineKernel(const __grid_constant__
   if (wid >= b.reqs * heads) return;
   const AttnReq& Q = b.req[wid / heads];
   const uint32_t hq = wid % heads;
-  // records of the request: (item, parity) pairs
+  // records of the request: one per item
   auto rec = [&](uint32_t i) {
-    return b.partials + (static_cast<uint64_t>(2 * Q.first_item + i) * heads + hq) * kAttnRecord;
+    return b.partials + (static_cast<uint64_t>(Q.first_item + i) * heads + hq) * kAttnRecord;
   };
-  const uint32_t records = 2 * Q.items;
+  const uint32_t records = Q.items;
   float M = -INFINITY;
   for (uint32_t i = lane; i < records; i += 32) M = fmaxf(M, rec(i)[kAttnHeadDim]);
 #pragma unroll
