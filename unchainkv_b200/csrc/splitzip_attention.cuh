@@ -154,11 +154,27 @@ struct AttnHandoff {
   uint32_t pad[2];
 };
 
+// The attention kernel's fixed6 pair table is stored swizzled: the entry of
+// code pair idx = c0 | c1 << 6 (pal[c0] << 8 | pal[c1] << 24) sits at slot
+// idx ^ (c1 & 31).  A warp's lookups then spread over the banks by c0 ^ c1
+// rather than by c0 alone: neighbouring channels' codes concentrate on a few
+// palette entries, and the decode shares the shared-memory pipe with the
+// MMA operand reads.
+__device__ __forceinline__ uint32_t pair_entry(const uint8_t* pal, uint32_t slot) {
+  const uint32_t idx = slot ^ ((slot >> 6) & 31u);
+  return (static_cast<uint32_t>(pal[idx & 63]) << 8) | (static_cast<uint32_t>(pal[idx >> 6]) << 24);
+}
+
+// Byte offset into the swizzled pair table of the code field f = 4 * idx.
+__device__ __forceinline__ uint32_t pair_slot(uint32_t f) { return f ^ ((f >> 6) & 0x7Cu); }
+
 // A warp's 16-token x 128-dim bf16 tile: rows of 16 chunks of 16 bytes, chunk
-// c of row t stored at chunk c ^ (t & 7) (ldmatrix reads 8 rows of one logical
-// chunk without bank conflicts).
+// c of row t stored at chunk c ^ (t & 7) ^ (c / 8).  ldmatrix reads 8 rows of
+// one logical chunk without bank conflicts, and so does the decode's store of
+// chunks 2g (g = 0..7) of one row: the c / 8 term moves the upper 4 onto the
+// odd bank groups.
 __device__ __forceinline__ uint8_t* tile_chunk(uint8_t* tile, uint32_t t, uint32_t c) {
-  return tile + t * 256 + ((c ^ (t & 7)) << 4);
+  return tile + t * 256 + ((c ^ (t & 7) ^ (c >> 3)) << 4);
 }
 
 // Decode this warp's head slice of a staged plane block into its tile: 128
@@ -186,14 +202,14 @@ __device__ __forceinline__ void attn_decode_tile(const AttnDesc& d, const uint8_
         smem_read16_window(stage + kAttnCodesOffset, d.pad_y + 3 * w0 / 4, Q);
       }
       uint32_t f[8];
-      f[0] = (Q[0] << 2) & 0x3FFCu;
-      f[1] = (Q[0] >> 10) & 0x3FFCu;
-      f[2] = __funnelshift_r(Q[0], Q[1], 22) & 0x3FFCu;
-      f[3] = (Q[1] >> 2) & 0x3FFCu;
-      f[4] = (Q[1] >> 14) & 0x3FFCu;
-      f[5] = __funnelshift_r(Q[1], Q[2], 26) & 0x3FFCu;
-      f[6] = (Q[2] >> 6) & 0x3FFCu;
-      f[7] = (Q[2] >> 18) & 0x3FFCu;
+      f[0] = pair_slot((Q[0] << 2) & 0x3FFCu);
+      f[1] = pair_slot((Q[0] >> 10) & 0x3FFCu);
+      f[2] = pair_slot(__funnelshift_r(Q[0], Q[1], 22) & 0x3FFCu);
+      f[3] = pair_slot((Q[1] >> 2) & 0x3FFCu);
+      f[4] = pair_slot((Q[1] >> 14) & 0x3FFCu);
+      f[5] = pair_slot(__funnelshift_r(Q[1], Q[2], 26) & 0x3FFCu);
+      f[6] = pair_slot((Q[2] >> 6) & 0x3FFCu);
+      f[7] = pair_slot((Q[2] >> 18) & 0x3FFCu);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         o[i] = __byte_perm(Lw[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140) |
@@ -306,7 +322,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
         consumer_wait(R, p, nullptr);
         const uint8_t* pal = D[p.s].pal;
         for (int i = tid; i < 4096; i += kAttnDecoders)
-          pair[i] = (static_cast<uint32_t>(pal[i & 63]) << 8) | (static_cast<uint32_t>(pal[i >> 6]) << 24);
+          pair[i] = pair_entry(pal, i);
         pair_req = req;
         attn_decoder_sync();
       }
