@@ -14,24 +14,26 @@
 // holds one or a few items).  Per item:
 //   - producer warp: for each block, stages the K plane block (16 tokens x
 //     8 heads x 128 dims), then the V plane block, into a ring of shared
-//     memory stages by TMA (the stream regions of that block's words: the
-//     low-byte plane and 6-bit codes for fixed6, the words for raw);
-//   - decoder warp h (kv head h): decodes its head's 16 x 128 slice of every
-//     staged plane block into a swizzled bf16 tile in shared memory (a K
-//     slot and a V slot per head) and releases the stage;
-//   - MMA warp h: computes S^T = K Q^T (16 tokens x g q heads) on one
-//     m16n8k16 bf16 MMA per 16 dims with K fragments from ldmatrix, keeps an
-//     online softmax per q head in fp32 (base 2), turns P^T into the PV
-//     operand in registers (movmatrix), and accumulates O^T += V^T P^T
-//     (128 dims x g) with V^T fragments from ldmatrix.trans; P is split into
-//     two bf16 parts (hi + lo) so that large V values do not amplify its
-//     rounding.  Decoder and MMA warp of a head hand the slots over with
-//     full/empty mbarriers, so decoding and MMAs overlap;
+//     memory stages by TMA, one copy per token row (the row's low bytes and
+//     6-bit codes for fixed6, its words for raw);
+//   - K warp h (kv head h): decodes its head's slice of each K block
+//     straight into the A fragments of S^T = K Q^T (16 tokens x g q heads,
+//     one m16n8k16 bf16 MMA per 16 dims) and hands the S^T fragments to the
+//     V warp through a two-slot buffer with full/empty mbarriers;
+//   - V warp h: keeps an online softmax per q head in fp32 (base 2), turns
+//     P^T into the PV operand in registers (movmatrix), decodes its head's
+//     slice of each V block straight into the A fragments of
+//     O^T += V^T P^T (128 dims x g) and accumulates; P is split into two
+//     bf16 parts (hi + lo) so that large V values do not amplify its
+//     rounding;
 //   - every item writes a partial (m, l, O) per q head to a workspace and
 //     AttnCombineKernel merges them per request.
-// The tiles have g useful columns of 8 (g = 4 for the benchmark), so they
-// run on warp-level MMAs; the kernel is bound by the HBM read of the
-// compressed K/V.
+// Decoding into fragments needs no bf16 tile in shared memory: the MMAs'
+// contraction and row orders are permuted so that each lane decodes
+// consecutive dims of a few tokens (the permutation is applied to Q as well,
+// and undone when O is written).  The tiles have g useful columns of 8
+// (g = 4 for the benchmark), so they run on warp-level MMAs; the kernel is
+// bound by the HBM read of the compressed K/V and by shared-memory traffic.
 #pragma once
 
 #include "splitzip_kernels.cuh"
@@ -40,18 +42,27 @@ namespace ukv {
 
 constexpr int kAttnHeadDim = 128;
 constexpr int kAttnBlockTokens = 16;
-constexpr int kAttnKvHeads = kWarps;  // consumer warps of one block parity
-constexpr int kAttnConsumerWarps = 2 * kAttnKvHeads;  // a decoder and an MMA warp per kv head
+constexpr int kAttnKvHeads = kWarps;  // consumer warps of one plane
+constexpr int kAttnConsumerWarps = 2 * kAttnKvHeads;  // a K and a V warp per kv head
 constexpr int kAttnConsumers = 32 * kAttnConsumerWarps;
 constexpr int kAttnThreads = kAttnConsumers + 32;     // + the producer warp
-constexpr int kAttnDecoders = 32 * kAttnKvHeads;      // threads of the decoder warps
+constexpr int kAttnKThreads = 32 * kAttnKvHeads;      // threads of the K warps
 constexpr uint32_t kAttnBlockWords = kAttnBlockTokens * kAttnKvHeads * kAttnHeadDim;  // per plane
-constexpr int kAttnStages = 4;
-constexpr uint32_t kAttnStageBytes = 2 * kAttnBlockWords + 64;  // raw words of one plane block + pads
-constexpr uint32_t kAttnCodesOffset = kAttnBlockWords + 32;     // fixed6 codes inside a stage
-constexpr uint32_t kAttnTileBytes = kAttnBlockTokens * kAttnHeadDim * 2;  // one warp's bf16 tile
-// dynamic shared memory: the ring stages, then one tile per consumer warp
-constexpr uint32_t kAttnSmemBytes = kAttnStages * kAttnStageBytes + kAttnConsumerWarps * kAttnTileBytes;
+constexpr int kAttnStages = 6;  // K and V plane blocks alternate: 3 blocks in flight
+// A stage holds one plane block as 16 token rows.  With kAttnRowPad = 16
+// each row is copied to a slot 16 bytes longer than the row (consecutive
+// rows start 4 banks apart, so fragment reads of 8 tokens at one offset do
+// not collide) by one bulk copy per row; with 0 the rows are contiguous and
+// a plane region goes by one bulk copy.
+constexpr uint32_t kAttnRowPad = 0;
+constexpr uint32_t kAttnRowWords = kAttnKvHeads * kAttnHeadDim;             // words of one token row
+constexpr uint32_t kAttnLowPitch = kAttnRowWords + kAttnRowPad;             // fixed6 low bytes
+constexpr uint32_t kAttnCodePitch = 3 * kAttnRowWords / 4 + kAttnRowPad;    // fixed6 codes
+constexpr uint32_t kAttnRawPitch = 2 * kAttnRowWords + kAttnRowPad;         // raw words
+constexpr uint32_t kAttnCodesOffset = kAttnBlockTokens * kAttnLowPitch + 16;  // fixed6 code rows inside a stage
+constexpr uint32_t kAttnStageBytes = kAttnBlockTokens * kAttnRawPitch + 32;  // + room for the pads of whole regions
+static_assert(kAttnCodesOffset + kAttnBlockTokens * kAttnCodePitch <= kAttnStageBytes, "fixed6 rows fit");
+constexpr uint32_t kAttnSmemBytes = kAttnStages * kAttnStageBytes;  // dynamic shared memory: the ring
 constexpr int kAttnMaxReqs = 64;
 constexpr int kAttnMaxItems = 1024;
 constexpr int kAttnMaxCtas = 320;
@@ -120,18 +131,6 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_addr(p)));
-}
-
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_addr(p)));
-}
-
 // Transpose an 8x8 bf16 matrix held in MMA fragment layout across the warp.
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t r;
@@ -139,14 +138,14 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return r;
 }
 
-// Barrier of the attention kernel's decoder warps (named barrier 1).
-__device__ __forceinline__ void attn_decoder_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kAttnDecoders) : "memory");
+// Barrier of the attention kernel's K and V warps (named barrier 1).
+__device__ __forceinline__ void attn_consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kAttnConsumers) : "memory");
 }
 
-// Tile hand-over between the decoder and the MMA warp of a head: slot 0
-// holds K tiles, slot 1 V tiles; full[slot] when decoded, empty[slot] when
-// the MMA warp is done with it.  `valid` carries the block's valid tokens.
+// S^T hand-over from the K warp to the V warp of a head: two slots used in
+// turn; full[slot] when written, empty[slot] when the V warp has read it.
+// `valid` carries the block's valid tokens.
 struct AttnHandoff {
   uint64_t full[2];
   uint64_t empty[2];
@@ -168,81 +167,143 @@ __device__ __forceinline__ uint32_t pair_entry(const uint8_t* pal, uint32_t slot
 // Byte offset into the swizzled pair table of the code field f = 4 * idx.
 __device__ __forceinline__ uint32_t pair_slot(uint32_t f) { return f ^ ((f >> 6) & 0x7Cu); }
 
-// A warp's 16-token x 128-dim bf16 tile: rows of 16 chunks of 16 bytes, chunk
-// c of row t stored at chunk c ^ (t & 7) ^ (c / 8).  ldmatrix reads 8 rows of
-// one logical chunk without bank conflicts, and so does the decode's store of
-// chunks 2g (g = 0..7) of one row: the c / 8 term moves the upper 4 onto the
-// odd bank groups.
-__device__ __forceinline__ uint8_t* tile_chunk(uint8_t* tile, uint32_t t, uint32_t c) {
-  return tile + t * 256 + ((c ^ (t & 7) ^ (c >> 3)) << 4);
+// Pair-table lookup: the decoded bf16 word pair of the 12-bit code field at
+// byte offset f (4 * field) with its two low bytes, which sit in bytes
+// (sel & 1) * 2 and +1 of lw.
+__device__ __forceinline__ uint32_t fixed6_pair(const uint8_t* pair, uint32_t f, uint32_t lw, bool upper) {
+  return __byte_perm(lw, 0, upper ? 0x4342 : 0x4140) | *reinterpret_cast<const uint32_t*>(pair + pair_slot(f));
 }
 
-// Decode this warp's head slice of a staged plane block into its tile: 128
-// units of 16 words (token t = u / 8, dims 16 * (u % 8)), 4 per lane.
-__device__ __forceinline__ void attn_decode_tile(const AttnDesc& d, const uint8_t* stage, const uint8_t* pair,
-                                                 uint8_t* tile, int head, int lane) {
-  const bool aligned = (d.pad_x | d.pad_y) == 0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t u = lane + 32 * k;
-    const uint32_t t = u >> 3, g = u & 7;
-    const uint32_t w0 = t * (kAttnKvHeads * kAttnHeadDim) + head * kAttnHeadDim + 16 * g;  // word in the block
-    uint32_t o[8];
-    if (d.mode == 3) {
-      uint32_t Lw[4];
-      uint32_t Q[4];  // 12 code bytes
-      if (aligned) {  // uniform: the stream regions start on 16-byte boundaries
-        const uint4 l4 = *reinterpret_cast<const uint4*>(stage + w0);
-        Lw[0] = l4.x; Lw[1] = l4.y; Lw[2] = l4.z; Lw[3] = l4.w;
-        const uint32_t* c = reinterpret_cast<const uint32_t*>(stage + kAttnCodesOffset + 3 * w0 / 4);
-        Q[0] = c[0]; Q[1] = c[1]; Q[2] = c[2]; Q[3] = 0;
-      } else {
-        smem_read16_window(stage, d.pad_x + w0, Lw);
-        // 16-byte window reads keep each quarter warp on one row's banks
-        smem_read16_window(stage + kAttnCodesOffset, d.pad_y + 3 * w0 / 4, Q);
-      }
-      uint32_t f[8];
-      f[0] = pair_slot((Q[0] << 2) & 0x3FFCu);
-      f[1] = pair_slot((Q[0] >> 10) & 0x3FFCu);
-      f[2] = pair_slot(__funnelshift_r(Q[0], Q[1], 22) & 0x3FFCu);
-      f[3] = pair_slot((Q[1] >> 2) & 0x3FFCu);
-      f[4] = pair_slot((Q[1] >> 14) & 0x3FFCu);
-      f[5] = pair_slot(__funnelshift_r(Q[1], Q[2], 26) & 0x3FFCu);
-      f[6] = pair_slot((Q[2] >> 6) & 0x3FFCu);
-      f[7] = pair_slot((Q[2] >> 18) & 0x3FFCu);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        o[i] = __byte_perm(Lw[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140) |
-               *reinterpret_cast<const uint32_t*>(pair + f[i]);
-    } else if (d.mode == 6) {  // raw
-      if (aligned) {
-        const uint4* r = reinterpret_cast<const uint4*>(stage + 2 * w0);
-        const uint4 a = r[0], b2 = r[1];
-        o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
-        o[4] = b2.x; o[5] = b2.y; o[6] = b2.z; o[7] = b2.w;
-      } else {
-        smem_read_words<8>(stage, d.pad_x + 2 * w0, o);
-      }
-    } else {  // a stream this kernel does not read: zeros (the producer raised an error)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = 0u;
-    }
-    *reinterpret_cast<uint4*>(tile_chunk(tile, t, 2 * g)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4*>(tile_chunk(tile, t, 2 * g + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+// Byte offset (4 * field) of 12-bit code field i (0..7) of 3 words.
+__device__ __forceinline__ uint32_t fixed6_field(const uint32_t* c, int i) {
+  switch (i) {
+    case 0: return (c[0] << 2) & 0x3FFCu;
+    case 1: return (c[0] >> 10) & 0x3FFCu;
+    case 2: return __funnelshift_r(c[0], c[1], 22) & 0x3FFCu;
+    case 3: return (c[1] >> 2) & 0x3FFCu;
+    case 4: return (c[1] >> 14) & 0x3FFCu;
+    case 5: return __funnelshift_r(c[1], c[2], 26) & 0x3FFCu;
+    case 6: return (c[2] >> 6) & 0x3FFCu;
+    default: return (c[2] >> 18) & 0x3FFCu;
   }
 }
 
+// One lane's share of staging a stage: `len` bytes at byte `off` of a stream
+// of `glen` bytes, copied to a row slot from the 16-byte boundary at or
+// below them (so the row starts `pad` bytes into the slot).  The 16-byte
+// aligned middle goes by one bulk copy; the bytes before the stream's first
+// or after its last 16-byte boundary by plain loads.
+struct RowCopy {
+  const uint8_t* first;  // the 16-byte boundary at or below the row
+  const uint8_t* lo;     // bulk copy source, `bulk` bytes
+  const uint8_t* row;    // the row, `len` bytes
+  uint32_t bulk;
+  uint32_t len;
+  uint32_t pad;
+};
+
+__device__ __forceinline__ RowCopy plan_row_copy(const uint8_t* g, uint64_t glen, uint64_t off, uint32_t len) {
+  const uintptr_t base = reinterpret_cast<uintptr_t>(g);
+  const uintptr_t A = base + off, E = A + len;
+  const uintptr_t F = A & ~static_cast<uintptr_t>(15);
+  const uintptr_t gal = (base + 15) & ~static_cast<uintptr_t>(15);
+  const uintptr_t gend = (base + glen) & ~static_cast<uintptr_t>(15);
+  const uintptr_t lo = F > gal ? F : gal;
+  const uintptr_t Eal = (E + 15) & ~static_cast<uintptr_t>(15);
+  const uintptr_t hi = Eal < gend ? Eal : gend;
+  RowCopy c;
+  c.first = reinterpret_cast<const uint8_t*>(F);
+  c.lo = reinterpret_cast<const uint8_t*>(lo);
+  c.row = reinterpret_cast<const uint8_t*>(A);
+  c.bulk = len > 0 && hi > lo ? static_cast<uint32_t>(hi - lo) : 0u;
+  c.len = len;
+  c.pad = static_cast<uint32_t>(A - F);
+  return c;
+}
+
+// Issue the planned copy into the slot at `dst` (the barrier already
+// expects the bulk bytes).
+__device__ __forceinline__ void issue_row_copy(const RowCopy& c, uint8_t* dst, uint64_t* bar) {
+  if (c.bulk > 0) bulk_g2s(dst + (c.lo - c.first), c.lo, c.bulk, bar);
+  const uint8_t* end = c.row + c.len;
+  const uint8_t* hi = c.bulk > 0 ? c.lo + c.bulk : c.row;
+  for (const uint8_t* a = c.row; a < (c.bulk > 0 ? c.lo : c.row); ++a) dst[a - c.first] = *a;
+  for (const uint8_t* a = hi > c.row ? hi : c.row; a < end; ++a) dst[a - c.first] = *a;
+}
+
+// Stage rows of token t: fixed6 low bytes, fixed6 codes, raw words.
+__device__ __forceinline__ const uint8_t* low_row(const uint8_t* stage, uint32_t t) { return stage + t * kAttnLowPitch; }
+__device__ __forceinline__ const uint8_t* code_row(const uint8_t* stage, uint32_t t) {
+  return stage + kAttnCodesOffset + t * kAttnCodePitch;
+}
+__device__ __forceinline__ const uint8_t* raw_row(const uint8_t* stage, uint32_t t) { return stage + t * kAttnRawPitch; }
+
+// The fixed6 inputs of NP word pairs of token t from word `dim` of the row:
+// low bytes L (NP / 2 words) and codes C (3 NP / 8 words).
+template <int NP>
+__device__ __forceinline__ void fixed6_load(const AttnDesc& d, const uint8_t* stage, uint32_t t, uint32_t dim,
+                                            uint32_t (&L)[NP / 2], uint32_t (&C)[3 * NP / 8]) {
+  const uint8_t* low = low_row(stage, t) + dim;
+  const uint8_t* codes = code_row(stage, t) + 3 * dim / 4;
+  if ((d.pad_x | d.pad_y) == 0) {  // the stream's regions start on 16-byte boundaries
+#pragma unroll
+    for (int j = 0; j < NP / 8; ++j) {
+      const uint4 l = reinterpret_cast<const uint4*>(low)[j];
+      L[4 * j] = l.x; L[4 * j + 1] = l.y; L[4 * j + 2] = l.z; L[4 * j + 3] = l.w;
+    }
+    if constexpr (NP == 16) {  // 24 code bytes, 8-byte aligned
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const uint2 c = reinterpret_cast<const uint2*>(codes)[j];
+        C[2 * j] = c.x;
+        C[2 * j + 1] = c.y;
+      }
+    } else {  // 12 code bytes, 4-byte aligned
+#pragma unroll
+      for (int j = 0; j < 3 * NP / 8; ++j) C[j] = reinterpret_cast<const uint32_t*>(codes)[j];
+    }
+  } else {
+    smem_read_words<NP / 2>(low, d.pad_x, L);
+    smem_read_words<3 * NP / 8>(codes, d.pad_y, C);
+  }
+}
+
+// Word pair i (words 2i, 2i + 1 from the loaded offset) of fixed6 inputs.
+template <int NP>
+__device__ __forceinline__ uint32_t fixed6_word_pair(const uint8_t* pair, const uint32_t (&L)[NP / 2],
+                                                     const uint32_t (&C)[3 * NP / 8], int i) {
+  return fixed6_pair(pair, fixed6_field(C + 3 * (i >> 3), i & 7), L[i >> 1], i & 1);
+}
+
+// Word pair i of token t from word `dim` of a raw row.
+__device__ __forceinline__ uint32_t raw_word_pair(const AttnDesc& d, const uint8_t* stage, uint32_t t, uint32_t dim,
+                                                  int i) {
+  const uint8_t* row = raw_row(stage, t) + 2 * dim + 4 * i;
+  if (d.pad_x == 0) return *reinterpret_cast<const uint32_t*>(row);
+  uint32_t w[1];
+  smem_read_words<1>(row, d.pad_x, w);
+  return w[0];
+}
+
+// 17 warps, one CTA per SM: a sub-partition hosting 5 of them allows 96
+// registers per thread.
 template <int kMaxR, int kMaxI>
 __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint32_t pair[4096];
+  __shared__ __align__(16) float4 scores[kAttnKvHeads][2][32];  // S^T fragments, two slots per head
   __shared__ __align__(16) AttnDesc D[kAttnStages];
-  __shared__ AttnRing R;  // empty barriers count the kWarps == kAttnKvHeads decoder warps
+  __shared__ AttnRing R;  // empty barriers count the kWarps == kAttnKvHeads warps of one plane
   __shared__ __align__(8) AttnHandoff hand[kAttnKvHeads];
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  ring_init(R);
+  if (tid == 0) {
+    for (int i = 0; i < kAttnStages; ++i) {
+      mbar_init(&R.full[i], 1);  // lane 0 of the producer, after the warp's copies are issued
+      mbar_init(&R.empty[i], kAttnKvHeads);
+    }
+  }
   if (tid < kAttnKvHeads) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&hand[tid].full[i], 1);
@@ -256,8 +317,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
 
   if (warp == kAttnConsumerWarps) {
     // ------------------------------------------------------------ producer
-    // K then V of each block of each item of this CTA; the mode byte and the
-    // palette of the item's stream are read once per item
+    // K then V of each block of each item of this CTA, one copy per token
+    // row; the mode byte and the palette of the item's stream are read once
+    // per item
     AttnPos p;
     for (uint32_t item = i_begin; item < i_end; ++item) {
       const AttnItem& I = b.item[item];
@@ -275,121 +337,163 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
         const uint32_t blk = I.block0 + (k >> 1), plane = k & 1;
         producer_acquire(R, p, nullptr);
         AttnDesc& d = D[p.s];
-        const uint64_t w0 = plane * (Q.n / 2) + static_cast<uint64_t>(blk) * kAttnBlockWords;
         uint8_t* stage = ring + p.s * kAttnStageBytes;
+        // lanes 0-15: the low-byte rows (fixed6) or the word rows (raw) of
+        // tokens 0-15; lanes 16-31: the code rows (fixed6).  Rows are 1024
+        // words apart, so every row has the same pad.
+        // (with contiguous rows, lanes 0 and 16 copy the whole regions)
+        const uint32_t t = lane & 15;
+        const uint64_t wt = plane * (Q.n / 2) + (static_cast<uint64_t>(blk) * kAttnBlockTokens + t) * kAttnRowWords;
+        constexpr uint32_t kRows = kAttnRowPad > 0 ? 1 : kAttnBlockTokens;  // rows per copy
+        const bool copies = kAttnRowPad > 0 || t == 0;
+        uint64_t off = 0;
+        uint32_t len = 0;
+        uint8_t* dst = stage;
+        if (mode == 3 && copies) {
+          off = lane < 16 ? 65 + wt : 65 + Q.n + 3 * wt / 4;
+          len = (lane < 16 ? kAttnRowWords : 3 * kAttnRowWords / 4) * kRows;
+          dst = lane < 16 ? stage + t * kAttnLowPitch : stage + kAttnCodesOffset + t * kAttnCodePitch;
+        } else if (mode == 6 && lane < 16 && copies) {
+          off = 1 + 2 * wt;
+          len = 2 * kAttnRowWords * kRows;
+          dst = stage + t * kAttnRawPitch;
+        }
+        const RowCopy c = plan_row_copy(Q.stream, Q.stream_bytes, off, len);
+        const uint32_t total = warp_sum(c.bulk);
+        if (lane == 0 && total > 0) mbar_expect_tx(&R.full[p.s], total);
+        __syncwarp();
+        issue_row_copy(c, dst, &R.full[p.s]);
+        const uint32_t pad = c.pad;
+        const uint32_t pad_y = __shfl_sync(kFull, pad, 16);
         if (lane == 0) {
-          uint2 pad{0, 0};
-          if (mode == 3) {
-            pad.x = stage_bytes_one(Q.stream, Q.stream_bytes, 65 + w0, kAttnBlockWords, stage, &R.full[p.s]);
-            pad.y = stage_bytes_one(Q.stream, Q.stream_bytes, 65 + Q.n + 3 * w0 / 4, 3 * kAttnBlockWords / 4,
-                                    stage + kAttnCodesOffset, &R.full[p.s]);
-          } else if (mode == 6) {
-            pad.x = stage_bytes_one(Q.stream, Q.stream_bytes, 1 + 2 * w0, 2 * kAttnBlockWords, stage, &R.full[p.s]);
-          }
           d.item = item;
           d.block = blk;
           d.plane = plane;
           d.mode = mode;
-          d.pad_x = pad.x;
-          d.pad_y = pad.y;
+          d.pad_x = pad;
+          d.pad_y = mode == 3 ? pad_y : 0u;
           const uint32_t first = blk * kAttnBlockTokens;
           d.valid = Q.ctx > first ? min(Q.ctx - first, static_cast<uint32_t>(kAttnBlockTokens)) : 0u;
         }
         reinterpret_cast<uint16_t*>(d.pal)[lane] = static_cast<uint16_t>(pal);
-        producer_commit(R, p);
+        __syncwarp();  // the lanes' palette and edge-byte stores precede lane 0's release
+        if (lane == 0) mbar_arrive(&R.full[p.s]);
         p.next();
       }
     }
     return;
   }
 
-  // ---------------------------------------------------------- decoder warps
-  const int head = warp & (kAttnKvHeads - 1);
-  uint8_t* tiles = ring + kAttnStages * kAttnStageBytes + head * 2 * kAttnTileBytes;  // K slot, V slot
+  const uint32_t gid = lane >> 2;  // MMA group
+  const uint32_t tig = lane & 3;   // thread in group
+  const uint32_t head = warp & (kAttnKvHeads - 1);
+  const uint32_t group = b.group;
   AttnHandoff& H = hand[head];
+  const uint8_t* pairs = reinterpret_cast<const uint8_t*>(pair);
+  int pair_req = -1;
+
   if (warp < kAttnKvHeads) {
-    int pair_req = -1;
-    uint32_t fills = 0;  // tiles decoded into each slot so far (same for both)
+    // ------------------------------------------------------------ K warps
+    // S^T = K Q^T over the K plane blocks (even ring positions).  The k
+    // index of the MMAs runs over the head's dims in a lane-friendly order:
+    // k slots 2 tig + {0, 1} of step kk are dims 32 tig + 4 kk + {0, 1}, k
+    // slots 2 tig + 8 + {0, 1} are dims 32 tig + 4 kk + {2, 3}, in both K
+    // and Q, so each lane decodes 32 consecutive dims of tokens gid, gid + 8.
+    uint32_t fills = 0;  // S^T fragments handed over
     AttnPos p;
     for (uint32_t item = i_begin; item < i_end; ++item) {
       const AttnItem& I = b.item[item];
       const int req = static_cast<int>(I.req);
       if (req != pair_req) {
-        // the request's fixed6 pair table, built by the decoder warps: all
-        // are past their stages of the previous item; the palette comes from
-        // the item's first stage
-        attn_decoder_sync();
+        // the request's fixed6 pair table: every consumer warp is past the
+        // previous item; the palette comes from the item's first stage
+        attn_consumer_sync();
         consumer_wait(R, p, nullptr);
         const uint8_t* pal = D[p.s].pal;
-        for (int i = tid; i < 4096; i += kAttnDecoders)
-          pair[i] = pair_entry(pal, i);
+        for (int i = tid; i < 4096; i += kAttnKThreads) pair[i] = pair_entry(pal, i);
         pair_req = req;
-        attn_decoder_sync();
+        attn_consumer_sync();
       }
-      for (uint32_t k = 0; k < 2 * I.blocks; ++k) {
-        const uint32_t slot = k & 1;
+      uint32_t qb[16];  // Q[q head gid][dims 32 tig + 2i, +1]
+      {
+        const uint32_t* qh = reinterpret_cast<const uint32_t*>(
+            b.req[I.req].q + static_cast<uint64_t>(head * group + gid) * kAttnHeadDim + 32 * tig);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) qb[i] = gid < group ? qh[i] : 0u;
+      }
+      for (uint32_t blk = 0; blk < I.blocks; ++blk, ++fills) {
         consumer_wait(R, p, nullptr);
         const AttnDesc& d = D[p.s];
-        if (fills > 0) wait_stage(&H.empty[slot], (fills - 1) & 1, nullptr);  // the MMA warp is done with it
-        attn_decode_tile(d, ring + p.s * kAttnStageBytes, reinterpret_cast<const uint8_t*>(pair),
-                         tiles + slot * kAttnTileBytes, head, lane);
-        if (lane == 0) H.valid[slot] = d.valid;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&H.full[slot]);
+        const uint8_t* stage = ring + p.s * kAttnStageBytes;
+        float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd steps
+        const uint32_t dim = head * kAttnHeadDim + 32 * tig;
+        if (d.mode == 3) {
+          uint32_t L0[8], C0[6], L1[8], C1[6];
+          fixed6_load<16>(d, stage, gid, dim, L0, C0);
+          fixed6_load<16>(d, stage, gid + 8, dim, L1, C1);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16((kk & 1) ? sd : sc, fixed6_word_pair<16>(pairs, L0, C0, 2 * kk),
+                     fixed6_word_pair<16>(pairs, L1, C1, 2 * kk), fixed6_word_pair<16>(pairs, L0, C0, 2 * kk + 1),
+                     fixed6_word_pair<16>(pairs, L1, C1, 2 * kk + 1), qb[2 * kk], qb[2 * kk + 1]);
+        } else if (d.mode == 6) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_bf16((kk & 1) ? sd : sc, raw_word_pair(d, stage, gid, dim, 2 * kk),
+                     raw_word_pair(d, stage, gid + 8, dim, 2 * kk), raw_word_pair(d, stage, gid, dim, 2 * kk + 1),
+                     raw_word_pair(d, stage, gid + 8, dim, 2 * kk + 1), qb[2 * kk], qb[2 * kk + 1]);
+        }  // else: a stream this kernel does not read (the producer raised an error): S^T = 0
+        const uint32_t valid = d.valid;
         consumer_release(R, p);
         p.next();
-        if (slot == 1) ++fills;
+        p.next();
+        // hand S^T to the V warp of the head
+        const uint32_t slot = fills & 1, use = fills >> 1;
+        if (use > 0) wait_stage(&H.empty[slot], (use - 1) & 1, nullptr);
+        scores[head][slot][lane] = make_float4(sc[0] + sd[0], sc[1] + sd[1], sc[2] + sd[2], sc[3] + sd[3]);
+        if (lane == 0) H.valid[slot] = valid;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&H.full[slot]);
       }
     }
     return;
   }
 
-  // -------------------------------------------------------------- MMA warps
-  const uint32_t group = b.group;
-  const uint32_t gid = lane >> 2;  // MMA group: token gid (+8) of S^T, dim 16m + gid (+8) of O^T
-  const uint32_t tig = lane & 3;   // q heads 2*tig, 2*tig + 1 of the group (valid below `group`)
-  const uint8_t* tileK = tiles;
-  const uint8_t* tileV = tiles + kAttnTileBytes;
-  uint32_t uses = 0;  // tiles consumed from each slot so far
+  // -------------------------------------------------------------- V warps
+  // Softmax of S^T and O^T += V^T P^T over the V plane blocks (odd ring
+  // positions).  The M index of the MMAs runs over the head's dims in a
+  // lane-friendly order: rows gid, gid + 8 of step m are dims 16 gid + 2m,
+  // +1, so each lane decodes 16 consecutive dims of tokens 2 tig, 2 tig + 1,
+  // 2 tig + 8, 2 tig + 9 and the k pairs of the A fragments come from
+  // byte permutes of two tokens' word pairs.
+  uint32_t uses = 0;  // S^T fragments taken
+  AttnPos p;
+  p.next();
   for (uint32_t item = i_begin; item < i_end; ++item) {
     const AttnItem& I = b.item[item];
-    // Q^T fragments (B operand of S^T = K Q^T): Q[q head gid][dims 16k + 2*tig (+8)]
-    uint32_t qb[8][2];
-    {
-      const uint16_t* qh = b.req[I.req].q + static_cast<uint64_t>(head * group + gid) * kAttnHeadDim;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        qb[k][0] = gid < group ? *reinterpret_cast<const uint32_t*>(qh + 16 * k + 2 * tig) : 0u;
-        qb[k][1] = gid < group ? *reinterpret_cast<const uint32_t*>(qh + 16 * k + 8 + 2 * tig) : 0u;
-      }
+    const int req = static_cast<int>(I.req);
+    if (req != pair_req) {  // the K warps rebuild the pair table in between
+      attn_consumer_sync();
+      pair_req = req;
+      attn_consumer_sync();
     }
-    float o[8][4];  // O^T per 16 dims: (dim 16m+gid, head 2tig), (.., 2tig+1), (dim +8, 2tig), (dim +8, 2tig+1)
+    float o[8][4];  // O^T: (dim 16 gid + 2m, head 2 tig), (.., 2 tig + 1), (dim + 1, 2 tig), (dim + 1, 2 tig + 1)
 #pragma unroll
     for (int m = 0; m < 8; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
     float mx[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
     for (uint32_t blk = 0; blk < I.blocks; ++blk, ++uses) {
-      // ---- S^T = K Q^T: 16 tokens x 8 head slots, 8 steps of 16 dims
-      wait_stage(&H.full[0], uses & 1, nullptr);
-      const uint32_t valid = H.valid[0];
-      float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd steps
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        // matrices: tokens 0-7 / 8-15 of dims 16kk..+7, then of dims 16kk+8..+15
-        uint32_t a[4];
-        ldmatrix_x4(a, tile_chunk(const_cast<uint8_t*>(tileK), (lane & 7) + ((lane >> 3) & 1) * 8,
-                                  2 * kk + (lane >> 4)));
-        mma_bf16((kk & 1) ? sd : sc, a[0], a[1], a[2], a[3], qb[kk][0], qb[kk][1]);
-      }
+      const uint32_t slot = uses & 1;
+      wait_stage(&H.full[slot], (uses >> 1) & 1, nullptr);
+      const float4 s4 = scores[head][slot][lane];
+      const uint32_t valid = H.valid[slot];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&H.empty[0]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) sc[i] += sd[i];
+      if (lane == 0) mbar_arrive(&H.empty[slot]);
       // ---- online softmax per q head (column) over tokens gid, gid + 8 of all lanes with this tig
       float x[4];
-      x[0] = gid < valid ? sc[0] * b.scale_log2 : -INFINITY;
-      x[1] = gid < valid ? sc[1] * b.scale_log2 : -INFINITY;
-      x[2] = gid + 8 < valid ? sc[2] * b.scale_log2 : -INFINITY;
-      x[3] = gid + 8 < valid ? sc[3] * b.scale_log2 : -INFINITY;
+      x[0] = gid < valid ? s4.x * b.scale_log2 : -INFINITY;
+      x[1] = gid < valid ? s4.y * b.scale_log2 : -INFINITY;
+      x[2] = gid + 8 < valid ? s4.z * b.scale_log2 : -INFINITY;
+      x[3] = gid + 8 < valid ? s4.w * b.scale_log2 : -INFINITY;
       float pe[4], alpha[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -423,32 +527,58 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
       const uint32_t l1 = pack_bf16(pe[2] - __uint_as_float(h1 << 16), pe[3] - __uint_as_float(h1 & 0xFFFF0000u));
       const uint32_t ph0 = movmatrix_trans(h0), ph1 = movmatrix_trans(h1);
       const uint32_t pl0 = movmatrix_trans(l0), pl1 = movmatrix_trans(l1);
-      // ---- O^T += V^T P^T: 8 steps of 16 dims, k = the block's 16 tokens
-      wait_stage(&H.full[1], uses & 1, nullptr);
+      // ---- O^T += V^T P^T
+      consumer_wait(R, p, nullptr);
+      {
+        const AttnDesc& d = D[p.s];
+        const uint8_t* stage = ring + p.s * kAttnStageBytes;
+        const uint32_t dim = head * kAttnHeadDim + 16 * gid;
+        // tokens 2 tig, 2 tig + 1, 2 tig + 8, 2 tig + 9; words past the
+        // context may hold anything (P is 0 there) and are read as 0
+        const uint32_t t0 = 2 * tig, t2 = 2 * tig + 8;
+        const bool k0 = t0 < valid, k1 = t0 + 1 < valid, k2 = t2 < valid, k3 = t2 + 1 < valid;
+        auto mma_step = [&](int m, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
+          v0 = k0 ? v0 : 0u;
+          v1 = k1 ? v1 : 0u;
+          v2 = k2 ? v2 : 0u;
+          v3 = k3 ? v3 : 0u;
+          const uint32_t a0 = __byte_perm(v0, v1, 0x5410), a1 = __byte_perm(v0, v1, 0x7632);
+          const uint32_t a2 = __byte_perm(v2, v3, 0x5410), a3 = __byte_perm(v2, v3, 0x7632);
+          mma_bf16(o[m], a0, a1, a2, a3, ph0, ph1);
+          mma_bf16(o[m], a0, a1, a2, a3, pl0, pl1);
+        };
+        if (d.mode == 3) {
+          uint32_t L0[4], C0[3], L1[4], C1[3], L2[4], C2[3], L3[4], C3[3];
+          fixed6_load<8>(d, stage, t0, dim, L0, C0);
+          fixed6_load<8>(d, stage, t0 + 1, dim, L1, C1);
+          fixed6_load<8>(d, stage, t2, dim, L2, C2);
+          fixed6_load<8>(d, stage, t2 + 1, dim, L3, C3);
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        // matrices: tokens 0-7 of dims 16m / 16m+8, then tokens 8-15 of dims 16m / 16m+8
-        uint32_t a[4];
-        ldmatrix_x4_trans(a, tile_chunk(const_cast<uint8_t*>(tileV), (lane & 7) + (lane >> 4) * 8,
-                                        2 * m + ((lane >> 3) & 1)));
-        mma_bf16(o[m], a[0], a[1], a[2], a[3], ph0, ph1);
-        mma_bf16(o[m], a[0], a[1], a[2], a[3], pl0, pl1);
+          for (int m = 0; m < 8; ++m)
+            mma_step(m, fixed6_word_pair<8>(pairs, L0, C0, m), fixed6_word_pair<8>(pairs, L1, C1, m),
+                     fixed6_word_pair<8>(pairs, L2, C2, m), fixed6_word_pair<8>(pairs, L3, C3, m));
+        } else if (d.mode == 6) {
+#pragma unroll
+          for (int m = 0; m < 8; ++m)
+            mma_step(m, raw_word_pair(d, stage, t0, dim, m), raw_word_pair(d, stage, t0 + 1, dim, m),
+                     raw_word_pair(d, stage, t2, dim, m), raw_word_pair(d, stage, t2 + 1, dim, m));
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&H.empty[1]);
+      consumer_release(R, p);
+      p.next();
+      p.next();
     }
-    // partial of the item: O^T columns of the group's heads, m and l
+    // partial of the item: O^T columns of the group's heads (dims 16 gid .. 16 gid + 15 per lane), m and l
     float* base = b.partials + static_cast<uint64_t>(item) * kAttnKvHeads * group * kAttnRecord;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const uint32_t hcol = 2 * tig + e;
       if (hcol < group) {
         float* dst = base + static_cast<uint64_t>(head * group + hcol) * kAttnRecord;
+        float4* row = reinterpret_cast<float4*>(dst + 16 * gid);
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          dst[16 * m + gid] = o[m][e];
-          dst[16 * m + gid + 8] = o[m][2 + e];
-        }
+        for (int j = 0; j < 4; ++j)
+          row[j] = make_float4(o[2 * j][e], o[2 * j][2 + e], o[2 * j + 1][e], o[2 * j + 1][2 + e]);
         if (gid == 0) {
           dst[kAttnHeadDim] = mx[e];
           dst[kAttnHeadDim + 1] = lsum[e];
