@@ -198,6 +198,35 @@ KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_splitzip_job* jo
                                                       unsigned long long count,
                                                       unsigned long long stream_ptr);
 
+/* ---- calibration (GPU form of the exponent-histogram trace that the
+ * reference's top16 codebooks come from: vllm_connector.py:2871-2904 counts
+ * (w >> 7) & 0xFF per plane with torch.bincount, trace.py:27-58 and
+ * scripts/extract_llama_top16_codebooks.py:39-40 rank them). */
+
+/* Exponent histograms of a batch of jobs.  Per job, `stream_ptr` points to
+ * 2 x 256 uint32 counters (K plane, then V; stream_bytes >= 2048, 4-byte
+ * aligned) to which the counts of the job's words are added; `tables_ptr`
+ * is not used.  Returns the number of jobs, 0 if declined, -1 on a CUDA
+ * error. */
+KVQ_API long long kvq_splitzip_bf16_exponent_histogram_batch(const kvq_splitzip_job* jobs,
+                                                             unsigned long long count,
+                                                             unsigned long long stream_ptr);
+
+/* Top16 device tables of `layers` layers from their histograms
+ * (layers x 2 x 256 uint32): per plane the 16 most frequent observed
+ * exponents ranked by (-count, exponent), code = rank, written as the
+ * 544-byte table the encoders take (layers x 544 bytes at tables_ptr; the
+ * layout of splitzip_cuda.py:283-298).  observed_ptr receives layers x 2
+ * uint32: the exponents with a nonzero count per plane.  With fewer than
+ * 16, the remaining codes take the unobserved exponents in ascending order
+ * (the reference's extractor rejects such a layer).  Returns layers, 0 if
+ * declined, -1 on a CUDA error. */
+KVQ_API long long kvq_splitzip_top16_tables_from_histograms(unsigned long long hist_ptr,
+                                                           unsigned long long layers,
+                                                           unsigned long long tables_ptr,
+                                                           unsigned long long observed_ptr,
+                                                           unsigned long long stream_ptr);
+
 /* Count of device-side bounded waits that ran out on the current device
  * since load (0 in normal operation).  Synchronous; -1 on CUDA error. */
 KVQ_API long long kvq_splitzip_device_errors(void);

@@ -21,7 +21,8 @@ imported from its source tree:
   (fixed6) and mode-4 (fixed5) receivers -> decoded caches of oracle-encoded
   fixed streams;
 * ``unchain_kv.trace.summarize_symbol_counts`` (src/unchain_kv/trace.py:27-58),
-  the palette ranking rule -> top-16 exponent lists of seeded histograms.
+  the palette ranking rule -> top-16 exponent lists of seeded histograms and
+  the whole summary the calibration trace records for them.
 
 The streams themselves come from the CPU oracle (oracle/splitzip_oracle.c);
 storing them pins the oracle's canonical bytes against regressions, while the
@@ -195,7 +196,7 @@ def main() -> None:
         hist[local.choice(256, size=40, replace=False)] = local.integers(1, 50, size=40)
         hist[local.choice(256, size=6, replace=False)] = 17  # ties
         summary = summarize_symbol_counts(hist.tolist())
-        rankings.append({"histogram": hist.tolist(), "top16": summary["top16_exponents"]})
+        rankings.append({"histogram": hist.tolist(), "top16": summary["top16_exponents"], "summary": summary})
     out["rankings"] = rankings
 
     np.savez_compressed(HERE / "golden.npz", **arrays)

@@ -135,3 +135,11 @@ def test_multithreaded_oracle_matches_single_thread():
                                          0, 25, out.ctypes.data, out.size, tables.ctypes.data, 4)
     assert res == single.size
     assert np.array_equal(out[:res], single)
+
+
+def test_exponent_summary_matches_reference():
+    """The calibration trace summary (trace.py:27-58 of the reference)."""
+    from unchainkv_b200 import splitzip_cuda
+
+    for row in META["rankings"]:
+        assert splitzip_cuda.summarize_symbol_counts(row["histogram"]) == row["summary"]

@@ -664,6 +664,69 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_split
   return decode_batch<0>(jobs, count, reinterpret_cast<cudaStream_t>(stream_ptr));
 }
 
+// -------------------------------------------------------------- calibration
+
+namespace {
+
+template <int kMax>
+long long launch_histograms(const std::vector<EncJob>& jobs, size_t first, size_t count, cudaStream_t stream) {
+  EncBatch<kMax> b{};
+  b.jobs = static_cast<uint32_t>(count);
+  uint32_t tiles = 0;
+  for (size_t i = 0; i < count; ++i) {
+    b.tile_start[i] = tiles;
+    b.job[i] = jobs[first + i];
+    tiles += b.job[i].tiles;
+  }
+  b.tile_start[count] = tiles;
+  return launch_persistent(ExpHistogramKernel<kMax>, "ExpHistogramKernel", kEncSmemBytes, b, tiles, stream);
+}
+
+}  // namespace
+
+extern "C" KVQ_API long long kvq_splitzip_bf16_exponent_histogram_batch(const kvq_splitzip_job* jobs,
+                                                                       unsigned long long count,
+                                                                       unsigned long long stream_ptr) {
+  if (!jobs || count == 0) return 0;
+  const auto stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  std::vector<EncJob> prepared(count);
+  for (unsigned long long i = 0; i < count; ++i) {
+    const kvq_splitzip_job& j = jobs[i];
+    if (!job_shape_ok(j) || j.stream_bytes < 2048 || j.stream_ptr % 4) return 0;
+    const Layout L = job_layout(j);
+    if (L.n == 0 || L.n > 0xFFFFFFFFULL) return 0;
+    prepared[i] = base_job(reinterpret_cast<const uint16_t*>(j.cache_ptr), L, reinterpret_cast<uint8_t*>(j.stream_ptr),
+                           nullptr);
+  }
+  if (count == 1) {
+    const long long rc = launch_histograms<1>(prepared, 0, 1, stream);
+    return rc < 0 ? rc : 1;
+  }
+  for (size_t first = 0; first < count; first += kMaxBatch) {
+    const long long rc = launch_histograms<kMaxBatch>(prepared, first, std::min<size_t>(kMaxBatch, count - first), stream);
+    if (rc < 0) return rc;
+  }
+  return static_cast<long long>(count);
+}
+
+extern "C" KVQ_API long long kvq_splitzip_top16_tables_from_histograms(unsigned long long hist_ptr,
+                                                                      unsigned long long layers,
+                                                                      unsigned long long tables_ptr,
+                                                                      unsigned long long observed_ptr,
+                                                                      unsigned long long stream_ptr) {
+  if (!hist_ptr || !tables_ptr || !observed_ptr || layers == 0 || layers > (1ULL << 20) || hist_ptr % 4 ||
+      observed_ptr % 4)
+    return 0;
+  const auto stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  const long long prof = prof_begin(stream);
+  Top16TablesKernel<<<static_cast<unsigned>(layers), 256, 0, stream>>>(
+      reinterpret_cast<const uint32_t*>(hist_ptr), static_cast<uint32_t>(layers), reinterpret_cast<uint8_t*>(tables_ptr),
+      reinterpret_cast<uint32_t*>(observed_ptr));
+  prof_end(prof, "Top16TablesKernel", stream);
+  const cudaError_t st = cudaGetLastError();
+  return st == cudaSuccess ? static_cast<long long>(layers) : Fail("Top16TablesKernel", st);
+}
+
 // ---------------------------------------------------------------- attention
 
 namespace {

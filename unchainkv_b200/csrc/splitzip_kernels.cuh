@@ -1140,6 +1140,123 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   }, prefix_hook);
 }
 
+// ------------------------------------------------------------ calibration
+//
+// Exponent histogram of each job's words per plane: counter
+// plane * 256 + ((w >> 7) & 0xFF) of the job's 2 x 256 u32 counters (EncJob::dst)
+// grows by the words with that exponent byte; counts accumulate over calls.
+// The reference computes the same counts with torch.bincount on the packed
+// layer for its trace (vllm_connector.py:2871-2904) and ranks them into the
+// top16 codebooks (trace.py:27-58).  Here the gather is fused: the producer
+// warp stages the job's tiles from the paged cache by TMA, and each consumer
+// warp counts into its own shared histogram with shared-memory atomics,
+// adding its nonzero bins to the job's counters when its job changes and at
+// the end (no CTA-wide synchronisation).
+template <int kMax>
+__global__ void __launch_bounds__(kCtaThreads, 2) ExpHistogramKernel(const __grid_constant__ EncBatch<kMax> b) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint32_t whist[kWarps][512];
+  __shared__ EncRing R;
+  __shared__ EncDesc D[kEncStages];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  for (int i = tid; i < kWarps * 512; i += kCtaThreads) (&whist[0][0])[i] = 0;
+  ring_init(R);
+  __syncthreads();
+  uint32_t* mine = whist[warp & (kWarps - 1)];
+  int hist_job = -1;
+  auto flush = [&](const EncJob& P) {
+    __syncwarp();
+    uint32_t* out = reinterpret_cast<uint32_t*>(P.dst);
+    for (int i = lane; i < 512; i += 32) {
+      const uint32_t c = mine[i];
+      if (c) {
+        atomicAdd(out + i, c);
+        mine[i] = 0;
+      }
+    }
+    __syncwarp();
+  };
+  encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
+                                           const EncPos&, const EncDesc&) {
+    if (j != hist_job) {
+      if (hist_job >= 0) flush(b.job[hist_job]);
+      hist_job = j;
+    }
+    const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
+    const uint32_t len = tile_len(J.n, t0);
+    if (len == kTileWords && (t0 >= J.half || t0 + kTileWords <= J.half)) {
+      const uint32_t poff = t0 >= J.half ? 256u : 0u;
+#pragma unroll
+      for (int s = 0; s < kStepsPerWarp; ++s) {
+        const uint16_t* w = sin + (warp * kStepsPerWarp + s) * kStepWords + 8 * lane;
+        const uint4 v0 = *reinterpret_cast<const uint4*>(w);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(w + 256);
+        const uint32_t x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          atomicAdd(mine + (((x[q] >> 7) & 0xFFu) | poff), 1u);
+          atomicAdd(mine + (((x[q] >> 23) & 0xFFu) | poff), 1u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int s = 0; s < kStepsPerWarp; ++s) {
+        const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
+        if (w0 >= len) continue;
+        const uint32_t valid = min(len - w0, static_cast<uint32_t>(kUnitWords));
+        const uint64_t g = t0 + w0;
+        for (uint32_t i = 0; i < valid; ++i)
+          atomicAdd(mine + (((g + i) >= J.half ? 256u : 0u) | ((sin[w0 + i] >> 7) & 0xFFu)), 1u);
+      }
+    }
+  });
+  if (warp == kProducerWarp) return;
+  if (hist_job >= 0) flush(b.job[hist_job]);
+}
+
+// Top16 tables from exponent histograms, one CTA per layer: per plane the
+// 16 most frequent observed exponents ranked by (-count, exponent), code =
+// rank (trace.py:30-33, scripts/extract_llama_top16_codebooks.py:39-40),
+// then the layer's 544-byte table as the reference builds it from its
+// codebooks (splitzip_cuda.py:283-298): [0,256) K exponent -> code (255 =
+// escape), [256,512) V, [512,528) K codebook, [528,544) V codebook.
+// observed[2 layer + plane] = exponents with a nonzero count; with fewer
+// than 16 the remaining codes take the unobserved exponents in ascending
+// order (the reference's extractor rejects such a layer; the host decides).
+__global__ void __launch_bounds__(256) Top16TablesKernel(const uint32_t* __restrict__ hist, uint32_t layers,
+                                                         uint8_t* tables, uint32_t* observed) {
+  __shared__ uint32_t cnt[256];
+  __shared__ uint8_t book[16];
+  const uint32_t layer = blockIdx.x;
+  if (layer >= layers) return;
+  const int e = threadIdx.x;
+  uint8_t* T = tables + static_cast<uint64_t>(layer) * 544;
+  for (int plane = 0; plane < 2; ++plane) {
+    cnt[e] = hist[(static_cast<uint64_t>(layer) * 2 + plane) * 256 + e];
+    __syncthreads();
+    const uint32_t c = cnt[e];
+    uint32_t rank = 0, below_unseen = 0, seen = 0;
+    for (int k = 0; k < 256; ++k) {
+      const uint32_t ck = cnt[k];
+      rank += (ck > c) || (ck == c && k < e);
+      below_unseen += ck == 0 && k < e;
+      seen += ck != 0;
+    }
+    if (c > 0 && rank < 16) book[rank] = static_cast<uint8_t>(e);
+    if (c == 0 && seen + below_unseen < 16) book[seen + below_unseen] = static_cast<uint8_t>(e);
+    T[plane * 256 + e] = 255;
+    if (e == 0) observed[layer * 2 + plane] = seen;
+    __syncthreads();
+    if (e < 16) {
+      T[plane * 256 + book[e]] = static_cast<uint8_t>(e);
+      T[512 + plane * 16 + e] = book[e];
+    }
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------------ decode
 //
 // Producer warp per tile: reads the job's mode byte (once per job), stages

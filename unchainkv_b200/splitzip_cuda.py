@@ -23,6 +23,7 @@ Differences, all additive:
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 import threading
 from pathlib import Path
@@ -70,6 +71,7 @@ _SIGNATURES = {
     "kvq_splitzip_bf16_encode_top16_blocks": [_U64] * 11,
     "kvq_splitzip_bf16_encode_mode_blocks": [_U64] * 10 + [ctypes.c_int],
     "kvq_splitzip_bf16_encode_top16_noalloc": [_U64] * 6,
+    "kvq_splitzip_top16_tables_from_histograms": [_U64] * 5,
     "kvq_splitzip_device_errors": [],
     "kvq_splitzip_abi_version": [],
 }
@@ -80,6 +82,7 @@ _BATCH_SIGNATURES = {
     "kvq_splitzip_bf16_decode_top16_batch": None,
     "kvq_splitzip_bf16_decode_fixed6_batch": None,
     "kvq_splitzip_bf16_decode_auto_batch": None,
+    "kvq_splitzip_bf16_exponent_histogram_batch": None,
 }
 
 
@@ -712,6 +715,90 @@ def decode_fixed6_batch(jobs, stream=None) -> int | None:
 def decode_auto_batch(jobs, stream=None) -> int | None:
     """Decode each job's stream by its mode byte (5, 3 or 6) on the device."""
     return _run_batch("kvq_splitzip_bf16_decode_auto_batch", jobs, stream)
+
+
+# ------------------------------------------------------------ calibration
+#
+# GPU form of the reference's exponent trace (vllm_connector.py:2871-2904)
+# and of its codebook ranking (trace.py:27-58,
+# scripts/extract_llama_top16_codebooks.py:39-40): histograms of
+# (w >> 7) & 0xFF per plane, gathered from the paged cache on the device,
+# then the top16 tables built on the device, so palettes can be calibrated
+# online without a host round trip.
+
+
+def histogram_job(kv_layer, block_ids, hist, block_start: int = 0, block_count: int | None = None) -> KvqJob:
+    """A calibration job: the layer's blocks (as ``make_job``) counted into
+    ``hist``, a [2, 256] int32 device tensor (K plane, then V)."""
+    if hist.dtype.itemsize != 4 or hist.numel() != 512 or not hist.is_contiguous():
+        raise ValueError("hist must be a contiguous [2, 256] 32-bit tensor")
+    return make_job(kv_layer, block_ids, hist, 2048, None, block_start, block_count)
+
+
+def exponent_histogram_batch(jobs, stream=None) -> int | None:
+    """Add the exponent counts of every job's words to its histogram (one
+    launch; counts accumulate across calls).  Returns the number of jobs,
+    None if any job is declined (nothing launched)."""
+    return _run_batch("kvq_splitzip_bf16_exponent_histogram_batch", jobs, stream)
+
+
+def top16_tables_from_histograms(hist, tables=None, observed=None, stream=None):
+    """Top16 device tables of ``hist`` ([layers, 2, 256] int32 counts):
+    returns (tables [layers, 544] uint8, observed [layers, 2] int32), the
+    tables in the layout ``_top16_tables`` gives and ``observed`` the number
+    of exponents with a nonzero count per plane.  A plane with fewer than
+    16 gets the unobserved exponents in ascending order as its last codes."""
+    lib = _require_lib()
+    import torch
+
+    if hist.dim() != 3 or tuple(hist.shape[1:]) != (2, 256) or hist.dtype.itemsize != 4 or not hist.is_contiguous():
+        raise ValueError("hist must be a contiguous [layers, 2, 256] 32-bit tensor")
+    layers = int(hist.shape[0])
+    if tables is None:
+        tables = torch.empty((layers, 544), dtype=torch.uint8, device=hist.device)
+    if observed is None:
+        observed = torch.empty((layers, 2), dtype=torch.int32, device=hist.device)
+    if stream is None:
+        stream = torch.cuda.current_stream(hist.device).cuda_stream
+    result = lib.kvq_splitzip_top16_tables_from_histograms(
+        int(hist.data_ptr()), layers, int(tables.data_ptr()), int(observed.data_ptr()), int(stream))
+    if result < 0:
+        _raise_last(lib, "kvq_splitzip_top16_tables_from_histograms failed")
+    if result == 0:
+        return None
+    return tables, observed
+
+
+def codebooks_from_tables(tables, observed) -> bytes:
+    """The 32 codebook bytes per layer (K then V) of device tables, for
+    ``register_top16_codebooks``.  Like the reference's extractor, raises
+    ValueError when a plane has fewer than 16 observed exponents."""
+    seen = observed.cpu().tolist()
+    for layer, planes in enumerate(seen):
+        for plane, count in zip("kv", planes):
+            if count < 16:
+                raise ValueError(f"layer {layer} {plane} has only {count} observed exponents")
+    return bytes(tables[:, 512:544].contiguous().cpu().numpy().tobytes())
+
+
+def summarize_symbol_counts(counts) -> dict:
+    """The exponent summary the reference's trace records for a 256-bin
+    histogram (trace.py:27-58): words, histogram, distinct exponents,
+    entropy in bits, and for the top 8 and 16 exponents by (-count,
+    exponent) the list, the covered fraction and the escapes."""
+    histogram = [int(v) for v in counts]
+    words = sum(histogram)
+    order = sorted((e for e, c in enumerate(histogram) if c > 0), key=lambda e: (-histogram[e], e))
+    # sum() of floats is compensated (as the trace's own summary is)
+    entropy = -sum((c / words) * math.log2(c / words) for c in histogram if c > 0) if words else 0.0
+    summary = {"words": words, "histogram": histogram, "unique_exponents": len(order), "entropy_bits": entropy}
+    for k in (8, 16):
+        covered = sum(histogram[e] for e in order[:k])
+        summary[f"top{k}_exponents"] = order[:k]
+        summary[f"top{k}_coverage"] = covered / words if words else 0.0
+        summary[f"top{k}_escape_count"] = words - covered
+        summary[f"top{k}_escape_rate"] = (words - covered) / words if words else 0.0
+    return summary
 
 
 # --------------------------------------------------------------- profiler
