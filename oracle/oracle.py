@@ -46,6 +46,8 @@ def lib():
             "orc_decode_fixed6_blocks_mt": (_i64, [_vp, _u64, _vp, _u64, _u64, _u64, _u64, _u64, _u64, _vp, ctypes.c_int]),
             "orc_decode_top16_blocks_mt": (_i64, [_vp, _u64, _vp, _u64, _u64, _u64, _u64, _u64, _u64, _vp, _vp, ctypes.c_int]),
             "orc_max_threads": (ctypes.c_int, []),
+            "orc_encode_torchop_blocks": (_i64, [_vp, _u64, _u64, _u64, _vp, _u64, _u64, _vp, _u64]),
+            "orc_decode_modes_blocks": (_i64, [_vp, _u64, _vp, _u64, _u64, _u64, _u64, _u64, _vp]),
         }
         for name, (restype, argtypes) in sigs.items():
             fn = getattr(handle, name)
@@ -158,6 +160,32 @@ def decode_fixed6_blocks(stream, cache, block_ids, block_start: int = 0):
     return int(lib().orc_decode_fixed6_blocks(
         _ptr(stream), stream.size, _ptr(cache), n, len(ids), block_words,
         plane_stride, block_words, block_start, _ptr(ids)))
+
+
+def encode_torchop_blocks(cache, block_ids, block_start: int = 0):
+    """The reference's torch-op encoder (modes 2, 0, 1 in that order) over the
+    blocks; (length, stream), length 0 when no form is smaller than raw."""
+    cache = _u16(cache)
+    plane_stride = int(np.prod(cache.shape[1:]))
+    block_words = int(np.prod(cache.shape[2:]))
+    ids = np.ascontiguousarray(block_ids, dtype=np.int64)
+    n = 2 * len(ids) * block_words
+    out = np.zeros(2 * n + 512, dtype=np.uint8)
+    result = lib().orc_encode_torchop_blocks(
+        _ptr(cache), plane_stride, block_words, block_words, _ptr(ids), block_start, len(ids), _ptr(out), out.size)
+    return int(result), out[: max(int(result), 0)]
+
+
+def decode_modes_blocks(stream, cache, block_ids, block_start: int = 0):
+    """Receiver decode of a mode 0/1/2/4 stream into ``cache`` (in place);
+    returns 2n, or 0 when the stream is declined."""
+    stream = np.ascontiguousarray(stream, dtype=np.uint8)
+    plane_stride = int(np.prod(cache.shape[1:]))
+    block_words = int(np.prod(cache.shape[2:]))
+    ids = np.ascontiguousarray(block_ids, dtype=np.int64)
+    return int(lib().orc_decode_modes_blocks(
+        _ptr(stream), stream.size, _ptr(cache), len(ids), block_words, plane_stride, block_words,
+        block_start, _ptr(ids)))
 
 
 def max_threads() -> int:

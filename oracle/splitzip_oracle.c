@@ -12,6 +12,8 @@
  *   fixed6/fixed5  native/unchain_kv/kvq_splitzip_cuda.cu:20-144, 292-379
  *   gather         src/unchain_kv/vllm_connector.py:2827-2869 (index_select over dim 1)
  *   CPU decoder    src/unchain_kv/vllm_connector.py:176-220
+ *   modes 0/1/2    src/unchain_kv/vllm_connector.py:3204-3366 (encoder, packing),
+ *   and fixed5     5168-5278 (receiver)
  *
  * Canonical form.  The reference GPU encoder is nondeterministic in three
  * places: escape-entry order (atomicAdd slot, .cu:177), unused escape slots
@@ -573,4 +575,203 @@ int orc_max_threads(void) {
 #else
   return 1;
 #endif
+}
+
+/* ------------------------------------------- receiver modes 0, 1, 2 and 4 */
+/*
+ * The reference's torch-op codec (the connector's path for tensors the CUDA
+ * library does not take): encoder src/unchain_kv/vllm_connector.py:3204-3343,
+ * bit packing :3345-3366, receiver :5168-5278.  Codes are packed LSB first:
+ * code i of width w sits at bits [i*w, i*w + w) of the plane.
+ *
+ * The encoder tries, in order, and keeps the first form smaller than raw:
+ *   mode 2, sign/magnitude, when the 7-bit magnitudes of the high bytes span
+ *     fewer than 7 bits: [0]=2 [1]=width [2]=min magnitude, the n low bytes,
+ *     n sign bits, n (magnitude - min) fields of `width` bits;
+ *   mode 0, palette of the distinct high bytes, when it has at most 128
+ *     entries: [0]=0 [1]=width=max(1, bitlen(distinct-1)) [2,258) the
+ *     distinct high bytes ascending then zeros, the n low bytes, n codes;
+ *   mode 1, nibble planes: [0]=1 [1,5) the widths of nibbles 0-3 (bits 0-3,
+ *     4-7, 8-11, 12-15; 1 for <= 2 distinct values, 2 for <= 4, else 4),
+ *     [5,69) four 16-byte palettes (distinct nibble values ascending, then
+ *     zeros), then the four code planes.
+ * Returns the stream length, or 0 when no form is smaller than raw.
+ */
+static inline uint32_t bitlen32(uint32_t v) {
+  uint32_t b = 0;
+  while (v) { ++b; v >>= 1; }
+  return b;
+}
+
+static void put_bits(uint8_t* plane, uint64_t i, uint32_t width, uint32_t code) {
+  const uint64_t bit = i * width;
+  uint32_t v = code << (bit % 8);
+  uint8_t* p = plane + bit / 8;
+  for (uint32_t k = 0; k * 8 < (bit % 8) + width; ++k) p[k] |= (uint8_t)(v >> (8 * k));
+}
+
+static uint32_t get_bits(const uint8_t* plane, uint64_t i, uint32_t width) {
+  const uint64_t bit = i * width;
+  const uint8_t* p = plane + bit / 8;
+  uint32_t v = 0;
+  for (uint32_t k = 0; k * 8 < (bit % 8) + width; ++k) v |= (uint32_t)p[k] << (8 * k);
+  return (v >> (bit % 8)) & ((1u << width) - 1u);
+}
+
+static int64_t torchop_encode_layout(const uint16_t* src, const orc_layout* l, uint8_t* dst,
+                                     uint64_t capacity) {
+  const uint64_t n = l->n, raw = 2 * n;
+  uint32_t mag_min = 127, mag_max = 0;
+  uint8_t seen[256] = {0};
+  for (uint64_t i = 0; i < n; ++i) {
+    const uint32_t high = src[orc_addr(l, i)] >> 8, mag = high & 0x7F;
+    if (mag < mag_min) mag_min = mag;
+    if (mag > mag_max) mag_max = mag;
+    seen[high] = 1;
+  }
+  uint32_t width = bitlen32(mag_max - mag_min);
+  if (width < 1) width = 1;
+  if (width < 7) {
+    const uint64_t sign_bytes = (n + 7) / 8, mag_bytes = (n * width + 7) / 8;
+    const uint64_t encoded = 3 + n + sign_bytes + mag_bytes;
+    if (encoded < raw) {
+      if (encoded > capacity) return 0;
+      memset(dst, 0, encoded);
+      dst[0] = 2;
+      dst[1] = (uint8_t)width;
+      dst[2] = (uint8_t)mag_min;
+      uint8_t* sign = dst + 3 + n;
+      uint8_t* mags = sign + sign_bytes;
+      for (uint64_t i = 0; i < n; ++i) {
+        const uint16_t w = src[orc_addr(l, i)];
+        dst[3 + i] = (uint8_t)(w & 0xFF);
+        put_bits(sign, i, 1, w >> 15);
+        put_bits(mags, i, width, ((w >> 8) & 0x7F) - mag_min);
+      }
+      return (int64_t)encoded;
+    }
+  }
+  uint8_t rank[256];
+  uint32_t distinct = 0;
+  for (uint32_t h = 0; h < 256; ++h)
+    if (seen[h]) rank[h] = (uint8_t)distinct++;
+  width = bitlen32(distinct - 1);
+  if (width < 1) width = 1;
+  if (width < 8) {
+    const uint64_t encoded = 258 + n + (n * width + 7) / 8;
+    if (encoded < raw) {
+      if (encoded > capacity) return 0;
+      memset(dst, 0, encoded);
+      dst[1] = (uint8_t)width;
+      for (uint32_t h = 0; h < 256; ++h)
+        if (seen[h]) dst[2 + rank[h]] = (uint8_t)h;
+      uint8_t* codes = dst + 258 + n;
+      for (uint64_t i = 0; i < n; ++i) {
+        const uint16_t w = src[orc_addr(l, i)];
+        dst[258 + i] = (uint8_t)(w & 0xFF);
+        put_bits(codes, i, width, rank[w >> 8]);
+      }
+      return (int64_t)encoded;
+    }
+  }
+  uint8_t nseen[4][16] = {{0}}, nrank[4][16];
+  uint32_t nw[4], nsize[4];
+  uint64_t encoded = 69;
+  for (uint64_t i = 0; i < n; ++i) {
+    const uint16_t w = src[orc_addr(l, i)];
+    for (int p = 0; p < 4; ++p) nseen[p][(w >> (4 * p)) & 0xF] = 1;
+  }
+  for (int p = 0; p < 4; ++p) {
+    uint32_t d = 0;
+    for (uint32_t v = 0; v < 16; ++v)
+      if (nseen[p][v]) nrank[p][v] = (uint8_t)d++;
+    nw[p] = d <= 2 ? 1 : d <= 4 ? 2 : 4;
+    nsize[p] = (uint32_t)((n * nw[p] + 7) / 8);
+    encoded += nsize[p];
+  }
+  if (encoded >= raw || encoded > capacity) return 0;
+  memset(dst, 0, encoded);
+  dst[0] = 1;
+  uint8_t* plane = dst + 69;
+  for (int p = 0; p < 4; ++p) {
+    dst[1 + p] = (uint8_t)nw[p];
+    for (uint32_t v = 0; v < 16; ++v)
+      if (nseen[p][v]) dst[5 + 16 * p + nrank[p][v]] = (uint8_t)v;
+    for (uint64_t i = 0; i < n; ++i)
+      put_bits(plane, i, nw[p], nrank[p][(src[orc_addr(l, i)] >> (4 * p)) & 0xF]);
+    plane += nsize[p];
+  }
+  return (int64_t)encoded;
+}
+
+int64_t orc_encode_torchop_blocks(const uint16_t* cache, uint64_t plane_stride,
+                                  uint64_t block_words, uint64_t block_stride,
+                                  const int64_t* block_ids, uint64_t block_start,
+                                  uint64_t block_count, uint8_t* dst,
+                                  uint64_t capacity) {
+  if (!cache || !dst || block_count == 0 || block_words == 0) return 0;
+  orc_layout l = block_layout(block_count, block_words, plane_stride,
+                              block_stride, block_start, block_ids);
+  return torchop_encode_layout(cache, &l, dst, capacity);
+}
+
+/* Receiver decode of modes 0, 1, 2 and 4 (fixed5) into the paged cache,
+ * with the receiver's checks (vllm_connector.py:5168-5278): a header field
+ * out of range or a stream length other than the mode's declines (returns
+ * 0); other modes decline too.  Returns 2n. */
+int64_t orc_decode_modes_blocks(const uint8_t* src, uint64_t encoded_bytes,
+                                uint16_t* dst, uint64_t block_count,
+                                uint64_t block_words, uint64_t plane_stride,
+                                uint64_t block_stride, uint64_t block_start,
+                                const int64_t* block_ids) {
+  if (!src || !dst || block_count == 0 || block_words == 0 || encoded_bytes == 0) return 0;
+  orc_layout l = block_layout(block_count, block_words, plane_stride,
+                              block_stride, block_start, block_ids);
+  const uint64_t n = l.n;
+  const uint8_t mode = src[0];
+  if (mode == 0) {
+    if (encoded_bytes < 258) return 0;
+    const uint32_t width = src[1];
+    if (width < 1 || width >= 8 || encoded_bytes != 258 + n + (n * width + 7) / 8) return 0;
+    for (uint64_t i = 0; i < n; ++i)
+      dst[orc_addr(&l, i)] =
+          (uint16_t)((src[2 + get_bits(src + 258 + n, i, width)] << 8) | src[258 + i]);
+  } else if (mode == 1) {
+    if (encoded_bytes < 69) return 0;
+    uint64_t total = 69;
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t w = src[1 + p];
+      if (w != 1 && w != 2 && w != 4) return 0;
+      total += (n * w + 7) / 8;
+    }
+    if (encoded_bytes != total) return 0;
+    for (uint64_t i = 0; i < n; ++i) {
+      const uint8_t* plane = src + 69;
+      uint32_t word = 0;
+      for (int p = 0; p < 4; ++p) {
+        const uint32_t w = src[1 + p];
+        word |= (uint32_t)src[5 + 16 * p + get_bits(plane, i, w)] << (4 * p);
+        plane += (n * w + 7) / 8;
+      }
+      dst[orc_addr(&l, i)] = (uint16_t)word;
+    }
+  } else if (mode == 2) {
+    const uint32_t width = src[1], mag_min = src[2];
+    if (width < 1 || width >= 7) return 0;
+    const uint64_t sign_bytes = (n + 7) / 8;
+    if (encoded_bytes != 3 + n + sign_bytes + (n * width + 7) / 8) return 0;
+    for (uint64_t i = 0; i < n; ++i) {
+      const uint32_t high = (get_bits(src + 3 + n, i, 1) << 7) |
+                            (get_bits(src + 3 + n + sign_bytes, i, width) + mag_min);
+      dst[orc_addr(&l, i)] = (uint16_t)((high << 8) | src[3 + i]);
+    }
+  } else if (mode == 4) {
+    if (encoded_bytes != 33 + n + (n * 5 + 7) / 8) return 0;
+    for (uint64_t i = 0; i < n; ++i)
+      dst[orc_addr(&l, i)] =
+          (uint16_t)((src[1 + get_bits(src + 33 + n, i, 5)] << 8) | src[33 + i]);
+  } else {
+    return 0;
+  }
+  return (int64_t)(2 * n);
 }

@@ -20,6 +20,9 @@ imported from its source tree:
   decoder off (src/unchain_kv/vllm_connector.py:5098-5313), the torch mode-3
   (fixed6) and mode-4 (fixed5) receivers -> decoded caches of oracle-encoded
   fixed streams;
+* ``UnchainKVConnector._splitzip_bf16_native_blocks`` on CPU tensors, the
+  torch-op encoder (src/unchain_kv/vllm_connector.py:3204-3366), and the
+  torch receiver -> mode 2 / 0 / 1 streams and their decoded caches;
 * ``unchain_kv.trace.summarize_symbol_counts`` (src/unchain_kv/trace.py:27-58),
   the palette ranking rule -> top-16 exponent lists of seeded histograms and
   the whole summary the calibration trace records for them.
@@ -187,6 +190,58 @@ def main() -> None:
         fixed_cases.append({"name": name, "bits": bits, "blocks": blocks,
                             "block_words": block_words, "pool": pool})
     out["fixed_cases"] = fixed_cases
+
+    # ---- torch-op modes 2 / 0 / 1: the reference's own encoder and receiver
+    # (src/unchain_kv/vllm_connector.py:3204-3366, 5168-5278) on CPU tensors
+    torchop_cases = []
+    saved = {name: os.environ.get(name) for name in ("UNCHAIN_KV_CODEC", "UNCHAIN_KV_CODEC_GPU_SLOTS")}
+    os.environ["UNCHAIN_KV_CODEC"] = "splitzip_bf16"
+    os.environ["UNCHAIN_KV_CODEC_GPU_SLOTS"] = "1"
+    for name, pool, block_words, blocks in (
+        ("mode2_narrow", 12, 512, 7),
+        ("mode0_palette", 10, 1024, 6),
+        ("mode1_nibbles", 9, 768, 5),
+        ("mode2_ragged", 6, 37, 5),
+    ):
+        shape = (2, pool, block_words)
+        if name.startswith("mode2"):
+            high = (rng.integers(0, 2, shape) << 7) | rng.integers(58, 64 + 3 * (name == "mode2_ragged"), shape)
+            low = rng.integers(0, 256, shape)
+        elif name == "mode0_palette":
+            highs = rng.choice(256, size=45, replace=False)
+            high, low = highs[rng.integers(0, 45, shape)], rng.integers(0, 256, shape)
+        else:
+            high, low = rng.integers(0, 256, shape), (rng.integers(0, 256, shape) & 0x31) | 0x04
+        cache = ((high << 8) | low).astype(np.uint16)
+        # the reference gathers a contiguous run of blocks on the CPU (a
+        # scattered list needs its GPU pack pool); its receiver scatters into
+        # a permuted list
+        start = int(rng.integers(0, pool - blocks + 1))
+        src_ids = list(range(start, start + blocks))
+        ids = [int(v) for v in rng.permutation(pool)[:blocks]]
+        connector = ref_connector.UnchainKVConnector(
+            SimpleNamespace(kv_transfer_config=SimpleNamespace(kv_role="kv_producer")), "worker")
+        kv = torch.from_numpy(cache.view(np.int16).copy()).view(torch.bfloat16)
+        encoded = connector._splitzip_bf16_native_blocks(kv, src_ids)
+        assert encoded is not None, name
+        data, _, raw_bytes, encoded_bytes, _ = encoded
+        stream = np.frombuffer(bytes(data), dtype=np.uint8)[:encoded_bytes].copy()
+        target = torch.zeros_like(kv)
+        restored, copied = make_connector()._copy_splitzip_bf16_native_blocks(
+            target, ids, [bytes(stream)], {"raw_bytes": raw_bytes, "encoded_bytes": encoded_bytes})
+        assert (restored, copied) == (blocks, raw_bytes), (name, restored, copied)
+        arrays[f"{name}_cache"] = cache
+        arrays[f"{name}_src_ids"] = np.array(src_ids, dtype=np.int64)
+        arrays[f"{name}_ids"] = np.array(ids, dtype=np.int64)
+        arrays[f"{name}_stream"] = stream
+        arrays[f"{name}_ref_cache"] = target.view(torch.int16).numpy().view(np.uint16).copy()
+        torchop_cases.append({"name": name, "mode": int(stream[0]), "blocks": blocks})
+    for key, value in saved.items():
+        if value is None:
+            os.environ.pop(key, None)
+        else:
+            os.environ[key] = value
+    out["torchop_cases"] = torchop_cases
 
     # ---- palette ranking rule ---------------------------------------------
     rankings = []

@@ -143,3 +143,45 @@ def test_exponent_summary_matches_reference():
 
     for row in META["rankings"]:
         assert splitzip_cuda.summarize_symbol_counts(row["histogram"]) == row["summary"]
+
+
+@pytest.mark.parametrize("case", META["torchop_cases"], ids=lambda c: c["name"])
+def test_torchop_modes_match_reference_encoder_and_receiver(case):
+    """Modes 2 / 0 / 1: the reference's own torch-op encoder produced the
+    stream; the oracle encoder reproduces it byte for byte, and the oracle
+    receiver decodes it to the cache the reference receiver wrote."""
+    name = case["name"]
+    cache = ARRAYS[f"{name}_cache"]
+    stream = ARRAYS[f"{name}_stream"]
+    result, ours = oracle.encode_torchop_blocks(cache, ARRAYS[f"{name}_src_ids"])
+    assert result == stream.size and stream[0] == case["mode"]
+    assert np.array_equal(ours, stream)
+    ref_cache = ARRAYS[f"{name}_ref_cache"]
+    target = np.zeros_like(ref_cache)
+    n = 2 * case["blocks"] * int(np.prod(ref_cache.shape[2:]))
+    assert oracle.decode_modes_blocks(stream, target, ARRAYS[f"{name}_ids"]) == 2 * n
+    assert np.array_equal(target, ref_cache)
+
+
+def test_fixed5_receiver_matches_reference():
+    case = next(c for c in META["fixed_cases"] if c["bits"] == 5)
+    name = case["name"]
+    ref_cache = ARRAYS[f"{name}_ref_cache"]
+    target = np.zeros_like(ref_cache)
+    n = 2 * case["blocks"] * case["block_words"]
+    assert oracle.decode_modes_blocks(ARRAYS[f"{name}_stream"], target, ARRAYS[f"{name}_ids"]) == 2 * n
+    assert np.array_equal(target, ref_cache)
+
+
+def test_receiver_declines_malformed_mode_streams():
+    name = "mode0_palette"
+    stream = ARRAYS[f"{name}_stream"].copy()
+    target = np.zeros_like(ARRAYS[f"{name}_ref_cache"])
+    ids = ARRAYS[f"{name}_ids"]
+    assert oracle.decode_modes_blocks(stream[:-1], target, ids) == 0  # short
+    bad = stream.copy()
+    bad[1] = 8  # width out of range
+    assert oracle.decode_modes_blocks(bad, target, ids) == 0
+    bad[0] = 7  # no such mode
+    assert oracle.decode_modes_blocks(bad, target, ids) == 0
+    assert not target.any()
