@@ -198,6 +198,18 @@ KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_splitzip_job* jo
                                                       unsigned long long count,
                                                       unsigned long long stream_ptr);
 
+/* Decode whichever stream each job holds, in every form the reference's
+ * receiver takes (vllm_connector.py:5098-5313): modes 5, 3 and 6 as
+ * kvq_splitzip_bf16_decode_auto_batch, plus the torch-op forms 0 (palette),
+ * 1 (nibble planes), 2 (sign/magnitude) and 4 (fixed5), for which
+ * stream_bytes must be the exact stream length and the receiver's header
+ * checks apply (vllm_connector.py:5168-5278).  A stream that fails them
+ * leaves its blocks untouched.  Returns the raw bytes of all jobs (2n each),
+ * 0 if declined, -1 on a CUDA error. */
+KVQ_API long long kvq_splitzip_bf16_decode_any_batch(const kvq_splitzip_job* jobs,
+                                                     unsigned long long count,
+                                                     unsigned long long stream_ptr);
+
 /* ---- calibration (GPU form of the exponent-histogram trace that the
  * reference's top16 codebooks come from: vllm_connector.py:2871-2904 counts
  * (w >> 7) & 0xFF per plane with torch.bincount, trace.py:27-58 and

@@ -664,6 +664,61 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_split
   return decode_batch<0>(jobs, count, reinterpret_cast<cudaStream_t>(stream_ptr));
 }
 
+// ------------------------------------------------- every receiver mode
+
+namespace {
+
+template <int kMax>
+long long launch_modes(const std::vector<DecJob>& jobs, size_t first, size_t count, cudaStream_t stream) {
+  static thread_local ModeBatch<kMax> b;
+  b.jobs = static_cast<uint32_t>(count);
+  uint64_t units = 0;
+  for (size_t i = 0; i < count; ++i) {
+    b.unit_start[i] = units;
+    b.job[i] = jobs[first + i];
+    units += (b.job[i].n + kUnitWords - 1) / kUnitWords;
+  }
+  b.unit_start[count] = units;
+  int device = 0, sms = 0;
+  cudaError_t st = cudaGetDevice(&device);
+  if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
+  const uint64_t blocks = std::min<uint64_t>((units + 255) / 256, static_cast<uint64_t>(sms) * 8);
+  const long long prof = prof_begin(stream);
+  ModeDecodeKernel<kMax><<<static_cast<unsigned>(std::max<uint64_t>(blocks, 1)), 256, 0, stream>>>(b);
+  prof_end(prof, "ModeDecodeKernel", stream);
+  st = cudaGetLastError();
+  return st == cudaSuccess ? 0 : Fail("ModeDecodeKernel", st);
+}
+
+}  // namespace
+
+extern "C" KVQ_API long long kvq_splitzip_bf16_decode_any_batch(const kvq_splitzip_job* jobs,
+                                                                unsigned long long count,
+                                                                unsigned long long stream_ptr) {
+  if (!jobs || count == 0) return 0;
+  const auto stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  std::vector<DecJob> prepared(count);
+  for (unsigned long long i = 0; i < count; ++i) {
+    const kvq_splitzip_job& j = jobs[i];
+    if (!job_shape_ok(j) || j.tables_ptr == 0 || j.stream_bytes == 0) return 0;
+    prepare_decode(reinterpret_cast<const uint8_t*>(j.stream_ptr), j.stream_bytes,
+                   reinterpret_cast<uint16_t*>(j.cache_ptr), job_layout(j),
+                   reinterpret_cast<const uint8_t*>(j.tables_ptr), prepared[i]);
+  }
+  // modes 5, 3 and 6 by the staged decoder, modes 0, 1, 2 and 4 by the unit
+  // decoder; each leaves the other's streams alone
+  const long long total = run_decode<0>(prepared, stream);
+  if (total < 0) return total;
+  for (size_t first = 0; first < prepared.size(); first += kMaxBatch) {
+    const size_t n = std::min<size_t>(kMaxBatch, prepared.size() - first);
+    const long long rc = n == 1 && prepared.size() == 1 ? launch_modes<1>(prepared, 0, 1, stream)
+                                                         : launch_modes<kMaxBatch>(prepared, first, n, stream);
+    if (rc < 0) return rc;
+  }
+  return total;
+}
+
 // -------------------------------------------------------------- calibration
 
 namespace {

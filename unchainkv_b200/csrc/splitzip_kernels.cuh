@@ -1793,6 +1793,136 @@ __global__ void __launch_bounds__(kThreads) RepairKernel(const __grid_constant__
 
 // ------------------------------------------------------------------- zero
 
+// --------------------------------------------- receiver modes 0, 1, 2, 4
+//
+// Decode of the reference's torch-op streams (modes 0, 1, 2) and of fixed5
+// (mode 4) into the paged cache, with the receiver's checks
+// (vllm_connector.py:5168-5278; a stream that fails them leaves its blocks
+// untouched).  Every plane of these forms holds a whole number of bytes per
+// 16-word unit (16 codes of w bits are 2w bytes), so one thread decodes one
+// unit from its bytes of each plane, read with aligned 4-byte loads that
+// stay inside the stream; the header (mode, widths, palettes) comes through
+// the read-only cache.  These forms are the receiver's fallbacks (the hot
+// path is modes 5, 3 and 6), so this is a plain grid-stride kernel.
+
+template <int kMax>
+struct ModeBatch {
+  uint32_t jobs;
+  uint64_t unit_start[kMax + 1];
+  DecJob job[kMax];
+};
+
+// Up to 16 bytes at p (nbytes of them defined) as a little-endian bit
+// string in out[0..4] (out[4] = 0 pads the funnel shifts).
+__device__ __forceinline__ void ldg_bytes16(const uint8_t* p, uint32_t nbytes, uint32_t (&out)[5]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
+  const uint32_t lead = static_cast<uint32_t>(a & 3);
+  const uint32_t words = (lead + nbytes + 3) / 4;  // <= 5
+  uint32_t v[6];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) v[k] = static_cast<uint32_t>(k) < words ? __ldg(w + k) : 0u;
+  v[5] = 0;
+#pragma unroll
+  for (int k = 0; k < 5; ++k) out[k] = __funnelshift_r(v[k], v[k + 1], 8 * lead);
+}
+
+// Field i (width w <= 8) of a bit string.
+__device__ __forceinline__ uint32_t bit_field(const uint32_t (&bits)[5], uint32_t i, uint32_t w) {
+  const uint32_t b = i * w, k = b >> 5;  // selects, not a dynamic index (keeps bits in registers)
+  const uint32_t lo = k == 0 ? bits[0] : k == 1 ? bits[1] : k == 2 ? bits[2] : bits[3];
+  const uint32_t hi = k == 0 ? bits[1] : k == 1 ? bits[2] : k == 2 ? bits[3] : bits[4];
+  return __funnelshift_r(lo, hi, b & 31) & ((1u << w) - 1u);
+}
+
+__device__ __forceinline__ uint64_t plane_bytes(uint64_t n, uint32_t w) { return (n * w + 7) / 8; }
+
+template <int kMax>
+__global__ void __launch_bounds__(256) ModeDecodeKernel(const __grid_constant__ ModeBatch<kMax> b) {
+  const uint64_t total = b.unit_start[b.jobs];
+  int j = 0;
+  for (uint64_t u = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < total;
+       u += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    while (u >= b.unit_start[j + 1]) ++j;  // a thread's units increase
+    const DecJob& J = b.job[j];
+    const uint8_t* s = J.src;
+    const uint64_t n = J.n, unit = u - b.unit_start[j], g = kUnitWords * unit;
+    const uint32_t valid = static_cast<uint32_t>(min(n - g, static_cast<uint64_t>(kUnitWords)));
+    const uint32_t mode = __ldg(s);
+    uint32_t hi[kUnitWords];  // high byte (modes 0, 2, 4) or the whole word (mode 1)
+    uint32_t low[5] = {0, 0, 0, 0, 0};
+    if (mode == 0) {
+      const uint32_t w = __ldg(s + 1);
+      if (J.src_bytes < 258 || w < 1 || w >= 8 || J.src_bytes != 258 + n + plane_bytes(n, w)) continue;
+      uint32_t c[5];
+      const uint64_t off = uint64_t{2} * w * unit;
+      ldg_bytes16(s + 258 + n + off, static_cast<uint32_t>(min(uint64_t{2} * w, plane_bytes(n, w) - off)), c);
+      ldg_bytes16(s + 258 + g, valid, low);
+#pragma unroll
+      for (int i = 0; i < kUnitWords; ++i) hi[i] = __ldg(s + 2 + bit_field(c, i, w));
+    } else if (mode == 2) {
+      const uint32_t w = __ldg(s + 1), mag_min = __ldg(s + 2);
+      const uint64_t sign_bytes = (n + 7) / 8;
+      if (J.src_bytes < 3 || w < 1 || w >= 7 || J.src_bytes != 3 + n + sign_bytes + plane_bytes(n, w)) continue;
+      uint32_t sg[5], mg[5];
+      const uint64_t off = uint64_t{2} * w * unit;
+      ldg_bytes16(s + 3 + n + 2 * unit, static_cast<uint32_t>(min(uint64_t{2}, sign_bytes - 2 * unit)), sg);
+      ldg_bytes16(s + 3 + n + sign_bytes + off, static_cast<uint32_t>(min(uint64_t{2} * w, plane_bytes(n, w) - off)), mg);
+      ldg_bytes16(s + 3 + g, valid, low);
+#pragma unroll
+      for (int i = 0; i < kUnitWords; ++i) hi[i] = (bit_field(sg, i, 1) << 7) | (bit_field(mg, i, w) + mag_min);
+    } else if (mode == 4) {
+      if (J.src_bytes != 33 + n + plane_bytes(n, 5)) continue;
+      uint32_t c[5];
+      const uint64_t off = uint64_t{10} * unit;
+      ldg_bytes16(s + 33 + n + off, static_cast<uint32_t>(min(uint64_t{10}, plane_bytes(n, 5) - off)), c);
+      ldg_bytes16(s + 33 + g, valid, low);
+#pragma unroll
+      for (int i = 0; i < kUnitWords; ++i) hi[i] = __ldg(s + 1 + bit_field(c, i, 5));
+    } else if (mode == 1) {
+      if (J.src_bytes < 69) continue;
+      uint32_t w[4];
+      uint64_t total_bytes = 69;
+      bool ok = true;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        w[q] = __ldg(s + 1 + q);
+        ok = ok && (w[q] == 1 || w[q] == 2 || w[q] == 4);
+        total_bytes += plane_bytes(n, w[q]);
+      }
+      if (!ok || J.src_bytes != total_bytes) continue;
+#pragma unroll
+      for (int i = 0; i < kUnitWords; ++i) hi[i] = 0;
+      const uint8_t* plane = s + 69;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t c[5];
+        const uint64_t off = uint64_t{2} * w[q] * unit;
+        ldg_bytes16(plane + off, static_cast<uint32_t>(min(uint64_t{2} * w[q], plane_bytes(n, w[q]) - off)), c);
+#pragma unroll
+        for (int i = 0; i < kUnitWords; ++i) hi[i] |= static_cast<uint32_t>(__ldg(s + 5 + 16 * q + bit_field(c, i, w[q]))) << (4 * q);
+        plane += plane_bytes(n, w[q]);
+      }
+    } else {
+      continue;  // modes 3, 5, 6 belong to DecodeKernel; others are not streams
+    }
+    uint32_t o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t w0, w1;
+      if (mode == 1) {
+        w0 = hi[2 * k];
+        w1 = hi[2 * k + 1];
+      } else {
+        w0 = (hi[2 * k] << 8) | bit_field(low, 2 * k, 8);
+        w1 = (hi[2 * k + 1] << 8) | bit_field(low, 2 * k + 1, 8);
+      }
+      o[k] = (w0 & 0xFFFFu) | (w1 << 16);
+    }
+    store_unit(J.dst, J.L, g, valid, o, J.vec != 0);
+  }
+}
+
 template <int kMax>
 __global__ void __launch_bounds__(kThreads) ZeroKernel(const __grid_constant__ ZeroBatch<kMax> z) {
   for (uint32_t r = blockIdx.y; r < z.count; r += gridDim.y) {

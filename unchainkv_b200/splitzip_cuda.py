@@ -83,6 +83,7 @@ _BATCH_SIGNATURES = {
     "kvq_splitzip_bf16_decode_fixed6_batch": None,
     "kvq_splitzip_bf16_decode_auto_batch": None,
     "kvq_splitzip_bf16_exponent_histogram_batch": None,
+    "kvq_splitzip_bf16_decode_any_batch": None,
 }
 
 
@@ -715,6 +716,15 @@ def decode_fixed6_batch(jobs, stream=None) -> int | None:
 def decode_auto_batch(jobs, stream=None) -> int | None:
     """Decode each job's stream by its mode byte (5, 3 or 6) on the device."""
     return _run_batch("kvq_splitzip_bf16_decode_auto_batch", jobs, stream)
+
+
+def decode_any_batch(jobs, stream=None) -> int | None:
+    """Decode each job's stream whatever its mode: 5, 3 and 6 as
+    ``decode_auto_batch``, and the receiver's other forms (the reference's
+    torch-op modes 0, 1, 2 and fixed5, mode 4) with the receiver's checks.
+    ``stream_bytes`` must be the stream's exact length for modes 0, 1, 2
+    and 4; a stream that fails its checks leaves its blocks untouched."""
+    return _run_batch("kvq_splitzip_bf16_decode_any_batch", jobs, stream)
 
 
 # ------------------------------------------------------------ calibration
