@@ -198,6 +198,17 @@ KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_splitzip_job* jo
                                                       unsigned long long count,
                                                       unsigned long long stream_ptr);
 
+/* The reference's torch-op encoder (vllm_connector.py:3204-3366) on the
+ * GPU: per job the first of sign/magnitude (mode 2), high-byte palette
+ * (mode 0) and nibble planes (mode 1) that is smaller than raw, else raw
+ * (mode 6), chosen on the device from the words' high- and low-byte sets.
+ * Needs stream_bytes >= align16(1 + 2n) + 416 (the plan follows the
+ * largest form).  Returns the sum of 1 + 2n over the jobs; a stream's
+ * length follows from its header. */
+KVQ_API long long kvq_splitzip_bf16_encode_torchop_batch(const kvq_splitzip_job* jobs,
+                                                         unsigned long long count,
+                                                         unsigned long long stream_ptr);
+
 /* Decode whichever stream each job holds, in every form the reference's
  * receiver takes (vllm_connector.py:5098-5313): modes 5, 3 and 6 as
  * kvq_splitzip_bf16_decode_auto_batch, plus the torch-op forms 0 (palette),

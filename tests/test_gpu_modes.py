@@ -146,3 +146,46 @@ def test_malformed_streams_leave_blocks_untouched():
              (nibble, ARRAYS["mode1_nibbles_ref_cache"].shape, ARRAYS["mode1_nibbles_ids"])]
     for got in decode_all(cases):
         assert not got.any()
+
+
+def gpu_torchop(cache, ids):
+    """GPU torch-op encode of `ids` of `cache`; (stream bytes, length)."""
+    kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+    ids_t = dev(np.asarray(ids, dtype=np.int64))
+    n = 2 * len(ids) * int(np.prod(cache.shape[2:]))
+    buf = torch.zeros(S.torchop_capacity(n), dtype=torch.uint8, device="cuda")
+    assert S.encode_torchop_batch([S.make_job(kv, ids_t, buf)]) == 1 + 2 * n
+    torch.cuda.synchronize()
+    out = buf.cpu().numpy()
+    length = S.stream_length(bytes(out[:8]), n)
+    return out[:length], length
+
+
+@pytest.mark.parametrize("name", ["mode2_narrow", "mode0_palette", "mode1_nibbles", "mode2_ragged"])
+def test_gpu_torchop_encoder_reproduces_reference_streams(name):
+    stream, length = gpu_torchop(ARRAYS[f"{name}_cache"], ARRAYS[f"{name}_src_ids"])
+    assert length == ARRAYS[f"{name}_stream"].size
+    assert np.array_equal(stream, ARRAYS[f"{name}_stream"])
+
+
+@pytest.mark.parametrize("kind", ["mode2_w1", "mode2_w3", "mode2_w6", "mode0_2", "mode0_9", "mode0_128", "mode1"])
+def test_gpu_torchop_encoder_matches_oracle_and_round_trips(kind):
+    rng = np.random.Generator(np.random.PCG64(zlib.crc32(kind.encode()) + 1))
+    for block_words in (1024, 96, 13):
+        cache = words_for(kind, rng, (2, 120, block_words))
+        ids = rng.permutation(120)[:100]
+        stream, length = gpu_torchop(cache, ids)
+        result, expected = oracle.encode_torchop_blocks(cache, ids)
+        assert length == result and np.array_equal(stream, expected), (kind, block_words)
+        (got,) = decode_all([(stream, cache.shape, ids)])
+        assert np.array_equal(got[:, ids], cache[:, ids])
+
+
+def test_gpu_torchop_encoder_falls_back_to_raw():
+    rng = np.random.Generator(np.random.PCG64(41))
+    cache = rng.integers(0, 1 << 16, size=(2, 20, 512), dtype=np.uint16)
+    ids = rng.permutation(20)[:11]
+    assert oracle.encode_torchop_blocks(cache, ids)[0] == 0  # the reference sends it raw
+    stream, length = gpu_torchop(cache, ids)
+    assert stream[0] == 6 and length == 1 + 2 * 2 * 11 * 512
+    assert np.array_equal(stream[1:].view(np.uint16), cache[:, ids].reshape(-1))

@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "splitzip_attention.cuh"
+#include "splitzip_torchop.cuh"
 #include "splitzip_kernels.cuh"
 #include "unchain_kv_splitzip.h"
 
@@ -662,6 +663,89 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_split
                                                                  unsigned long long count,
                                                                  unsigned long long stream_ptr) {
   return decode_batch<0>(jobs, count, reinterpret_cast<cudaStream_t>(stream_ptr));
+}
+
+// --------------------------------------------------- torch-op encoder
+
+namespace {
+
+template <int kMax>
+long long launch_torchop(const std::vector<Prepared>& jobs, size_t first, size_t count, cudaStream_t stream) {
+  long long rc = launch_zero<kMax>(jobs, first, count, stream);
+  if (rc < 0) return rc;
+  EncBatch<kMax> e{};
+  e.jobs = static_cast<uint32_t>(count);
+  uint32_t tiles = 0;
+  for (size_t i = 0; i < count; ++i) {
+    e.tile_start[i] = tiles;
+    e.job[i] = jobs[first + i].job;
+    tiles += e.job[i].tiles;
+  }
+  e.tile_start[count] = tiles;
+  rc = launch_persistent(TorchopStatsKernel<kMax>, "TorchopStatsKernel", kEncSmemBytes, e, tiles, stream);
+  if (rc < 0) return rc;
+  long long prof = prof_begin(stream);
+  TorchopDecideKernel<kMax><<<static_cast<unsigned>(count), 32, 0, stream>>>(e);
+  prof_end(prof, "TorchopDecideKernel", stream);
+  cudaError_t st = cudaGetLastError();
+  if (st != cudaSuccess) return Fail("TorchopDecideKernel", st);
+  static thread_local TorchopBatch<kMax> b;
+  b.jobs = e.jobs;
+  uint64_t units = 0;
+  for (size_t i = 0; i < count; ++i) {
+    b.unit_start[i] = units;
+    b.job[i] = e.job[i];
+    b.vec[i] = vec_ok(e.job[i].src, e.job[i].L) ? 1 : 0;
+    units += (e.job[i].n + kUnitWords - 1) / kUnitWords;
+  }
+  b.unit_start[count] = units;
+  int device = 0, sms = 0;
+  st = cudaGetDevice(&device);
+  if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
+  const uint64_t blocks = std::max<uint64_t>(1, std::min<uint64_t>((units + 255) / 256, static_cast<uint64_t>(sms) * 8));
+  prof = prof_begin(stream);
+  TorchopEncodeKernel<kMax><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(b);
+  prof_end(prof, "TorchopEncodeKernel", stream);
+  st = cudaGetLastError();
+  return st == cudaSuccess ? 0 : Fail("TorchopEncodeKernel", st);
+}
+
+}  // namespace
+
+extern "C" KVQ_API long long kvq_splitzip_bf16_encode_torchop_batch(const kvq_splitzip_job* jobs,
+                                                                    unsigned long long count,
+                                                                    unsigned long long stream_ptr) {
+  if (!jobs || count == 0) return 0;
+  const auto stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  std::vector<Prepared> prepared(count);
+  long long total = 0;
+  for (unsigned long long i = 0; i < count; ++i) {
+    const kvq_splitzip_job& j = jobs[i];
+    if (!job_shape_ok(j)) return 0;
+    const Layout L = job_layout(j);
+    auto* dst = reinterpret_cast<uint8_t*>(j.stream_ptr);
+    const uint64_t n = L.n;
+    if (n == 0 || n > 0xFFFFFFFFULL) return 0;
+    const uint64_t so = align16_from(dst, 1 + 2 * n);
+    if (so + kTorchopScratch > j.stream_bytes) return 0;
+    Prepared& p = prepared[i];
+    p.job = base_job(reinterpret_cast<const uint16_t*>(j.cache_ptr), L, dst, nullptr);
+    p.job.scratch = dst + so;
+    p.zero_ptr = p.job.scratch;
+    p.zero_bytes = kTorchopScratch;
+    p.result = 1 + 2 * n;
+    total += static_cast<long long>(p.result);
+  }
+  if (count == 1) {
+    const long long rc = launch_torchop<1>(prepared, 0, 1, stream);
+    return rc < 0 ? rc : total;
+  }
+  for (size_t first = 0; first < count; first += kMaxBatch) {
+    const long long rc = launch_torchop<kMaxBatch>(prepared, first, std::min<size_t>(kMaxBatch, count - first), stream);
+    if (rc < 0) return rc;
+  }
+  return total;
 }
 
 // ------------------------------------------------- every receiver mode

@@ -84,6 +84,7 @@ _BATCH_SIGNATURES = {
     "kvq_splitzip_bf16_decode_auto_batch": None,
     "kvq_splitzip_bf16_exponent_histogram_batch": None,
     "kvq_splitzip_bf16_decode_any_batch": None,
+    "kvq_splitzip_bf16_encode_torchop_batch": None,
 }
 
 
@@ -631,6 +632,30 @@ def stream_bytes(mode: int, n: int) -> int | None:
     return None
 
 
+def stream_length(header: bytes, n: int) -> int | None:
+    """Length of a stream of n words from its first bytes (at least 5), for
+    every form: modes 5, 3, 6 from the mode byte, the torch-op forms 2, 0,
+    1 from their widths, fixed5 (4).  None: not a stream."""
+    mode = header[0]
+    if mode in (5, 3, 6):
+        return stream_bytes(mode, n)
+    if mode == 4:
+        return 33 + n + (5 * n + 7) // 8
+    if mode == 2:
+        return 3 + n + (n + 7) // 8 + (n * header[1] + 7) // 8
+    if mode == 0:
+        return 258 + n + (n * header[1] + 7) // 8
+    if mode == 1:
+        return 69 + sum((n * w + 7) // 8 for w in header[1:5])
+    return None
+
+
+def torchop_capacity(n: int) -> int:
+    """Stream-buffer bytes for encode_torchop_batch: raw mode 6 (the largest
+    form) plus the job's 416-byte plan."""
+    return (1 + 2 * n + 15) // 16 * 16 + 416 + 16
+
+
 def auto_capacity(n: int, raw: bool = True) -> int:
     """Stream-buffer bytes for encode_auto_batch: room for the largest form
     (raw mode 6 when ``raw``) plus the statistics scratch."""
@@ -716,6 +741,15 @@ def decode_fixed6_batch(jobs, stream=None) -> int | None:
 def decode_auto_batch(jobs, stream=None) -> int | None:
     """Decode each job's stream by its mode byte (5, 3 or 6) on the device."""
     return _run_batch("kvq_splitzip_bf16_decode_auto_batch", jobs, stream)
+
+
+def encode_torchop_batch(jobs, stream=None) -> int | None:
+    """The reference's torch-op encoder on the GPU, every job in one batch:
+    the first of sign/magnitude (mode 2), high-byte palette (mode 0) and
+    nibble planes (mode 1) that is smaller than raw, else raw (mode 6).
+    Capacity: ``torchop_capacity(n)``.  Returns the sum of 1 + 2n over the
+    jobs; each stream's length follows from its header (``stream_length``)."""
+    return _run_batch("kvq_splitzip_bf16_encode_torchop_batch", jobs, stream)
 
 
 def decode_any_batch(jobs, stream=None) -> int | None:
