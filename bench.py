@@ -48,9 +48,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("c1", "c2", "c3", "c4"), default="c1",
+    p.add_argument("--workload", choices=("c1", "c2", "c3", "c4", "calib", "modes"), default="c1",
                    help="c1: configs[1] (default); c2: configs[2] per-GPU TP shard; c3: configs[3] mixed batch; "
-                        "c4: configs[4] decode attention over compressed KV")
+                        "c4: configs[4] decode attention over compressed KV; calib: GPU calibration over the "
+                        "configs[1] cache; modes: receiver decode of the torch-op forms")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -279,6 +280,10 @@ def reference_arm(args):
         return
     from unchainkv_b200 import workloads
 
+    if args.workload in ("calib", "modes"):
+        print(json.dumps({"impl": "reference", "unavailable": "auxiliary workload; its line reports the CPU "
+                          "restatement as cpu_baseline"}), flush=True)
+        return
     cfg = workloads.CONFIGS[args.workload]
     if args.workload == "c4":
         gbs, threads, sample = attention_cpu_gbs(cfg, repeats=max(1, args.steps))
@@ -869,12 +874,285 @@ def attention_arm(args):
         dist.destroy_process_group()
 
 
+def modes_layer_words(layer: int, shape, rng):
+    """Host words of a `modes` layer: the configs[1] draw (sign/magnitude,
+    mode 2), 40 high bytes with magnitudes spanning 7 bits (palette, mode
+    0), or random high bytes over 2-value low nibbles (nibble planes, mode
+    1), by layer % 3."""
+    from unchainkv_b200 import workloads as W
+
+    kind = layer % 3
+    if kind == 0:
+        tokens = shape[1] * shape[2] // (W.KV_HEADS * W.HEAD_DIM)
+        words = W.draw_tokens(2000 + layer, W.channel_scales(layer), tokens)
+        return np.ascontiguousarray(words.reshape(shape))
+    if kind == 1:
+        rest = np.array([h for h in range(256) if h not in (0x10, 0xF5)])
+        highs = np.concatenate([[0x10, 0xF5], rng.choice(rest, size=38, replace=False)])
+        high, low = highs[rng.integers(0, 40, shape)], rng.integers(0, 256, shape)
+    else:
+        high, low = rng.integers(0, 256, shape), (rng.integers(0, 256, shape) & 0x11) | 0x40
+    return ((high << 8) | low).astype(np.uint16)
+
+
+def aux_arm(args):
+    """--workload calib: GPU calibration (exponent histograms gathered from
+    the configs[1] paged cache + device-ranked top16 tables of all 32
+    layers).  --workload modes: the receiver's torch-op forms (modes 2, 0, 1)
+    decoded into the paged cache, 12 configs[1]-shaped layers."""
+    import torch
+    import torch.distributed as dist
+
+    from unchainkv_b200 import splitzip_cuda as S
+    from unchainkv_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        os.environ["NCCL_DEBUG"] = "WARN"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if not S.available():
+        raise RuntimeError(f"splitzip library missing: {S.load_error()}")
+    cfg = W.CONFIGS["c1"]
+    stream = torch.cuda.current_stream(device)
+    lib = S._load()
+    keep = []
+
+    if args.workload == "calib":
+        L = args.layers or cfg.layers
+        P = build_plan(cfg, L, device, rank)
+        src, ids = P["src"], P["src_t"][0]
+        hist = torch.zeros((L, 2, 256), dtype=torch.int32, device=device)
+        tables = torch.empty((L, 544), dtype=torch.uint8, device=device)
+        observed = torch.empty((L, 2), dtype=torch.int32, device=device)
+        jobs = S.job_array([S.histogram_job(src[l], ids, hist[l]) for l in range(L)])
+        raw = P["raw_bytes"]
+
+        def step():
+            hist.zero_()
+            if S.exponent_histogram_batch(jobs) != L:
+                raise RuntimeError("histograms declined")
+            S.top16_tables_from_histograms(hist, tables, observed)
+
+        step()
+        torch.cuda.synchronize()
+        for l in range(L):  # the reference's bincount and ranking, exactly
+            w = src[l][:, ids].reshape(2, -1).view(torch.int16).to(torch.int32) & 0xFFFF
+            ref = torch.stack([torch.bincount((p >> 7) & 0xFF, minlength=256) for p in w]).to(torch.int32)
+            if not torch.equal(ref, hist[l]):
+                raise RuntimeError(f"layer {l}: histogram differs from bincount")
+            h = hist[l].cpu().tolist()
+            books = bytes(S.rank_top16(h[0]) + S.rank_top16(h[1]))
+            if len(books) == 32 and bytes(tables[l].cpu().numpy().tobytes()) != S.build_top16_tables(books):
+                raise RuntimeError(f"layer {l}: device table differs from the ranking rule")
+        alg = {"ExpHistogramKernel": raw + 2048 * L, "Top16TablesKernel": 2048 * L + 552 * L}
+        dominant = "ExpHistogramKernel"
+        metric = "calibration GB/s of raw bf16 KV per GPU (exponent histograms + top16 tables)"
+        extra_cfg = {"layers": L, "tokens": cfg.tokens, "tables_bytes": 544 * L}
+        tables_host = torch.empty((L, 544), dtype=torch.uint8).pin_memory()
+        obs_host = torch.empty((L, 2), dtype=torch.int32).pin_memory()
+
+        def e2e_step():
+            step()
+            tables_host.copy_(tables, non_blocking=True)
+            obs_host.copy_(observed, non_blocking=True)
+
+        e2e_io = (0, tables.numel() + observed.numel() * 4,
+                  "KV cache resident in HBM -> histograms -> device tables -> pinned host tables")
+
+        def cpu_baseline():
+            sample = 2
+            host = [src[l][:, ids].reshape(2, -1).view(torch.int16).cpu().numpy().view(np.uint16) for l in range(sample)]
+            t0 = time.perf_counter()
+            for words in host:
+                counts = [np.bincount((p >> 7) & 0xFF, minlength=256) for p in words]
+                _ = [S.rank_top16(c) for c in counts]
+            dt = time.perf_counter() - t0
+            return sample * raw / L / dt / 1e9, 1, f"{sample} of {L} layers, numpy bincount + ranking"
+    else:  # modes: GPU torch-op encode + decode_any round trip
+        L = args.layers or 12
+        blocks, pool = cfg.blocks, cfg.blocks * cfg.pool_factor
+        src_ids = torch.as_tensor(W.block_table(pool, blocks, 3000), device=device)
+        dst_ids = torch.as_tensor(W.block_table(pool, blocks, 3001), device=device)
+        bw = cfg.block_tokens * cfg.kv_heads * cfg.head_dim
+        shape = (2, pool, bw)
+        rng = np.random.Generator(np.random.PCG64(4100 + rank))
+        src = torch.zeros((L,) + shape, dtype=torch.int16, device=device)
+        for l in range(L):
+            src[l][:, src_ids] = torch.from_numpy(modes_layer_words(l, (2, blocks, bw), rng).view(np.int16)).to(device)
+        src = src.view(torch.bfloat16)
+        dst = torch.zeros_like(src)
+        n = 2 * blocks * bw
+        cap = S.torchop_capacity(n)
+        streams = torch.zeros(L * cap, dtype=torch.uint8, device=device)
+        enc = S.job_array([S.make_job(src[l], src_ids, streams[l * cap:(l + 1) * cap]) for l in range(L)])
+        S.encode_torchop_batch(enc)
+        torch.cuda.synchronize()
+        heads = streams.view(L, cap)[:, :8].cpu().numpy()
+        lengths = [S.stream_length(bytes(h), n) for h in heads]
+        tables = torch.from_numpy(np.frombuffer(S.build_top16_tables(S._DEFAULT_TOP16_CODEBOOKS[:32]),
+                                                np.uint8).copy()).to(device)
+        dec = S.job_array([S.make_job(dst[l], dst_ids, streams[l * cap:(l + 1) * cap], lengths[l], tables)
+                           for l in range(L)])
+        raw = 2 * L * n
+        stream_total = sum(lengths)
+
+        def encode():
+            if S.encode_torchop_batch(enc) is None:
+                raise RuntimeError("torch-op encode declined")
+
+        def decode():
+            if S.decode_any_batch(dec) is None:
+                raise RuntimeError("decode declined")
+
+        def step():
+            encode()
+            decode()
+
+        step()
+        torch.cuda.synchronize()
+        for l in range(L):
+            if not torch.equal(dst[l][:, dst_ids].view(torch.int16), src[l][:, src_ids].view(torch.int16)):
+                raise RuntimeError(f"layer {l}: round trip differs")
+        alg = {"TorchopStatsKernel": raw, "TorchopEncodeKernel": raw + stream_total,
+               "ModeDecodeKernel": stream_total + raw}
+        dominant = None
+        metric = "torch-op codec round trip GB/s of raw bf16 KV per GPU (modes 2, 0, 1: GPU encode + receiver decode)"
+        extra_cfg = {"layers": L, "tokens": cfg.tokens, "modes": [int(h[0]) for h in heads],
+                     "stream_bytes_per_step": stream_total, "ratio": round(raw / stream_total, 4)}
+        host = torch.empty(L * cap, dtype=torch.uint8).pin_memory()
+
+        def e2e_step():
+            # each stream's exact bytes (lengths from the headers) leave and
+            # come back through pinned host memory
+            encode()
+            for l in range(L):
+                host[l * cap:l * cap + lengths[l]].copy_(streams[l * cap:l * cap + lengths[l]], non_blocking=True)
+            for l in range(L):
+                streams[l * cap:l * cap + lengths[l]].copy_(host[l * cap:l * cap + lengths[l]], non_blocking=True)
+            decode()
+
+        e2e_io = (stream_total, stream_total, "encode_torchop_batch -> D2H pinned -> H2D -> decode_any_batch")
+
+        def cpu_baseline():
+            from oracle import oracle
+
+            ids = W.block_table(pool, blocks, 3000)
+            sample = 3
+            caches = []
+            for l in range(sample):
+                cache = np.zeros(shape, dtype=np.uint16)
+                cache[:, ids] = src[l][:, src_ids].view(torch.int16).cpu().numpy().view(np.uint16)
+                caches.append(cache)
+            t0 = time.perf_counter()
+            for cache in caches:
+                _, stream_c = oracle.encode_torchop_blocks(cache, ids)
+                target = np.zeros(shape, dtype=np.uint16)
+                oracle.decode_modes_blocks(stream_c, target, ids)
+            dt = time.perf_counter() - t0
+            return sample * raw / L / dt / 1e9, 1, f"{sample} layers (one of each mode), oracle encode + receiver, 1 thread"
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end)
+        barrier()
+        return W.max_over_ranks(ms)
+
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms_step = timed(step, args.steps) / args.steps
+    if sampler:
+        sampler.stop()
+    prof_steps = max(1, min(args.steps, 200))
+    S.profile_enable(True)
+    for _ in range(prof_steps):
+        step()
+    prof = S.profile_collect()
+    S.profile_enable(False)
+    e2e = None
+    if not args.skip_e2e:
+        e2e_ms = timed(e2e_step, args.e2e_steps) / args.e2e_steps
+        e2e = {"value": round(world * raw / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": e2e_io[0], "d2h_bytes_per_step": e2e_io[1], "ms_per_step": round(e2e_ms, 4),
+               "path": e2e_io[2]}
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = peaks()
+    kernels = {}
+    for name, (ms, nl) in prof.items():
+        per = ms / nl
+        kernels[name] = {"launches": nl, "ms_per_launch": round(per, 5), "alg_bytes_per_launch": alg.get(name),
+                         "gbs": round(alg[name] / (per * 1e-3) / 1e9, 1) if name in alg else None}
+    if dominant is None:
+        dominant = max((k for k in kernels if k in alg), key=lambda k: kernels[k]["ms_per_launch"])
+    dom = kernels[dominant]
+    cpu = None
+    if not args.no_cpu_baseline:
+        gbs, threads, sample = cpu_baseline()
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
+               "cpu": cpu_model()}
+    line = {
+        "metric": metric,
+        "value": round(world * raw / (ms_step * 1e-3) / 1e9, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u16",
+        "data": "synthetic (seeded draws, configs[1] shape)",
+        "config": {"workload": args.workload, **extra_cfg, "raw_bytes_per_step": raw,
+                   "l2": "raw KV per step larger than L2",
+                   "parallelism": f"independent per-GPU shards x{world} (no collective)"},
+        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": round(dom["gbs"] / peak, 4), "peak_kind": peak_kind,
+                     "traffic": ncu_traffic(args.workload, dominant), "alg_bytes_per_launch": dom["alg_bytes_per_launch"]},
+        "kernels": kernels,
+        "gpu_launches": int(round(sum(nl for _, nl in prof.values()) / prof_steps * args.steps)),
+        "clocks": sampler.summary() if sampler else None,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         reference_arm(args)
     elif args.workload == "c4":
         attention_arm(args)
+    elif args.workload in ("calib", "modes"):
+        aux_arm(args)
     else:
         b200_arm(args)
 
