@@ -48,7 +48,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("c1", "c2", "c3", "c4", "calib", "modes"), default="c1",
+    p.add_argument("--workload", choices=("c1", "c2", "c3", "c4", "calib", "modes", "writeback"), default="c1",
                    help="c1: configs[1] (default); c2: configs[2] per-GPU TP shard; c3: configs[3] mixed batch; "
                         "c4: configs[4] decode attention over compressed KV; calib: GPU calibration over the "
                         "configs[1] cache; modes: receiver decode of the torch-op forms")
@@ -280,7 +280,7 @@ def reference_arm(args):
         return
     from unchainkv_b200 import workloads
 
-    if args.workload in ("calib", "modes"):
+    if args.workload in ("calib", "modes", "writeback"):
         print(json.dumps({"impl": "reference", "unavailable": "auxiliary workload; its line reports the CPU "
                           "restatement as cpu_baseline"}), flush=True)
         return
@@ -974,6 +974,78 @@ def aux_arm(args):
                 _ = [S.rank_top16(c) for c in counts]
             dt = time.perf_counter() - t0
             return sample * raw / L / dt / 1e9, 1, f"{sample} of {L} layers, numpy bincount + ranking"
+    elif args.workload == "writeback":  # auto encode + writeback over the blocks, configs[1]
+        L = args.layers or cfg.layers
+        blocks, pool = cfg.blocks, cfg.blocks * cfg.pool_factor
+        start = pool - blocks  # one contiguous run per layer (the reference writes back single runs)
+        run_ids = torch.arange(start, start + blocks, device=device)
+        kv = torch.empty((L, 2, pool, cfg.block_tokens, cfg.kv_heads, cfg.head_dim), dtype=torch.bfloat16,
+                         device=device)
+        books = b"".join(W.fill_layer_device(kv[l], cfg, l, run_ids.cpu().numpy(), shard=rank) for l in range(L))
+        tables = torch.tensor(np.frombuffer(b"".join(S.build_top16_tables(books[l * 32:(l + 1) * 32])
+                                                     for l in range(L)), np.uint8).reshape(L, 544).copy(),
+                              device=device)
+        original = kv.clone()
+        n = 2 * blocks * cfg.block_words
+        cap = (S.auto_capacity(n) + 15) // 16 * 16
+        buf = torch.zeros(L * cap, dtype=torch.uint8, device=device)
+        enc = S.job_array([S.make_job(kv[l], None, buf[l * cap:(l + 1) * cap], cap, tables[l], start, blocks)
+                           for l in range(L)])
+        S.encode_auto_batch(enc)
+        torch.cuda.synchronize()
+        heads = buf.view(L, cap)[:, :8].cpu().numpy()
+        lengths = [S.stream_length(bytes(h), n) for h in heads]
+        wb = S.job_array([S.writeback_job(kv[l], buf[l * cap:(l + 1) * cap], lengths[l], start, blocks)
+                          for l in range(L)])
+        raw = 2 * L * n
+        stream_total = sum(lengths)
+        host = torch.empty(stream_total, dtype=torch.uint8).pin_memory()
+
+        def step():
+            # the writeback of all layers' streams (the encode that made them
+            # is the c1 workload's; once written back the blocks hold the
+            # stream, so a step repeats the same copy)
+            if S.writeback_batch(wb) != stream_total:
+                raise RuntimeError("writeback declined")
+
+        step()
+        torch.cuda.synchronize()
+        for l in range(L):
+            staged = torch.cat(S.writeback_segments(kv[l], start, blocks))[:lengths[l]]
+            if not torch.equal(staged, buf[l * cap:l * cap + lengths[l]]):
+                raise RuntimeError(f"layer {l}: written-back bytes differ from the stream")
+            if not torch.equal(kv[l][:, :start], original[l][:, :start]):
+                raise RuntimeError(f"layer {l}: blocks outside the run changed")
+        del original
+        alg = {"WritebackKernel": 2 * stream_total}
+        dominant = "WritebackKernel"
+        metric = "codec writeback GB/s of raw bf16 KV per GPU (configs[1] streams over their own blocks)"
+        extra_cfg = {"layers": L, "tokens": cfg.tokens, "stream_bytes_per_step": stream_total,
+                     "modes": [int(h[0]) for h in heads]}
+
+        def e2e_step():
+            step()
+            offset = 0
+            for l in range(L):  # the host stages from the blocks, as the reference does
+                for seg in S.writeback_segments(kv[l], start, blocks):
+                    take = min(seg.numel(), lengths[l] - (offset - sum(lengths[:l])))
+                    if take <= 0:
+                        break
+                    host[offset:offset + take].copy_(seg[:take], non_blocking=True)
+                    offset += take
+
+        e2e_io = (0, stream_total, "writeback_batch -> D2H from the blocks to pinned host (the reference's staging)")
+
+        def cpu_baseline():
+            t0 = time.perf_counter()
+            for l in range(2):
+                src = buf[l * cap:l * cap + lengths[l]].cpu().numpy()
+                segs = [np.empty(2 * blocks * cfg.block_words, dtype=np.uint8) for _ in range(2)]
+                k = min(lengths[l], segs[0].size)
+                segs[0][:k] = src[:k]
+                segs[1][:lengths[l] - k] = src[k:]
+            dt = time.perf_counter() - t0
+            return 2 * 2 * n * 2 / dt / 1e9, 1, "2 layers, host memcpy of the stream into the segments"
     else:  # modes: GPU torch-op encode + decode_any round trip
         L = args.layers or 12
         blocks, pool = cfg.blocks, cfg.blocks * cfg.pool_factor
@@ -1151,7 +1223,7 @@ def main():
         reference_arm(args)
     elif args.workload == "c4":
         attention_arm(args)
-    elif args.workload in ("calib", "modes"):
+    elif args.workload in ("calib", "modes", "writeback"):
         aux_arm(args)
     else:
         b200_arm(args)

@@ -198,6 +198,16 @@ KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_splitzip_job* jo
                                                       unsigned long long count,
                                                       unsigned long long stream_ptr);
 
+/* Codec writeback (vllm_connector.py:3460-3563, 3720-3738): per job, the
+ * first stream_bytes of stream_ptr are copied over the job's own blocks,
+ * the K-plane run [block_start, block_start + block_count) first, then the
+ * V-plane run.  Declines (0) unless block_ids_ptr is 0 and block_stride ==
+ * block_words (one contiguous run of adjacent blocks), the stream fits the
+ * two runs, and it does not overlap them.  Returns the bytes written. */
+KVQ_API long long kvq_splitzip_writeback_batch(const kvq_splitzip_job* jobs,
+                                               unsigned long long count,
+                                               unsigned long long stream_ptr);
+
 /* The reference's torch-op encoder (vllm_connector.py:3204-3366) on the
  * GPU: per job the first of sign/magnitude (mode 2), high-byte palette
  * (mode 0) and nibble planes (mode 1) that is smaller than raw, else raw

@@ -665,6 +665,76 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_split
   return decode_batch<0>(jobs, count, reinterpret_cast<cudaStream_t>(stream_ptr));
 }
 
+// -------------------------------------------------------------- writeback
+
+namespace {
+
+template <int kMax>
+long long launch_writeback(const std::vector<WritebackJob>& jobs, size_t first, size_t count, cudaStream_t stream) {
+  static thread_local WritebackBatch<kMax> b;
+  b.jobs = static_cast<uint32_t>(count);
+  uint64_t chunks = 0;
+  for (size_t i = 0; i < count; ++i) {
+    b.chunk_start[i] = chunks;
+    b.job[i] = jobs[first + i];
+    chunks += b.job[i].chunks;
+  }
+  b.chunk_start[count] = chunks;
+  int device = 0, sms = 0;
+  cudaError_t st = cudaGetDevice(&device);
+  if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
+  const uint64_t blocks = std::max<uint64_t>(1, std::min<uint64_t>((chunks + 255) / 256, static_cast<uint64_t>(sms) * 8));
+  const long long prof = prof_begin(stream);
+  WritebackKernel<kMax><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(b);
+  prof_end(prof, "WritebackKernel", stream);
+  st = cudaGetLastError();
+  return st == cudaSuccess ? 0 : Fail("WritebackKernel", st);
+}
+
+}  // namespace
+
+extern "C" KVQ_API long long kvq_splitzip_writeback_batch(const kvq_splitzip_job* jobs, unsigned long long count,
+                                                          unsigned long long stream_ptr) {
+  if (!jobs || count == 0) return 0;
+  const auto stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  std::vector<WritebackJob> prepared(count);
+  long long total = 0;
+  for (unsigned long long i = 0; i < count; ++i) {
+    const kvq_splitzip_job& j = jobs[i];
+    // one contiguous run of whole, adjacent blocks (the reference skips
+    // fragmented or non-contiguous segments), and a stream that fits them
+    // and does not overlap them
+    if (!job_shape_ok(j) || j.block_ids_ptr != 0 || j.block_stride != j.block_words || j.stream_bytes == 0)
+      return 0;
+    auto* cache = reinterpret_cast<uint8_t*>(j.cache_ptr);
+    const uint64_t seg_bytes = 2 * j.block_count * j.block_words;
+    if (j.stream_bytes > 2 * seg_bytes) return 0;
+    WritebackJob& w = prepared[i];
+    w.src = reinterpret_cast<const uint8_t*>(j.stream_ptr);
+    w.bytes = j.stream_bytes;
+    w.seg[0] = cache + 2 * j.block_start * j.block_stride;
+    w.seg[1] = w.seg[0] + 2 * j.plane_stride;
+    w.seg_bytes = seg_bytes;
+    w.chunks = (w.bytes + 15) / 16;
+    for (int s = 0; s < 2; ++s) {
+      const uintptr_t a = reinterpret_cast<uintptr_t>(w.seg[s]), e = a + seg_bytes;
+      const uintptr_t sa = reinterpret_cast<uintptr_t>(w.src), se = sa + w.bytes;
+      if (sa < e && a < se) return 0;  // the stream aliases the blocks
+    }
+    w.vec = (reinterpret_cast<uintptr_t>(w.src) % 16 == 0 && reinterpret_cast<uintptr_t>(w.seg[0]) % 16 == 0 &&
+             reinterpret_cast<uintptr_t>(w.seg[1]) % 16 == 0 && seg_bytes % 16 == 0)
+                ? 1
+                : 0;
+    total += static_cast<long long>(w.bytes);
+  }
+  for (size_t first = 0; first < count; first += kMaxBatch) {
+    const long long rc = launch_writeback<kMaxBatch>(prepared, first, std::min<size_t>(kMaxBatch, count - first), stream);
+    if (rc < 0) return rc;
+  }
+  return total;
+}
+
 // --------------------------------------------------- torch-op encoder
 
 namespace {

@@ -1923,6 +1923,55 @@ __global__ void __launch_bounds__(256) ModeDecodeKernel(const __grid_constant__ 
   }
 }
 
+// -------------------------------------------------------------- writeback
+//
+// Codec writeback (vllm_connector.py:3460-3563, segments :3720-3738): a
+// job's stream is copied over its own source blocks, the K-plane run of the
+// job's contiguous blocks first, then the V-plane run, so that the transfer
+// buffer can be reused while the stream waits in the (no longer needed) KV
+// blocks for its copy to the host.  One launch for all jobs; 16-byte copies
+// when the stream and the segments are 16-byte aligned.
+struct WritebackJob {
+  const uint8_t* src;  // the stream
+  uint64_t bytes;      // its length
+  uint8_t* seg[2];     // K- and V-plane runs of the blocks
+  uint64_t seg_bytes;  // bytes per run
+  uint64_t chunks;     // 16-byte chunks of the stream (rounded up)
+  int vec;
+  int pad;
+};
+
+template <int kMax>
+struct WritebackBatch {
+  uint32_t jobs;
+  uint64_t chunk_start[kMax + 1];
+  WritebackJob job[kMax];
+};
+
+template <int kMax>
+__global__ void __launch_bounds__(256) WritebackKernel(const __grid_constant__ WritebackBatch<kMax> b) {
+  const uint64_t total = b.chunk_start[b.jobs];
+  int j = 0;
+  for (uint64_t c = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
+       c += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    while (c >= b.chunk_start[j + 1]) ++j;
+    const WritebackJob& W = b.job[j];
+    const uint64_t off = 16 * (c - b.chunk_start[j]);
+    const uint64_t n = min(uint64_t{16}, W.bytes - off);
+    const int s = off >= W.seg_bytes ? 1 : 0;
+    uint8_t* dst = W.seg[s] + (off - (s ? W.seg_bytes : 0));
+    if (W.vec && n == 16) {
+      *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(W.src + off));
+    } else {
+      for (uint64_t k = 0; k < n; ++k) {
+        const uint64_t o = off + k;
+        const int t = o >= W.seg_bytes ? 1 : 0;
+        W.seg[t][o - (t ? W.seg_bytes : 0)] = __ldg(W.src + o);
+      }
+    }
+  }
+}
+
 template <int kMax>
 __global__ void __launch_bounds__(kThreads) ZeroKernel(const __grid_constant__ ZeroBatch<kMax> z) {
   for (uint32_t r = blockIdx.y; r < z.count; r += gridDim.y) {

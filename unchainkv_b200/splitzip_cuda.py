@@ -85,6 +85,7 @@ _BATCH_SIGNATURES = {
     "kvq_splitzip_bf16_exponent_histogram_batch": None,
     "kvq_splitzip_bf16_decode_any_batch": None,
     "kvq_splitzip_bf16_encode_torchop_batch": None,
+    "kvq_splitzip_writeback_batch": None,
 }
 
 
@@ -741,6 +742,30 @@ def decode_fixed6_batch(jobs, stream=None) -> int | None:
 def decode_auto_batch(jobs, stream=None) -> int | None:
     """Decode each job's stream by its mode byte (5, 3 or 6) on the device."""
     return _run_batch("kvq_splitzip_bf16_decode_auto_batch", jobs, stream)
+
+
+def writeback_job(kv_layer, stream_buffer, stream_bytes_: int, block_start: int, block_count: int) -> KvqJob:
+    """A writeback job: the first ``stream_bytes_`` of ``stream_buffer`` go
+    over the layer's blocks [block_start, block_start + block_count)."""
+    return make_job(kv_layer, None, stream_buffer, stream_bytes_, None, block_start, block_count)
+
+
+def writeback_batch(jobs, stream=None) -> int | None:
+    """Codec writeback (the reference's ``_try_splitzip_writeback``): copy
+    each job's stream over its own blocks, K-plane run first, then the
+    V-plane run, in one launch.  Like the reference, declines (None) a job
+    whose blocks are not one contiguous run of adjacent blocks or whose
+    stream overlaps them.  Returns the bytes written."""
+    return _run_batch("kvq_splitzip_writeback_batch", jobs, stream)
+
+
+def writeback_segments(kv_layer, block_start: int, block_count: int):
+    """The byte views a writeback fills, in order (the reference's
+    ``_kv_writeback_segments`` for one run): K-plane blocks, V-plane blocks."""
+    import torch
+
+    return [kv_layer[plane, block_start:block_start + block_count].reshape(-1).view(torch.uint8)
+            for plane in range(2)]
 
 
 def encode_torchop_batch(jobs, stream=None) -> int | None:
