@@ -198,6 +198,24 @@ KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_splitzip_job* jo
                                                       unsigned long long count,
                                                       unsigned long long stream_ptr);
 
+/* ---- GPU-to-GPU stream transport (replaces the D2H -> TCP -> H2D hop of
+ * the compressed-layer frames, src/unchain_kv/tcp_data.py:615-652 and
+ * native/unchain_kv/kvq_tcp.cc:224-270): the sender's stream buffers are
+ * opened by the receiving process over CUDA IPC, and its decode reads the
+ * streams from the sender's HBM over NVLink. */
+
+/* cudaMalloc of a stream buffer on the current device (0 on failure). */
+KVQ_API unsigned long long kvq_splitzip_ipc_alloc(unsigned long long bytes);
+KVQ_API long long kvq_splitzip_ipc_free(unsigned long long ptr);
+/* The 64-byte IPC handle of a kvq_splitzip_ipc_alloc buffer; returns 64. */
+KVQ_API long long kvq_splitzip_ipc_get_handle(unsigned long long ptr, unsigned char* handle64);
+/* Open a handle from another process on the current device (peer access
+ * enabled lazily); its address in this process, 0 on failure. */
+KVQ_API unsigned long long kvq_splitzip_ipc_open(const unsigned char* handle64);
+KVQ_API long long kvq_splitzip_ipc_close(unsigned long long ptr);
+/* 1 if the current device can read peer_device's memory directly. */
+KVQ_API long long kvq_splitzip_peer_access(long long peer_device);
+
 /* Codec writeback (vllm_connector.py:3460-3563, 3720-3738): per job, the
  * first stream_bytes of stream_ptr are copied over the job's own blocks,
  * the K-plane run [block_start, block_start + block_count) first, then the

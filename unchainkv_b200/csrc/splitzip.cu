@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <atomic>
 #include <cstdint>
 #include <map>
@@ -663,6 +664,69 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_decode_auto_batch(const kvq_split
                                                                  unsigned long long count,
                                                                  unsigned long long stream_ptr) {
   return decode_batch<0>(jobs, count, reinterpret_cast<cudaStream_t>(stream_ptr));
+}
+
+// ---------------------------------------------------------- peer streams
+//
+// Host plumbing of the GPU-to-GPU stream transport: stream buffers the
+// sender allocates here (whole cudaMalloc allocations, so an IPC handle
+// covers them from offset 0) are opened by the receiving process on its own
+// device with lazy peer access, and its decode kernels read the streams
+// straight from the sender's HBM over NVLink.
+
+extern "C" KVQ_API unsigned long long kvq_splitzip_ipc_alloc(unsigned long long bytes) {
+  void* p = nullptr;
+  const cudaError_t st = cudaMalloc(&p, bytes);
+  if (st != cudaSuccess) {
+    Fail("cudaMalloc", st);
+    return 0;
+  }
+  return reinterpret_cast<unsigned long long>(p);
+}
+
+extern "C" KVQ_API long long kvq_splitzip_ipc_free(unsigned long long ptr) {
+  const cudaError_t st = cudaFree(reinterpret_cast<void*>(ptr));
+  return st == cudaSuccess ? 0 : Fail("cudaFree", st);
+}
+
+// The 64-byte IPC handle of an allocation made by kvq_splitzip_ipc_alloc.
+extern "C" KVQ_API long long kvq_splitzip_ipc_get_handle(unsigned long long ptr, unsigned char* handle64) {
+  if (ptr == 0 || handle64 == nullptr) return 0;
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  const cudaError_t st = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr));
+  if (st != cudaSuccess) return Fail("cudaIpcGetMemHandle", st);
+  std::memcpy(handle64, &h, sizeof(h));
+  return 64;
+}
+
+// Open another process's allocation on the current device (peer access
+// enabled lazily); returns its address here, 0 on failure.
+extern "C" KVQ_API unsigned long long kvq_splitzip_ipc_open(const unsigned char* handle64) {
+  if (handle64 == nullptr) return 0;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t st = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (st != cudaSuccess) {
+    Fail("cudaIpcOpenMemHandle", st);
+    return 0;
+  }
+  return reinterpret_cast<unsigned long long>(p);
+}
+
+extern "C" KVQ_API long long kvq_splitzip_ipc_close(unsigned long long ptr) {
+  const cudaError_t st = cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+  return st == cudaSuccess ? 0 : Fail("cudaIpcCloseMemHandle", st);
+}
+
+// 1 when the current device can read `peer_device`'s memory directly.
+extern "C" KVQ_API long long kvq_splitzip_peer_access(long long peer_device) {
+  int device = 0, ok = 0;
+  cudaError_t st = cudaGetDevice(&device);
+  if (st == cudaSuccess) st = cudaDeviceCanAccessPeer(&ok, device, static_cast<int>(peer_device));
+  if (st != cudaSuccess) return Fail("cudaDeviceCanAccessPeer", st);
+  return ok ? 1 : 0;
 }
 
 // -------------------------------------------------------------- writeback

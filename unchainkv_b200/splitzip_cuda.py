@@ -149,6 +149,18 @@ def _load():
             lib.kvq_splitzip_attention_workspace_bytes.restype = ctypes.c_longlong
             lib.kvq_splitzip_attention_decode.argtypes = [ctypes.POINTER(KvqAttnRequest)] + [_U64] * 5
             lib.kvq_splitzip_attention_decode.restype = ctypes.c_longlong
+            _bytes64 = ctypes.POINTER(ctypes.c_ubyte)
+            for name, argtypes, restype in (
+                ("kvq_splitzip_ipc_alloc", [_U64], _U64),
+                ("kvq_splitzip_ipc_free", [_U64], ctypes.c_longlong),
+                ("kvq_splitzip_ipc_get_handle", [_U64, _bytes64], ctypes.c_longlong),
+                ("kvq_splitzip_ipc_open", [_bytes64], _U64),
+                ("kvq_splitzip_ipc_close", [_U64], ctypes.c_longlong),
+                ("kvq_splitzip_peer_access", [ctypes.c_longlong], ctypes.c_longlong),
+            ):
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = restype
             lib.kvq_splitzip_last_error.argtypes = []
             lib.kvq_splitzip_last_error.restype = ctypes.c_char_p
             lib.kvq_splitzip_profile_enable.argtypes = [ctypes.c_int]
