@@ -48,7 +48,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("c1", "c2", "c3", "c4", "calib", "modes", "writeback"), default="c1",
+    p.add_argument("--workload", choices=("c1", "c2", "c3", "c4", "calib", "modes", "writeback", "transfer"),
+                   default="c1",
                    help="c1: configs[1] (default); c2: configs[2] per-GPU TP shard; c3: configs[3] mixed batch; "
                         "c4: configs[4] decode attention over compressed KV; calib: GPU calibration over the "
                         "configs[1] cache; modes: receiver decode of the torch-op forms")
@@ -280,7 +281,7 @@ def reference_arm(args):
         return
     from unchainkv_b200 import workloads
 
-    if args.workload in ("calib", "modes", "writeback"):
+    if args.workload in ("calib", "modes", "writeback", "transfer"):
         print(json.dumps({"impl": "reference", "unavailable": "auxiliary workload; its line reports the CPU "
                           "restatement as cpu_baseline"}), flush=True)
         return
@@ -1217,6 +1218,183 @@ def aux_arm(args):
         dist.destroy_process_group()
 
 
+def transfer_arm(args):
+    """--workload transfer (N >= 2, even): prefill -> decode KV transfer.
+    Rank 2p encodes configs[1] (auto codec, all 32 layers) into its stream
+    buffers; rank 2p + 1 decodes them straight from rank 2p's HBM over
+    NVLink into its own paged cache (unchainkv_b200.transport).  Two steps
+    are in flight.  The line also times the same bytes of raw KV sent over
+    NCCL between the pair (what moving it uncompressed costs)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from unchainkv_b200 import splitzip_cuda as S
+    from unchainkv_b200 import workloads as W
+    from unchainkv_b200.transport import StreamTransport, peer_job
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2 or world % 2:
+        raise SystemExit("--workload transfer needs an even number of GPUs >= 2 (sender, receiver pairs)")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    os.environ["NCCL_DEBUG"] = "WARN"
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if not S.available():
+        raise RuntimeError(f"splitzip library missing: {S.load_error()}")
+    cfg = W.CONFIGS["c1"]
+    L = args.layers or cfg.layers
+    pair = rank // 2
+    sender, receiver = 2 * pair, 2 * pair + 1
+    P = build_plan(cfg, L, device, pair)  # both ranks of a pair hold the same source words
+    jobs, raw = P["jobs"], P["raw_bytes"]
+    capacity = int(P["streams"].numel())
+    transports = [StreamTransport(capacity, sender=2 * q, receiver=2 * q + 1) for q in range(world // 2)]
+    tr = transports[pair]
+    role = tr.role
+    J = len(jobs)
+    slots = []
+    for s in range(tr.slots):
+        base = tr.buffer(s)
+        if role == "sender":
+            slots.append(S.job_array([peer_job(P["src"][l], P["src_t"][r], base + o, c, P["tables"][l])
+                                      for l, r, n, o, c in jobs]))
+        else:
+            slots.append(S.job_array([peer_job(P["dst"][l], P["dst_t"][r], base + o, c, P["tables"][l])
+                                      for l, r, n, o, c in jobs]))
+    lib = S._load()
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+    k_step = [0]
+
+    def step():
+        k = k_step[0]
+        if role == "sender":
+            if lib.kvq_splitzip_bf16_encode_auto_batch(slots[k % tr.slots], J, sp) <= 0:
+                raise RuntimeError("encode declined: " + lib.kvq_splitzip_last_error().decode())
+            tr.step(k)
+        else:
+            tr.step(k)
+            if lib.kvq_splitzip_bf16_decode_auto_batch(slots[k % tr.slots], J, sp) <= 0:
+                raise RuntimeError("decode declined: " + lib.kvq_splitzip_last_error().decode())
+        k_step[0] = k + 1
+
+    step()
+    torch.cuda.synchronize()
+    if role == "receiver":
+        check_round_trip(P, "transferred step")
+    # the streams' lengths: the same encode into the plan's local buffer
+    stream_sizes_total = 0
+    if role == "sender":
+        if lib.kvq_splitzip_bf16_encode_auto_batch(P["enc"], J, sp) <= 0:
+            raise RuntimeError("encode declined")
+        torch.cuda.synchronize()
+        offsets = torch.tensor([o for _, _, _, o, _ in jobs], device=device)
+        modes = P["streams"][offsets].cpu().tolist()
+        stream_sizes_total = sum(S.stream_bytes(m, n) or 0 for m, (_, _, n, _, _) in zip(modes, jobs))
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        dist.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end)
+        dist.barrier()
+        return W.max_over_ranks(ms)
+
+    sampler = ClockSampler(range(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms_step = timed(step, args.steps) / args.steps
+    if sampler:
+        sampler.stop()
+    prof_steps = max(1, min(args.steps, 100))
+    S.profile_enable(True)
+    for _ in range(prof_steps):
+        step()
+    torch.cuda.synchronize()
+    prof = S.profile_collect()
+    S.profile_enable(False)
+    for t in transports:
+        t.finish()
+    # the same bytes of raw KV over NCCL between the pair
+    raw_buf = torch.empty(raw, dtype=torch.uint8, device=device)
+
+    def raw_step():
+        if role == "sender":
+            dist.send(raw_buf, receiver)
+        else:
+            dist.recv(raw_buf, sender)
+
+    raw_steps = max(3, min(args.steps, 50))
+    ms_raw = timed(raw_step, raw_steps) / raw_steps
+    # the receivers' decode and the senders' encode kernels, max over ranks
+    dec_ms = prof.get("DecodeAutoKernel", (0.0, 1))
+    enc_ms = prof.get("EncodeAutoKernel", (0.0, 1))
+    per = torch.tensor([dec_ms[0] / max(dec_ms[1], 1), enc_ms[0] / max(enc_ms[1], 1)], device=device)
+    dist.all_reduce(per, op=dist.ReduceOp.MAX)
+    launches = torch.tensor([sum(nl for _, nl in prof.values()) / prof_steps], device=device)
+    dist.all_reduce(launches)
+    if rank != 0:
+        for t in transports:
+            t.close()
+        dist.destroy_process_group()
+        return
+    peak, peak_kind = peaks()
+    nvlink_peak = 770.0  # measured peer copy per direction on this pool's B200s (GB/s)
+    dec_launch_ms, enc_launch_ms = float(per[0]), float(per[1])
+    stream_total = stream_sizes_total
+    pairs = world // 2
+    line = {
+        "metric": "KV transfer GB/s of raw bf16 KV delivered (encode on the sender GPU, decode on arrival over "
+                  "NVLink on the receiver GPU)",
+        "value": round(pairs * raw / (ms_step * 1e-3) / 1e9, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u16",
+        "data": "synthetic (seeded device draw of the configs[1] distribution)",
+        "config": {"workload": "transfer", "layers": L, "tokens": cfg.tokens, "pairs": pairs,
+                   "raw_bytes_per_step": raw, "stream_bytes_per_step": stream_total,
+                   "ratio": round(raw / stream_total, 4) if stream_total else None,
+                   "slots_in_flight": tr.slots,
+                   "raw_kv_over_nccl_gbs": round(pairs * raw / (ms_raw * 1e-3) / 1e9, 3),
+                   "parallelism": f"{pairs} sender -> receiver pair(s), ordered by NCCL tokens"},
+        "roofline": {"bound": "nvlink", "kernel": "DecodeAutoKernel (receiver, reading the sender's streams)",
+                     "achieved": round(stream_total / (dec_launch_ms * 1e-3) / 1e9, 1) if dec_launch_ms else None,
+                     "peak": nvlink_peak, "unit": "GB/s",
+                     "frac": round(stream_total / (dec_launch_ms * 1e-3) / 1e9 / nvlink_peak, 4) if dec_launch_ms else None,
+                     "peak_kind": "measured peer copy (pool reference)", "traffic": None,
+                     "alg_bytes_per_launch": stream_total},
+        "kernels": {"DecodeAutoKernel": {"ms_per_launch": round(dec_launch_ms, 5)},
+                    "EncodeAutoKernel": {"ms_per_launch": round(enc_launch_ms, 5)}},
+        "gpu_launches": int(round(float(launches[0]) * args.steps)),
+        "clocks": sampler.summary() if sampler else None,
+        "cpu_baseline": None,
+        "e2e": None,
+        "e2e_note": "device-resident KV to device-resident KV: no host copy is part of this path",
+    }
+    print(json.dumps(line), flush=True)
+    for t in transports:
+        t.close()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -1225,6 +1403,8 @@ def main():
         attention_arm(args)
     elif args.workload in ("calib", "modes", "writeback"):
         aux_arm(args)
+    elif args.workload == "transfer":
+        transfer_arm(args)
     else:
         b200_arm(args)
 
