@@ -39,7 +39,6 @@ using namespace ukv;
 namespace {
 
 thread_local std::string g_last_error;
-std::atomic<unsigned int> g_decode_slot_counter{0};
 
 long long Fail(const char* what, cudaError_t status) {
   g_last_error = std::string(what) + ": " + cudaGetErrorString(status);
@@ -296,7 +295,6 @@ void prepare_decode(const uint8_t* src, uint64_t src_bytes, uint16_t* dst, const
   d.tables = tables;
   d.tiles = static_cast<uint32_t>(tiles_for(L.n));
   d.vec = vec_ok(dst, L);
-  d.slot = g_decode_slot_counter.fetch_add(1, std::memory_order_relaxed) % kDecodeSlots;
 }
 
 // ------------------------------------------------------------------ launch
@@ -416,13 +414,27 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
     return rc;
   } else {
     if (rc < 0) return rc;
-    // top16 streams whose entries the tiles could not all take (unsorted
-    // streams from other encoders) are finished by one CTA per job
+    // the escaped words of the top16 streams, one thread per entry
+    static thread_local PatchBatch<kMax> pb;
+    pb.jobs = b.jobs;
+    uint64_t entries = 0;
+    for (size_t i = 0; i < count; ++i) {
+      pb.entry_start[i] = entries;
+      pb.job[i] = b.job[i];
+      entries += b.job[i].cap;
+    }
+    pb.entry_start[count] = entries;
+    int device = 0, sms = 0;
+    cudaError_t st = cudaGetDevice(&device);
+    if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
+    const uint64_t blocks =
+        std::max<uint64_t>(1, std::min<uint64_t>((entries + 255) / 256, static_cast<uint64_t>(sms) * 4));
     const long long prof = prof_begin(stream);
-    RepairKernel<kMax, kMode><<<static_cast<unsigned>(count), kThreads, 0, stream>>>(b);
-    prof_end(prof, "RepairKernel", stream);
-    const cudaError_t st = cudaGetLastError();
-    return st == cudaSuccess ? 0 : Fail("RepairKernel", st);
+    EscapePatchKernel<kMax, kMode><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(pb);
+    prof_end(prof, "EscapePatchKernel", stream);
+    st = cudaGetLastError();
+    return st == cudaSuccess ? 0 : Fail("EscapePatchKernel", st);
   }
 }
 

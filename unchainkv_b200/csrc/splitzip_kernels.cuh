@@ -26,7 +26,6 @@ namespace ukv {
 
 constexpr int kMaxBatch = 96;
 constexpr uint64_t kStatusFlag = 1ull << 63;
-constexpr int kDecodeSlots = 1024;
 constexpr int kEncStages = 4;  // ring depth of the encode kernels (16 KiB stages)
 constexpr int kDecStages = 3;  // ring depth of the decode kernel (16.1 KiB stages + descriptors)
 constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 16 KiB of words
@@ -34,13 +33,6 @@ constexpr uint32_t kDecStageBytes = 2 * kTileWords + 128;
 constexpr uint32_t kDecCodesOffset = kTileWords + 128;  // top16/fixed6 codes inside a stage
 constexpr uint32_t kEncSmemBytes = kEncStages * kEncStageBytes;
 constexpr uint32_t kDecSmemBytes = kDecStages * kDecStageBytes;
-
-// Per-call decode state: escape entries the tiles of a top16 stream took
-// (compared with the stream's count by RepairKernel, which resets it).
-struct DecodeSlot {
-  unsigned int covered;
-  unsigned int pad[3];
-};
 
 // ------------------------------------------------------------------ jobs
 
@@ -78,7 +70,7 @@ struct DecJob {
   uint64_t cap;
   const uint8_t* tables;
   uint32_t tiles;
-  uint32_t slot;
+  uint32_t pad0;
   int vec;  // 16-byte stores of whole units into the destination layout
   int pad;
 };
@@ -151,7 +143,6 @@ __host__ __device__ constexpr uint64_t auto_scratch_bytes(uint64_t tiles) {
 constexpr uint64_t kFixedScratchBytes = 36;
 
 __device__ unsigned int g_device_errors;
-__device__ DecodeSlot g_decode_slots[kDecodeSlots];
 
 __device__ __forceinline__ void raise_error(uint32_t* flag) {
   if (flag) atomicOr(flag, 1u);
@@ -1267,7 +1258,6 @@ __global__ void __launch_bounds__(256) Top16TablesKernel(const uint32_t* __restr
 // 16-byte stores per lane at the resolved step address.
 
 constexpr uint32_t kStepsPerTile = kTileWords / kStepWords;
-constexpr uint32_t kStageEscapes = 512;  // escapes one tile descriptor holds
 
 // Decode stage descriptor, written by the producer warp.
 struct DecDesc {
@@ -1278,9 +1268,6 @@ struct DecDesc {
   uint32_t pad_y;  // offset of the codes in the stage's codes region
   uint32_t unused;
   uint16_t* step_dst[kStepsPerTile];   // 16-byte aligned contiguous destination of a step, or null
-  uint32_t esc_bits[kTileWords / 32];  // top16: escaped words of the tile
-  uint16_t esc_rank[kTileWords / 32];  // top16: escapes before each bitmap word
-  uint8_t esc_exp[kStageEscapes];      // top16: exponents in position order
 };
 
 // fixed6 pair table of the consumers' current job: entry (c0 | c1 << 6)
@@ -1361,157 +1348,6 @@ __device__ __forceinline__ uint2 decode_stage(const DecJob& J, uint32_t mode, ui
   return pad;
 }
 
-// First entry index whose position is >= t0, assuming ascending positions
-// (warp-wide 32-ary search).
-__device__ uint64_t escape_lower_bound(const uint8_t* entries, uint64_t count, uint64_t t0) {
-  const int lane = threadIdx.x & 31;
-  uint64_t lo = 0, hi = count;  // answer in [lo, hi]
-  while (hi - lo > 32) {
-    const uint64_t step = (hi - lo + 31) / 32;
-    const uint64_t idx = lo + lane * step;
-    const bool probe = idx < hi;
-    const bool below = probe && entry_pos(entries, idx) < t0;
-    const uint32_t nb = __popc(__ballot_sync(kFull, below));
-    const uint32_t np = __popc(__ballot_sync(kFull, probe));
-    const uint64_t nlo = nb ? lo + (nb - 1) * step + 1 : lo;
-    const uint64_t nhi = nb < np ? lo + nb * step : hi;
-    lo = nlo;
-    hi = nhi;
-  }
-  const uint64_t idx = lo + lane;
-  const bool below = idx < hi && entry_pos(entries, idx) < t0;
-  return lo + __popc(__ballot_sync(kFull, below));
-}
-
-// 128 consecutive escape entries held in the producer warp's registers:
-// entry base + 32*j + lane in slot j of each lane (position -2 past the end).
-struct EscWindow {
-  static constexpr int kPerLane = 4;
-  uint64_t base = ~0ull;
-  int64_t pos[kPerLane];
-  uint32_t exps[kPerLane];
-};
-
-// Issue the loads of the window at `base` (the registers are first read at
-// the next scan, so the loads stay in flight meanwhile).
-__device__ __forceinline__ void load_window(EscWindow& w, const uint8_t* entries, uint64_t count, uint64_t base) {
-  const int lane = threadIdx.x & 31;
-  w.base = base;
-#pragma unroll
-  for (int j = 0; j < EscWindow::kPerLane; ++j) {
-    const uint64_t idx = base + 32 * j + lane;
-    const bool exists = idx < count;
-    w.pos[j] = exists ? static_cast<int64_t>(entry_pos(entries, idx)) : -2;
-    w.exps[j] = exists ? __ldg(entries + idx * 5 + 4) : 0u;
-  }
-}
-
-// Producer warp: this tile's escapes into the descriptor (bitmap, ranks,
-// exponents in position order).  Entries are taken from `cursor` (the lower
-// bound of t0 when cursor_ok, else searched) while their positions fall in
-// the tile and strictly increase, up to kStageEscapes.  They are read from
-// the register window `win`, which the previous tile prefetched at the
-// cursor; the window for the next tile is prefetched on return.  Returns the
-// entries taken; any other entry (out of position order, >= n, or past a
-// tile's capacity) is left to RepairKernel, which applies every entry of a
-// stream whose tiles did not take them all.  cursor_ok says whether the
-// cursor ended on the next tile's lower bound.
-__device__ __forceinline__ uint32_t producer_escapes(const DecJob& J, uint64_t count, uint64_t t0, uint32_t len,
-                                                     DecDesc& d, uint64_t& cursor, bool& cursor_ok,
-                                                     EscWindow& win) {
-  constexpr int kPerLane = EscWindow::kPerLane;
-  const int lane = threadIdx.x & 31;
-  const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
-  const int64_t lo = static_cast<int64_t>(t0), hi = static_cast<int64_t>(t0 + len);
-#pragma unroll
-  for (int w = 0; w < static_cast<int>(kTileWords / 32 / 32); ++w) d.esc_bits[w * 32 + lane] = 0;
-  if (!cursor_ok) cursor = escape_lower_bound(entries, count, t0);
-  if (win.base != cursor) load_window(win, entries, count, cursor);
-  __syncwarp();
-  uint32_t taken = 0;
-  int64_t last = -1;
-  bool clean = true;
-  while (cursor < count) {
-    // take = number of leading window entries that belong to this tile, in order
-    bool next_tile[kPerLane];  // entry opens a later tile in order (or there is none)
-    uint32_t bad[kPerLane];
-    int64_t group_last = last;
-#pragma unroll
-    for (int j = 0; j < kPerLane; ++j) {
-      const bool exists = win.base + 32 * j + lane < count;
-      const int64_t pos = win.pos[j];
-      int64_t prev = __shfl_up_sync(kFull, pos, 1);
-      if (lane == 0) prev = group_last;
-      const bool ok = exists && pos >= lo && pos < hi && pos > prev && taken + 32 * j + lane < kStageEscapes;
-      next_tile[j] = !exists || (pos >= hi && pos > prev);
-      bad[j] = __ballot_sync(kFull, !ok);
-      group_last = __shfl_sync(kFull, pos, 31);
-    }
-    uint32_t take = 32 * kPerLane;
-    bool stop_clean = false;
-#pragma unroll
-    for (int j = kPerLane - 1; j >= 0; --j) {
-      if (bad[j]) {  // uniform; the lowest group with a bad entry wins
-        const int first = __ffs(bad[j]) - 1;
-        take = 32 * j + first;
-        stop_clean = __shfl_sync(kFull, next_tile[j], first);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kPerLane; ++j) {
-      const uint32_t k = 32 * j + lane;
-      if (k < take) {
-        const uint32_t local = static_cast<uint32_t>(win.pos[j] - lo);
-        atomicOr(&d.esc_bits[local >> 5], 1u << (local & 31));
-        d.esc_exp[taken + k] = static_cast<uint8_t>(win.exps[j]);
-      }
-    }
-    if (take > 0) {
-      const uint32_t j = (take - 1) >> 5;
-      int64_t v = win.pos[0];
-#pragma unroll
-      for (int i = 1; i < kPerLane; ++i) v = (static_cast<uint32_t>(i) == j) ? win.pos[i] : v;
-      last = __shfl_sync(kFull, v, static_cast<int>((take - 1) & 31));
-    }
-    taken += take;
-    cursor += take;
-    if (take < 32 * kPerLane) {
-      clean = stop_clean;
-      break;
-    }
-    load_window(win, entries, count, cursor);  // more than a window in this tile
-  }
-  cursor_ok = clean;
-  __syncwarp();
-  // ranks: lane covers bitmap words 8*lane .. 8*lane+7
-  constexpr int kPer = kTileWords / 32 / 32;
-  uint32_t c[kPer];
-  uint32_t mine = 0;
-#pragma unroll
-  for (int w = 0; w < kPer; ++w) {
-    c[w] = __popc(d.esc_bits[kPer * lane + w]);
-    mine += c[w];
-  }
-  uint32_t incl = mine;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t v = __shfl_up_sync(kFull, incl, o);
-    if (lane >= o) incl += v;
-  }
-  uint32_t run = incl - mine;
-#pragma unroll
-  for (int w = 0; w < kPer; ++w) {
-    d.esc_rank[kPer * lane + w] = static_cast<uint16_t>(run);
-    run += c[w];
-  }
-  // prefetch the window of the next tile
-  if (cursor_ok && cursor < count && win.base != cursor) load_window(win, entries, count, cursor);
-  return taken;
-}
-
-// Mode of a job's stream, or 0 when this kernel must leave it alone
-// (kMode != 0: the reference writes nothing for another mode; kMode == 0:
-// unknown modes and streams shorter than their mode's length are skipped).
 template <int kMode>
 __device__ __forceinline__ uint32_t job_mode(const DecJob& J) {
   const uint32_t mode = __ldg(J.src);
@@ -1532,10 +1368,6 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
   int ji = find_job<kMax>(b.tile_start, b.jobs, c.first);
   int mode_job = -1;
   uint32_t mode = 0;
-  uint64_t count = 0;
-  uint64_t cursor = 0;
-  bool cursor_ok = false;
-  EscWindow win;
   for (uint32_t t = c.first;; ++t) {
     producer_acquire(R, p, nullptr);
     DecDesc& d = D[p.s];
@@ -1548,9 +1380,6 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
     const DecJob& N = b.job[ji];
     if (ji != mode_job) {
       mode = job_mode<kMode>(N);
-      count = mode == 5 ? min(static_cast<uint64_t>(load_u32le(N.src + 1)), N.cap) : 0;
-      cursor_ok = false;
-      win.base = ~0ull;
       mode_job = ji;
     }
     const uint64_t t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
@@ -1563,8 +1392,7 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
       d.pad_x = pad.x;
       d.pad_y = pad.y;
     }
-    // destination of each 512-word step (its block-table load stays in
-    // flight across the escape scan; the result is stored last)
+    // destination of each 512-word step
     uint16_t* q = nullptr;
     if (lane < static_cast<int>(kStepsPerTile)) {
       const uint32_t sb = lane * kStepWords;
@@ -1573,18 +1401,16 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
         if (layout_run(N.L, g) >= kStepWords) q = N.dst + layout_addr(N.L, g);
       }
     }
-    if (mode == 5 && count > 0) {
-      const uint32_t covered = producer_escapes(N, count, t0, len, d, cursor, cursor_ok, win);
-      if (lane == 0 && covered) atomicAdd(&g_decode_slots[N.slot].covered, covered);
-    }
     if (lane < static_cast<int>(kStepsPerTile)) d.step_dst[lane] = q;
     producer_commit(R, p);
     p.next();
   }
 }
 
+// Every word with its book exponent; EscapePatchKernel then rewrites the
+// escaped words.
 __device__ __forceinline__ void decode_top16_compute(const DecJob& J, const DecDesc& d, const uint8_t* stage,
-                                                     uint64_t t0, uint32_t len, uint32_t hrel, bool escapes,
+                                                     uint64_t t0, uint32_t len, uint32_t hrel,
                                                      const uint32_t (&bk0)[4], const uint32_t (&bk1)[4]) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -1627,20 +1453,6 @@ __device__ __forceinline__ void decode_top16_compute(const DecJob& J, const DecD
       const uint32_t body2 = __byte_perm(B[i >> 1], 0, (i & 1) ? 0x3322 : 0x1100);
       const uint32_t ex = __byte_perm(e[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140) << 7;
       o[i] = (body2 & 0x807F807Fu) | ex;
-    }
-    // the escape map is written only for streams with escapes
-    const uint32_t word = escapes ? d.esc_bits[w0 >> 5] : 0u;
-    const uint32_t eb = (word >> (w0 & 31)) & 0xFFFFu;
-    if (eb) {
-      uint32_t r = d.esc_rank[w0 >> 5] + __popc(word & ((1u << (w0 & 31)) - 1u));
-#pragma unroll
-      for (int i = 0; i < kUnitWords; ++i) {
-        if ((eb >> i) & 1u) {
-          const uint32_t ev = d.esc_exp[r++];
-          const uint32_t sh = (i & 1) * 16;
-          o[i >> 1] = (o[i >> 1] & ~(0x7F80u << sh)) | ((ev << 7) << sh);
-        }
-      }
     }
     store_step(J, d, t0, step, valid, lane, o);
   }
@@ -1716,7 +1528,6 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
     return;
   }
   int book_job = -1, pair_job = -1;
-  uint64_t job_count = 0;                                 // escape count of book_job's stream
   uint32_t bk0[4] = {0, 0, 0, 0}, bk1[4] = {0, 0, 0, 0};  // top16 codebooks of book_job
   DecPos p;
   for (;;) {
@@ -1739,12 +1550,11 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
             bk0[k] = load_u32le(books + 4 * k);
             bk1[k] = load_u32le(books + 16 + 4 * k);
           }
-          job_count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
           book_job = ji;
         }
         const uint32_t hrel =
             J.half <= t0 ? 0u : static_cast<uint32_t>(min(J.half - t0, static_cast<uint64_t>(kTileWords)));
-        decode_top16_compute(J, d, stage, t0, len, hrel, job_count > 0, bk0, bk1);
+        decode_top16_compute(J, d, stage, t0, len, hrel, bk0, bk1);
       } else if (mode == 3) {
         if (ji != pair_job) {
           consumer_sync();  // every warp is done with the previous table
@@ -1765,29 +1575,39 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
   }
 }
 
-// Runs after DecodeKernel in stream order, one CTA per job: a top16 stream
-// whose tiles did not take every escape entry (entries out of position
-// order, or at positions >= n) gets all its entries applied, in entry order
-// per thread; then the job's slot is reset for the next call.  Streams with
-// sorted entries (every stream this library writes) skip the work.
+// Runs after DecodeKernel in stream order: every escape entry of every top16
+// job, one thread per entry (entry indices of a job run to its capacity
+// ceil(n/200); those at or past the stream's count do nothing).  The decode
+// wrote each word with its book exponent; the escaped word is rewritten
+// from its body byte and the entry's exponent, which is what the
+// reference's (w & 0x807F) | (exp << 7) patch of the decoded word gives
+// (kvq_splitzip_cuda.cu:254-284).  Entries may come in any order; positions
+// at or past n are skipped.
+template <int kMax>
+struct PatchBatch {
+  uint32_t jobs;
+  uint64_t entry_start[kMax + 1];
+  DecJob job[kMax];
+};
+
 template <int kMax, int kMode>
-__global__ void __launch_bounds__(kThreads) RepairKernel(const __grid_constant__ DecBatch<kMax> b) {
-  for (uint32_t j = blockIdx.x; j < b.jobs; j += gridDim.x) {
+__global__ void __launch_bounds__(256) EscapePatchKernel(const __grid_constant__ PatchBatch<kMax> b) {
+  const uint64_t total = b.entry_start[b.jobs];
+  int j = 0;
+  for (uint64_t e = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    while (e >= b.entry_start[j + 1]) ++j;
     const DecJob& J = b.job[j];
-    if (job_mode<kMode>(J) != 5) continue;  // uniform across the CTA
+    if (job_mode<kMode>(J) != 5) continue;
+    const uint64_t i = e - b.entry_start[j];
     const uint64_t count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
-    const uint32_t covered = ld_volatile_u32(&g_decode_slots[J.slot].covered);
-    if (covered != count) {
-      const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
-      for (uint64_t i = threadIdx.x; i < count; i += kThreads) {
-        const uint32_t q = entry_pos(entries, i);
-        if (q >= J.n) continue;
-        uint16_t* w = J.dst + layout_addr(J.L, q);
-        *w = static_cast<uint16_t>((*w & 0x807Fu) | (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7));
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) g_decode_slots[J.slot].covered = 0;
+    if (i >= count) continue;
+    const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
+    const uint32_t q = entry_pos(entries, i);
+    if (q >= J.n) continue;
+    const uint32_t body = __ldg(J.src + 5 + q);
+    const uint32_t w = (body & 0x7Fu) | ((body & 0x80u) << 8) | (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7);
+    J.dst[layout_addr(J.L, q)] = static_cast<uint16_t>(w);
   }
 }
 
