@@ -271,8 +271,6 @@ struct EncDesc {
   uint32_t aux;
   uint32_t unused;
   uint64_t prefix;        // auto top16: escapes of the job before this tile
-  uint64_t zero_lo;       // auto top16: this tile's share [zero_lo, zero_hi) of the
-  uint64_t zero_hi;       //   unused escape-slot bytes to clear
   uint32_t wpre[kWarps];  // auto top16: escapes of the tile before each warp's run
 };
 
@@ -512,23 +510,57 @@ __device__ __forceinline__ uint32_t escape_offsets(const uint32_t (&masks)[kStep
   return total;
 }
 
-// Offsets of this lane's escapes inside its warp's run (step 0's lanes,
-// then step 1's), from the per-step masks; no cross-warp exchange.
-__device__ __forceinline__ void warp_escape_offsets(const uint32_t (&masks)[kStepsPerWarp],
-                                                    uint32_t (&off)[kStepsPerWarp]) {
-  static_assert(kStepsPerWarp == 2, "two steps per warp");
+// Escape entries of this warp's run (its kStepsPerWarp steps, in position
+// order), the first at slot `base`.  A step without escapes costs one
+// ballot; when no lane has two escapes in the step (the common case) a
+// lane's offset is the number of lower lanes with one, else a warp scan.
+__device__ __forceinline__ void warp_write_escapes(const EncJob& J, uint64_t t0, const uint16_t* sin,
+                                                   const uint32_t (&masks)[kStepsPerWarp], uint64_t base) {
   const int lane = threadIdx.x & 31;
-  const uint32_t mine = __popc(masks[0]) | (__popc(masks[1]) << 16);
-  uint32_t incl = mine;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lower = (1u << lane) - 1u;
+  uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t t = __shfl_up_sync(kFull, incl, o);
-    if (lane >= o) incl += t;
+  for (int s = 0; s < kStepsPerWarp; ++s) {
+    const uint32_t m = masks[s];
+    const uint32_t lanes = __ballot_sync(kFull, m != 0);
+    if (lanes == 0) continue;  // uniform
+    uint32_t off, total;
+    if (__ballot_sync(kFull, (m & (m - 1)) != 0) == 0) {
+      off = __popc(lanes & lower);
+      total = __popc(lanes);
+    } else {
+      const uint32_t mine = __popc(m);
+      uint32_t incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+      }
+      off = incl - mine;
+      total = __shfl_sync(kFull, incl, 31);
+    }
+    if (m != 0) {
+      const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
+      uint64_t slot = base + off;
+      uint32_t bits = m;
+      do {
+        const uint32_t w = w0 + (__ffs(bits) - 1);
+        bits &= bits - 1;
+        if (slot < J.cap) {
+          const uint32_t pos = static_cast<uint32_t>(t0 + w);
+          uint8_t* en = entries + slot * 5;
+          en[0] = static_cast<uint8_t>(pos);
+          en[1] = static_cast<uint8_t>(pos >> 8);
+          en[2] = static_cast<uint8_t>(pos >> 16);
+          en[3] = static_cast<uint8_t>(pos >> 24);
+          en[4] = static_cast<uint8_t>(sin[w] >> 7);
+        }
+        ++slot;
+      } while (bits);
+    }
+    base += total;
   }
-  const uint32_t excl = incl - mine;
-  const uint32_t total0 = __shfl_sync(kFull, incl, 31) & 0xFFFFu;
-  off[0] = excl & 0xFFFFu;
-  off[1] = total0 + (excl >> 16);
 }
 
 __device__ __forceinline__ void write_escapes(const EncJob& J, uint64_t t0, const uint16_t* sin,
@@ -1016,8 +1048,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   // offset in the job and each warp's offset inside the tile.  Job-level
   // values are read once per job; consecutive tiles keep a running prefix
   // and a register window of 32 tiles' per-warp counts (one load round per
-  // 32 tiles).  The tile's share of the unused escape slots to zero comes
-  // with it.
+  // 32 tiles).  The producer also clears the tile's share of the unused
+  // escape slots.
   const EncJob* hook_job = nullptr;
   uint32_t hook_next = 0, win_first = 0;
   bool hook_top16 = false;
@@ -1035,10 +1067,11 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
     if (&J != hook_job || tile != hook_next) {
       hook_job = &J;
       const uint64_t escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
-      hook_top16 = escapes <= J.cap;
+      // the consumers' choice of kind: top16 unless the stats pass failed
+      hook_top16 = escapes <= J.cap && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch + 4)) == 0;
       zlo0 = 5 * escapes;
       zhi = 5 * J.cap;
-      zshare = zlo0 < zhi ? (zhi - zlo0 + J.tiles - 1) / J.tiles : 0;
+      zshare = hook_top16 && zlo0 < zhi ? (zhi - zlo0 + J.tiles - 1) / J.tiles : 0;
       running = 0;
       if (hook_top16) {
         const uint64_t* groups = reinterpret_cast<const uint64_t*>(J.scratch + 64);
@@ -1073,13 +1106,14 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
       running += total;
     }
     hook_next = tile + 1;
-    if (lane == 0) {
-      d.prefix = prefix;
-      const uint64_t a = min(zhi, zlo0 + zshare * tile);
-      d.zero_lo = a;
-      d.zero_hi = min(zhi, a + zshare);
-    }
+    if (lane == 0) d.prefix = prefix;
     if (lane < kWarps) d.wpre[lane] = wpre;
+    // the tile's share of the unused escape slots, cleared here (no consumer
+    // writes them)
+    uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
+    const uint64_t a = min(zhi, zlo0 + zshare * tile);
+    const uint64_t e = min(zhi, a + zshare);
+    for (uint64_t i = a + lane; i < e; i += 32) entries[i] = 0;
   };
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
                                            const EncPos& p, const EncDesc& desc) {
@@ -1118,16 +1152,10 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
       raw_tile_body(J, t0, len, sin);
       return;
     }
-    // top16: this tile's escapes start at desc.prefix (from the stats pass)
-    {  // zero this tile's share of the unused escape slots (from the producer)
-      uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
-      for (uint64_t i = desc.zero_lo + tid; i < desc.zero_hi; i += kThreads) entries[i] = 0;
-    }
+    // top16: this warp's escapes start at desc.prefix + desc.wpre[warp]
     uint32_t masks[kStepsPerWarp];
     top16_tile_body(J, t0, len, sin, stbl, masks);
-    uint32_t off[kStepsPerWarp];
-    warp_escape_offsets(masks, off);
-    write_escapes(J, t0, sin, masks, off, desc.prefix + desc.wpre[tid >> 5]);
+    warp_write_escapes(J, t0, sin, masks, desc.prefix + desc.wpre[tid >> 5]);
   }, prefix_hook);
 }
 
