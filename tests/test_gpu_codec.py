@@ -76,7 +76,7 @@ def test_top16_encode_flat_matches_oracle(n, rate):
     rng = np.random.Generator(np.random.PCG64(n * 7 + int(rate * 1e4)))
     tables = tables_for(n % 32)
     words = book_words(rng, (n,), splitzip_cuda._DEFAULT_TOP16_CODEBOOKS[(n % 32) * 32:][:32], rate)
-    capacity = max(2 * n, oracle.top16_encoded_bytes(n) + 64 + 8 * ((n + 8191) // 8192))
+    capacity = max(2 * n, splitzip_cuda.top16_capacity(n))
     expected_res, expected = oracle.encode_top16(words, tables, capacity=capacity)
     res, stream = gpu_encode_top16(words, tables, capacity=capacity)
     assert res == expected_res > 0
@@ -88,10 +88,11 @@ def test_top16_encode_declines_like_reference():
     assert gpu_encode_top16(np.zeros(21, np.uint16), tables)[0] == 0   # does not compress
     n = 1 << 16
     enc = oracle.top16_encoded_bytes(n)
-    # room for the stream plus this implementation's tile-scan scratch
+    # room for the stream plus this implementation's per-tile escape counts
     words = np.zeros(n, np.uint16)
-    ok = gpu_encode_top16(words, tables, capacity=enc + 16 + 16 + 8 * (n // 8192))
-    assert ok[0] == enc
+    need = splitzip_cuda.top16_capacity(n)
+    assert gpu_encode_top16(words, tables, capacity=need)[0] == enc
+    assert gpu_encode_top16(words, tables, capacity=need - 1)[0] == 0
     assert gpu_encode_top16(words, tables, capacity=enc + 4)[0] == 0
 
 

@@ -220,7 +220,9 @@ EncJob base_job(const uint16_t* src, const Layout& L, uint8_t* dst, const uint8_
   return j;
 }
 
-// top16: the reference's rules (.cu:385-395) plus room for the tile scan.
+// top16: the reference's rules (.cu:385-395) plus room for the escape
+// counts of the statistics pass (the auto encode's layout, without the
+// bitmap).  The unused escape slots are cleared by the encode kernel.
 bool prepare_top16(const uint16_t* src, const Layout& L, uint8_t* dst, uint64_t capacity,
                    const uint8_t* tables, Prepared& p) {
   const uint64_t n = L.n;
@@ -229,13 +231,12 @@ bool prepare_top16(const uint16_t* src, const Layout& L, uint8_t* dst, uint64_t 
   if (encoded >= n * 2 || ((encoded + 3) & ~3ULL) + 8 > capacity) return false;
   const uint64_t tiles = tiles_for(n);
   const uint64_t so = align16_from(dst, encoded);
-  const uint64_t scratch = top16_scratch_bytes(tiles);
+  const uint64_t scratch = auto_scratch_bytes(tiles);
   if (so + scratch > capacity) return false;
   p.job = base_job(src, L, dst, tables);
   p.job.scratch = dst + so;
-  const uint64_t entries = 5 + n + (n + 1) / 2;
-  p.zero_ptr = dst + entries;
-  p.zero_bytes = so + scratch - entries;
+  p.zero_ptr = dst + so;
+  p.zero_bytes = scratch;
   p.result = encoded;
   return true;
 }
@@ -342,12 +343,17 @@ long long launch_persistent(Kernel kernel, const char* name, size_t dyn_smem, co
 template <int kMax>
 long long launch_encode_kernels(EncOp op, const EncBatch<kMax>& b, uint32_t tiles, cudaStream_t stream) {
   switch (op) {
-    case EncOp::kTop16:
-      return launch_persistent(EncodeTop16Kernel<kMax>, "EncodeTop16Kernel", kEncSmemBytes, b, tiles, stream);
+    case EncOp::kTop16: {
+      // escape counts of every tile, then the top16 streams at known offsets
+      const long long rc =
+          launch_persistent(PresenceKernel<kMax, kStatsTop16>, "Top16StatsKernel", kEncSmemBytes, b, tiles, stream);
+      if (rc < 0) return rc;
+      return launch_persistent(EncodeAutoKernel<kMax, true>, "EncodeTop16Kernel", kEncSmemBytes, b, tiles, stream);
+    }
     case EncOp::kFixed6:
     case EncOp::kFixed5: {
       const long long rc =
-          launch_persistent(PresenceKernel<kMax, false>, "PresenceKernel", kEncSmemBytes, b, tiles, stream);
+          launch_persistent(PresenceKernel<kMax, kStatsPresence>, "PresenceKernel", kEncSmemBytes, b, tiles, stream);
       if (rc < 0) return rc;
       return op == EncOp::kFixed6
                  ? launch_persistent(EncodeFixedKernel<kMax, 6>, "EncodeFixed6Kernel", kEncSmemBytes, b, tiles, stream)
@@ -355,9 +361,9 @@ long long launch_encode_kernels(EncOp op, const EncBatch<kMax>& b, uint32_t tile
     }
     case EncOp::kAuto: {
       const long long rc =
-          launch_persistent(PresenceKernel<kMax, true>, "StatsKernel", kEncSmemBytes, b, tiles, stream);
+          launch_persistent(PresenceKernel<kMax, kStatsAuto>, "StatsKernel", kEncSmemBytes, b, tiles, stream);
       if (rc < 0) return rc;
-      return launch_persistent(EncodeAutoKernel<kMax>, "EncodeAutoKernel", kEncSmemBytes, b, tiles, stream);
+      return launch_persistent(EncodeAutoKernel<kMax, false>, "EncodeAutoKernel", kEncSmemBytes, b, tiles, stream);
     }
   }
   return 0;
@@ -1203,7 +1209,7 @@ namespace {
 // 16384 tiles); the array is 16 + 8*512 + 8*16384 = 135184 bytes.
 constexpr uint64_t kNoAllocMaxWords = 1ull << 27;
 constexpr uint64_t kNoAllocTiles = (kNoAllocMaxWords + kTileWords - 1) / kTileWords;
-constexpr uint64_t kNoAllocScratchBytes = top16_scratch_bytes(kNoAllocTiles);
+constexpr uint64_t kNoAllocScratchBytes = auto_scratch_bytes(kNoAllocTiles);
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -1273,14 +1279,10 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned lon
   b.tile_start[0] = 0;
   b.tile_start[1] = b.job[0].tiles;
   // Every call shares the array and finds the previous call's contents in
-  // it: clear the ticket, error flag, group and status words, and the escape
-  // entries of the stream (unused slots must read zero).
-  const uint64_t entries = 5 + n + (n + 1) / 2;
-  cudaError_t st = cudaMemsetAsync(dst + entries, 0, encoded - entries, stream);
+  // it: clear the escape total, error flag, group words and tile counts (the
+  // encode kernel clears the stream's unused escape slots).
+  const cudaError_t st = cudaMemsetAsync(scratch, 0, auto_scratch_bytes(b.job[0].tiles), stream);
   if (st != cudaSuccess) return Fail("cudaMemsetAsync", st);
-  st = cudaMemsetAsync(scratch, 0, top16_scratch_bytes(b.job[0].tiles), stream);
-  if (st != cudaSuccess) return Fail("cudaMemsetAsync", st);
-  const long long rc =
-      launch_persistent(EncodeTop16Kernel<1>, "EncodeTop16Kernel", kEncSmemBytes, b, b.job[0].tiles, stream);
+  const long long rc = launch_encode_kernels(EncOp::kTop16, b, b.job[0].tiles, stream);
   return rc < 0 ? rc : static_cast<long long>(encoded);
 }

@@ -25,7 +25,6 @@
 namespace ukv {
 
 constexpr int kMaxBatch = 96;
-constexpr uint64_t kStatusFlag = 1ull << 63;
 constexpr int kEncStages = 4;  // ring depth of the encode kernels (16 KiB stages)
 constexpr int kDecStages = 3;  // ring depth of the decode kernel (16.1 KiB stages + descriptors)
 constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 16 KiB of words
@@ -123,17 +122,12 @@ __device__ __forceinline__ Chunk cta_chunk(uint32_t total) {
 }
 
 // Scratch layouts (byte offsets from EncJob::scratch).
-//   top16 encode: [0,4) batch tile ticket (job 0), [4,8) error flag,
-//     [16, 16+8G) group words (done<<32 | escapes of 32 tiles),
-//     [16+8G, 16+8G+8T) tile status words (flag | escapes).
 //   fixed encode: [0,32) high-byte bitmap, [32,36) error flag.
-//   auto encode:  [0,4) escape total, [4,8) error flag, [16,48) bitmap,
-//     [64, 64+8G) group words (escapes of 32 tiles), then from the next
-//     16-byte boundary 16T bytes of escape counts per (tile, warp) as u16.
+//   auto and top16 encode: [0,4) escape total, [4,8) error flag, [16,48)
+//     bitmap (auto only), [64, 64+8G) group words (escapes of 32 tiles),
+//     then from the next 16-byte boundary 16T bytes of escape counts per
+//     (tile, warp) as u16.
 __host__ __device__ constexpr uint64_t groups_for(uint64_t tiles) { return (tiles + 31) / 32; }
-__host__ __device__ constexpr uint64_t top16_scratch_bytes(uint64_t tiles) {
-  return 16 + 8 * groups_for(tiles) + 8 * tiles;
-}
 __host__ __device__ constexpr uint64_t auto_counts_offset(uint64_t tiles) {
   return 64 + (8 * groups_for(tiles) + 15) / 16 * 16;
 }
@@ -476,40 +470,6 @@ __device__ __forceinline__ void top16_tile_body(const EncJob& J, uint64_t t0, ui
   }
 }
 
-// CTA-wide exclusive offsets of this lane's escapes (position order: warp,
-// then step, then lane).  Returns the tile total; off[s] = offset of the
-// lane's first escape of step s.  Uses s_wtot[2][kWarps] (alternate two of
-// them tile by tile) and one consumer barrier.
-__device__ __forceinline__ uint32_t escape_offsets(const uint32_t (&masks)[kStepsPerWarp],
-                                                   uint32_t (*s_wtot)[kWarps],
-                                                   uint32_t (&off)[kStepsPerWarp]) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const uint32_t mine = __popc(masks[0]) | (__popc(masks[1]) << 16);
-  uint32_t incl = mine;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t t = __shfl_up_sync(kFull, incl, o);
-    if (lane >= o) incl += t;
-  }
-  const uint32_t excl = incl - mine;
-  if (lane == 31) {
-    s_wtot[0][warp] = incl & 0xFFFFu;
-    s_wtot[1][warp] = incl >> 16;
-  }
-  consumer_sync();
-  uint32_t before = 0, total = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    const uint32_t t = s_wtot[0][w] + s_wtot[1][w];
-    if (w < warp) before += t;
-    total += t;
-  }
-  off[0] = before + (excl & 0xFFFFu);
-  off[1] = before + s_wtot[0][warp] + (excl >> 16);
-  return total;
-}
-
 // Escape entries of this warp's run (its kStepsPerWarp steps, in position
 // order), the first at slot `base`.  A step without escapes costs one
 // ballot; when no lane has two escapes in the step (the common case) a
@@ -563,35 +523,6 @@ __device__ __forceinline__ void warp_write_escapes(const EncJob& J, uint64_t t0,
   }
 }
 
-__device__ __forceinline__ void write_escapes(const EncJob& J, uint64_t t0, const uint16_t* sin,
-                                              const uint32_t (&masks)[kStepsPerWarp],
-                                              const uint32_t (&off)[kStepsPerWarp], uint64_t prefix) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
-#pragma unroll
-  for (int s = 0; s < kStepsPerWarp; ++s) {
-    uint32_t m = masks[s];
-    if (!m) continue;
-    const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-    uint64_t slot = prefix + off[s];
-    while (m) {
-      const int j = __ffs(m) - 1;
-      m &= m - 1;
-      if (slot < J.cap) {
-        const uint32_t pos = static_cast<uint32_t>(t0 + w0 + j);
-        uint8_t* e = entries + slot * 5;
-        e[0] = static_cast<uint8_t>(pos);
-        e[1] = static_cast<uint8_t>(pos >> 8);
-        e[2] = static_cast<uint8_t>(pos >> 16);
-        e[3] = static_cast<uint8_t>(pos >> 24);
-        e[4] = static_cast<uint8_t>((sin[w0 + j] >> 7) & 0xFFu);
-      }
-      ++slot;
-    }
-  }
-}
-
 __device__ __forceinline__ void write_top16_header(uint8_t* dst, uint64_t total, uint64_t cap,
                                                    bool error) {
   dst[0] = (total > cap || error) ? 255 : 5;
@@ -602,124 +533,33 @@ __device__ __forceinline__ void write_top16_header(uint8_t* dst, uint64_t total,
   dst[4] = static_cast<uint8_t>(cnt >> 24);
 }
 
-// Bounded wait for a published tile status; returns its count (0 on timeout).
-__device__ __forceinline__ uint64_t wait_status(const uint64_t* p, uint32_t* error) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    const uint64_t s = ld_acquire(p);
-    if (s & kStatusFlag) return s & ~kStatusFlag;
-    __nanosleep(64);
-  }
-  raise_error(error);
-  return 0;
-}
-
-// Bounded wait for a complete group of 32 tiles; returns its escape sum.
-__device__ __forceinline__ uint64_t wait_group(const uint64_t* p, uint32_t* error) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    const uint64_t s = ld_relaxed_u64(p);
-    if ((s >> 32) >= 32) return s & 0xFFFFFFFFull;
-    __nanosleep(64);
-  }
-  raise_error(error);
-  return 0;
-}
-
-// Two-level counting scan across the tiles of one job, run by one warp.
-// Tile `tile` publishes its count to its status word and to its group of 32
-// tiles, then sums (a) complete groups before its group and (b) the tiles of
-// its own group before it.  Tiles are numbered by ticket, so every tile it
-// waits on is held by a running CTA; the wait never depends on later tiles.
-__device__ uint64_t tile_prefix(uint8_t* scratch, uint32_t tiles, uint32_t tile, uint32_t count,
-                                uint32_t* error) {
-  const int lane = threadIdx.x & 31;
-  uint64_t* groups = reinterpret_cast<uint64_t*>(scratch + 16);
-  uint64_t* status = groups + groups_for(tiles);
-  const uint32_t g = tile >> 5;
-  const uint32_t r = tile & 31;
-  if (lane == 0) {
-    st_release(&status[tile], kStatusFlag | count);
-    atomicAdd(reinterpret_cast<unsigned long long*>(&groups[g]), (1ull << 32) | count);
-  }
-  uint64_t v = 0;
-  if (static_cast<uint32_t>(lane) < r) v = wait_status(&status[(g << 5) + lane], error);
-  uint64_t prefix = warp_sum(v);
-  for (uint32_t base = 0; base < g; base += 32) {
-    v = 0;
-    if (base + lane < g) v = wait_group(&groups[base + lane], error);
-    prefix += warp_sum(v);
-  }
-  return prefix;
-}
-
-// top16 encode: tiles by ticket (ascending within each CTA; the producer
-// takes a ticket once it holds a free stage), escape offsets by the
-// two-level scan.
-template <int kMax>
-__global__ void __launch_bounds__(kCtaThreads, 3) EncodeTop16Kernel(const __grid_constant__ EncBatch<kMax> b) {
-  extern __shared__ __align__(128) uint8_t ring[];
-  __shared__ uint32_t stbl[512];
-  __shared__ EncRing R;
-  __shared__ EncDesc D[kEncStages];
-  __shared__ uint32_t s_wtot[2][2][kWarps];
-  __shared__ uint64_t s_prefix[2];
-  const int tid = threadIdx.x;
-  ring_init(R);
-  __syncthreads();
-  if ((tid >> 5) == kProducerWarp) {
-    uint32_t* ticket = reinterpret_cast<uint32_t*>(b.job[0].scratch);
-    encode_producer<kMax>(b, ring, R, D, [&]() {
-      uint32_t t = 0;
-      if ((tid & 31) == 0) t = atomicAdd(ticket, 1u);
-      return __shfl_sync(kFull, t, 0);
-    });
-    return;
-  }
-  int table_job = -1;
-  encode_consumer<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos& p, const EncDesc&) {
-    uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 4);
-    if (j != table_job) {  // uniform across the consumers
-      consumer_sync();     // every warp is done with the previous table
-      load_top16_table(J.tables, stbl);
-      table_job = j;
-      consumer_sync();
-    }
-    const uint64_t t0 = static_cast<uint64_t>(tile) * kTileWords;
-    const uint32_t len = tile_len(J.n, t0);
-    uint32_t masks[kStepsPerWarp];
-    top16_tile_body(J, t0, len, sin, stbl, masks);
-    uint32_t off[kStepsPerWarp];
-    const uint32_t count = escape_offsets(masks, s_wtot[p.k & 1], off);
-    if ((tid >> 5) == 0) {
-      const uint64_t prefix = tile_prefix(J.scratch, J.tiles, tile, count, error);
-      if (tid == 0) s_prefix[p.k & 1] = prefix;
-    }
-    consumer_sync();
-    const uint64_t prefix = s_prefix[p.k & 1];
-    write_escapes(J, t0, sin, masks, off, prefix);
-    if (tile == J.tiles - 1 && tid == 0) {
-      write_top16_header(J.dst, prefix + count, J.cap, ld_volatile_u32(error) != 0);
-    }
-  });
-}
-
 // ------------------------------------------------- presence / auto stats
 
-// High-byte presence of every word (-> job bitmap) and, for kStats, the
-// top16 escape count of every tile (-> tile count, group sum, job total; each
-// warp adds its own share, so no CTA barrier is needed for the counts).
+// Statistics pass, by kKind:
+//   kStatsPresence: high-byte presence of every word (-> job bitmap), for the
+//     fixed6 / fixed5 palette;
+//   kStatsAuto: the bitmap and the top16 escape count of every tile (-> tile
+//     count per warp, group sum, job total; each warp adds its own share, so
+//     no CTA barrier is needed for the counts), for the auto encode;
+//   kStatsTop16: the escape counts alone, for the explicit top16 encode.
 //
 // The presence table holds high byte h at index h ^ (sign << 2), so that a
 // value and its negation (which share every other bit of h) fall in
 // different shared-memory banks.  Word order does not matter here, so each
 // lane reads two 16-byte chunks that are contiguous across the warp
-// (conflict-free).  Once a job's running escape total exceeds its top16
-// capacity the job cannot be top16 and its remaining tiles skip the escape
-// count (the producer reads the total for each tile).
+// (conflict-free).  For kStatsAuto, once a job's running escape total
+// exceeds its top16 capacity the job cannot be top16 and its remaining tiles
+// skip the escape count (the producer reads the total for each tile).  The
+// explicit top16 encode counts every tile: an overflowing stream still holds
+// the first `cap` escapes, so every tile's offset must be exact.
 __device__ __forceinline__ uint32_t presence_index(uint32_t h) { return h ^ ((h >> 5) & 4u); }
 
-template <int kMax, bool kStats>
+enum StatsKind { kStatsPresence = 0, kStatsAuto = 1, kStatsTop16 = 2 };
+
+template <int kMax, int kKind>
 __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_constant__ EncBatch<kMax> b) {
+  constexpr bool kStats = kKind != kStatsPresence;
+  constexpr bool kPresence = kKind != kStatsTop16;
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint8_t spres[256];
   __shared__ uint8_t sesc[512];  // 1 where the exponent has no top16 code
@@ -743,7 +583,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
   };
   // aux = 1 when the job's escapes already exceed its top16 capacity
   auto over_cap = [](const EncJob& J, uint32_t, EncDesc& d) {
-    const bool over = kStats && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap;
+    const bool over = kKind == kStatsAuto && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap;
     if ((threadIdx.x & 31) == 0) d.aux = over;
   };
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
@@ -752,7 +592,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     if (j != pres_job || (kStats && j != table_job)) {  // uniform across the consumers
       consumer_sync();
       if (j != pres_job) {
-        if (pres_job >= 0) flush(b.job[pres_job]);
+        if (kPresence && pres_job >= 0) flush(b.job[pres_job]);
         pres_job = j;
       }
       if (kStats && j != table_job) {
@@ -774,16 +614,20 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
         const uint4 v0 = *reinterpret_cast<const uint4*>(w);
         const uint4 v1 = *reinterpret_cast<const uint4*>(w + 256);
         const uint32_t x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        if (kPresence) {
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          const uint32_t y = x[p] ^ ((x[p] >> 5) & 0x04000400u);
-          spres[__byte_perm(y, 0, 0x4441)] = 1;
-          spres[y >> 24] = 1;
+          for (int p = 0; p < 8; ++p) {
+            const uint32_t y = x[p] ^ ((x[p] >> 5) & 0x04000400u);
+            spres[__byte_perm(y, 0, 0x4441)] = 1;
+            spres[y >> 24] = 1;
+          }
         }
         if (count) {
+          // exponent bytes: byte 1 of x << 1 (even word), x >> 23 (odd word)
+          const uint8_t* tb = poff ? sesc + 256 : sesc;
 #pragma unroll
           for (int p = 0; p < 8; ++p)
-            escapes += sesc[((x[p] >> 7) & 0xFFu) | poff] + sesc[((x[p] >> 23) & 0xFFu) | poff];
+            escapes += tb[__byte_perm(x[p] << 1, 0, 0x4441)] + tb[(x[p] >> 23) & 0xFFu];
         }
       }
     } else {
@@ -795,7 +639,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
         const uint64_t g = t0 + w0;
         for (uint32_t i = 0; i < valid; ++i) {
           const uint32_t w = sin[w0 + i];
-          spres[presence_index(w >> 8)] = 1;
+          if (kPresence) spres[presence_index(w >> 8)] = 1;
           if (count) escapes += sesc[((g + i) >= J.half ? 256 : 0) + ((w >> 7) & 0xFFu)];
         }
       }
@@ -811,7 +655,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
       }
     }
   }, over_cap);
-  if (warp == kProducerWarp) return;
+  if (warp == kProducerWarp || !kPresence) return;
   consumer_sync();
   if (pres_job >= 0) flush(b.job[pres_job]);
 }
@@ -1028,9 +872,13 @@ __device__ __forceinline__ void raw_tile_body(const EncJob& J, uint64_t t0, uint
 // fallback order (vllm_connector.py:3104-3118, 4557-4633): top16 if the
 // escapes fit, else fixed6 if <= 64 high bytes, else raw mode 6 when the
 // buffer holds it, else a fixed6 overflow stream (mode 255) for the host.
+// With kTop16Only (the explicit top16 encode, after a kStatsTop16 pass)
+// every job is coded as top16; one whose escapes exceed its capacity gets
+// the reference's overflow form (mode byte 255, count = cap, the first cap
+// escapes).
 enum AutoKind { kAutoTop16 = 0, kAutoFixed6 = 1, kAutoRaw = 2, kAutoOverflow = 3 };
 
-template <int kMax>
+template <int kMax, bool kTop16Only>
 __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_constant__ EncBatch<kMax> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint32_t stbl[512];
@@ -1068,7 +916,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
       hook_job = &J;
       const uint64_t escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
       // the consumers' choice of kind: top16 unless the stats pass failed
-      hook_top16 = escapes <= J.cap && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch + 4)) == 0;
+      hook_top16 = kTop16Only ||
+                   (escapes <= J.cap && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch + 4)) == 0);
       zlo0 = 5 * escapes;
       zhi = 5 * J.cap;
       zshare = hook_top16 && zlo0 < zhi ? (zhi - zlo0 + J.tiles - 1) / J.tiles : 0;
@@ -1119,19 +968,22 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
                                            const EncPos& p, const EncDesc& desc) {
     if (j != setup_job) {  // uniform across the consumers
       consumer_sync();     // every warp is done with the previous ranks/table
-      uint32_t distinct, rank;
-      bool present;
-      palette_ranks(reinterpret_cast<const uint32_t*>(J.scratch + 16), srank, distinct, present, rank);
+      uint32_t distinct = 0, rank = 0;
+      bool present = false;
+      if (!kTop16Only) palette_ranks(reinterpret_cast<const uint32_t*>(J.scratch + 16), srank, distinct, present, rank);
       escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
       const bool err = ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch + 4)) != 0;
-      kind = err ? kAutoOverflow
+      kind = kTop16Only ? kAutoTop16
+           : err ? kAutoOverflow
            : escapes <= J.cap ? kAutoTop16
            : distinct <= 64 ? kAutoFixed6
            : J.raw_ok ? kAutoRaw : kAutoOverflow;
       if (tile == 0 || setup_job < 0) {
         // the CTA holding tile 0 writes the header
         if (tile == 0) {
-          if (kind == kAutoOverflow) write_fixed_header<6>(J.dst, distinct > 64 ? distinct : 65, present, rank, true);
+          if (kTop16Only) {
+            if (tid == 0) write_top16_header(J.dst, escapes, J.cap, err);
+          } else if (kind == kAutoOverflow) write_fixed_header<6>(J.dst, distinct > 64 ? distinct : 65, present, rank, true);
           else if (kind == kAutoFixed6) write_fixed_header<6>(J.dst, distinct, present, rank, false);
           else if (kind == kAutoRaw && tid == 0) J.dst[0] = 6;
           else if (kind == kAutoTop16 && tid == 0) write_top16_header(J.dst, escapes, J.cap, false);

@@ -669,6 +669,16 @@ def torchop_capacity(n: int) -> int:
     return (1 + 2 * n + 15) // 16 * 16 + 416 + 16
 
 
+def top16_capacity(n: int) -> int:
+    """Stream-buffer bytes for the top16 encoders (kvq_splitzip_bf16_encode_top16
+    and its _blocks / _batch forms) with a 16-byte aligned buffer: the stream,
+    then from its next 16-byte boundary the escape counts of the statistics
+    pass.  The _noalloc form needs only the reference's rule."""
+    tiles = (n + 8191) // 8192
+    scratch = 64 + (8 * ((tiles + 31) // 32) + 15) // 16 * 16 + 16 * tiles
+    return (top16_stream_bytes(n) + 15) // 16 * 16 + scratch
+
+
 def auto_capacity(n: int, raw: bool = True) -> int:
     """Stream-buffer bytes for encode_auto_batch: room for the largest form
     (raw mode 6 when ``raw``) plus the statistics scratch."""
