@@ -8,7 +8,6 @@
 //   its bytes by the run's misalignment, borrowing the next lane's first
 //   bytes, so every interior store is an aligned S-byte store.  Only the two
 //   end slots of a run are written bytewise, clipped to the run.
-// * Release/acquire helpers for the decoupled look-back of the escape scan.
 #pragma once
 
 #include <cstdint>
@@ -23,9 +22,6 @@ constexpr int kStepWords = 32 * kUnitWords;           // 512 words per warp step
 constexpr int kStepsPerWarp = 2;
 constexpr int kTileWords = kWarps * kStepsPerWarp * kStepWords;  // 8192
 constexpr unsigned kFull = 0xffffffffu;
-// Bounded waits: iterations of a polling loop before a wait is abandoned and
-// the error flag is raised (each iteration is at least a few hundred ns).
-constexpr uint32_t kWaitLimit = 1u << 22;
 
 // ---------------------------------------------------------------- layouts
 
@@ -130,16 +126,6 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t 
           smem_addr(sdst)),
       "l"(gsrc), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
-}
-
-__device__ __forceinline__ void st_release(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ uint64_t ld_acquire(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
 }
 
 __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {

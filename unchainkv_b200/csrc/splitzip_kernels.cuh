@@ -143,12 +143,6 @@ __device__ __forceinline__ void raise_error(uint32_t* flag) {
   atomicAdd(&g_device_errors, 1u);
 }
 
-__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ uint32_t tile_len(uint64_t n, uint64_t t0) {
   return static_cast<uint32_t>(n - t0 < kTileWords ? n - t0 : kTileWords);
 }
