@@ -420,16 +420,15 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
     return rc;
   } else {
     if (rc < 0) return rc;
-    // the escaped words of the top16 streams, one thread per entry
+    // the escaped words of the top16 streams, one thread per entry; the grid
+    // covers the largest job's capacity, the jobs go one after another
     static thread_local PatchBatch<kMax> pb;
     pb.jobs = b.jobs;
     uint64_t entries = 0;
     for (size_t i = 0; i < count; ++i) {
-      pb.entry_start[i] = entries;
       pb.job[i] = b.job[i];
-      entries += b.job[i].cap;
+      entries = std::max<uint64_t>(entries, b.job[i].cap);
     }
-    pb.entry_start[count] = entries;
     int device = 0, sms = 0;
     cudaError_t st = cudaGetDevice(&device);
     if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);

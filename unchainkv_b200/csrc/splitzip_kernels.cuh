@@ -1460,28 +1460,34 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
 template <int kMax>
 struct PatchBatch {
   uint32_t jobs;
-  uint64_t entry_start[kMax + 1];
   DecJob job[kMax];
 };
 
 template <int kMax, int kMode>
 __global__ void __launch_bounds__(256) EscapePatchKernel(const __grid_constant__ PatchBatch<kMax> b) {
-  const uint64_t total = b.entry_start[b.jobs];
-  int j = 0;
-  for (uint64_t e = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
-       e += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    while (e >= b.entry_start[j + 1]) ++j;
-    const DecJob& J = b.job[j];
-    if (job_mode<kMode>(J) != 5) continue;
-    const uint64_t i = e - b.entry_start[j];
-    const uint64_t count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
-    if (i >= count) continue;
-    const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
-    const uint32_t q = entry_pos(entries, i);
-    if (q >= J.n) continue;
-    const uint32_t body = __ldg(J.src + 5 + q);
-    const uint32_t w = (body & 0x7Fu) | ((body & 0x80u) << 8) | (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7);
-    J.dst[layout_addr(J.L, q)] = static_cast<uint16_t>(w);
+  const uint64_t first = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  // the top16 jobs, 32 at a time (lane k reads job base + k's mode byte, all
+  // in flight together); for each, the grid strides over the entries its
+  // stream holds
+  const uint32_t lane = threadIdx.x & 31;
+  for (uint32_t base = 0; base < b.jobs; base += 32) {
+    const uint32_t mine = base + lane;
+    uint32_t jobs = __ballot_sync(kFull, mine < b.jobs && job_mode<kMode>(b.job[mine]) == 5);
+    while (jobs) {
+      const DecJob& J = b.job[base + __ffs(jobs) - 1];
+      jobs &= jobs - 1;
+      const uint64_t count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
+      const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
+      for (uint64_t i = first; i < count; i += stride) {
+        const uint32_t q = entry_pos(entries, i);
+        if (q >= J.n) continue;
+        const uint32_t body = __ldg(J.src + 5 + q);
+        const uint32_t w =
+            (body & 0x7Fu) | ((body & 0x80u) << 8) | (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7);
+        J.dst[layout_addr(J.L, q)] = static_cast<uint16_t>(w);
+      }
+    }
   }
 }
 
