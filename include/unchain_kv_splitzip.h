@@ -313,9 +313,13 @@ KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned long long src_
  * One request of a decode-attention batch: its transfer stream of one layer
  * (the codec's output for the request's `blocks` paged blocks, K plane then
  * V plane, of shape [16 tokens, 8 kv heads, 128 dims] per block: fixed6
- * mode 3 or raw mode 6), the number of valid tokens (the last block may be
- * partial), and its query and output, bf16 [8 * group][128] (q head
- * kv_head * group + i attends with kv head kv_head). */
+ * mode 3, raw mode 6, or top16 mode 5 with `tables_ptr`, the layer's
+ * 544-byte table, and its escape entries sorted by position as this
+ * library's encoders write them), the number of valid tokens (the last
+ * block may be partial), and its query and output, bf16 [8 * group][128]
+ * (q head kv_head * group + i attends with kv head kv_head).  tables_ptr
+ * may be 0 for requests that are not top16.  (ABI revision 3 added
+ * tables_ptr.) */
 typedef struct kvq_splitzip_attn_request {
   unsigned long long stream_ptr;
   unsigned long long stream_bytes;
@@ -323,6 +327,7 @@ typedef struct kvq_splitzip_attn_request {
   unsigned long long ctx_tokens;
   unsigned long long q_ptr;
   unsigned long long out_ptr;
+  unsigned long long tables_ptr;
 } kvq_splitzip_attn_request;
 
 /* Device workspace bytes kvq_splitzip_attention_decode needs for this batch
@@ -335,8 +340,9 @@ KVQ_API long long kvq_splitzip_attention_workspace_bytes(const kvq_splitzip_attn
  * and V read from the streams, fp32 accumulation, bf16 output.  group: q
  * heads per kv head, 1..16; count: 1..64 requests.  Returns count, 0 if
  * declined (shape, sizes or workspace too small), -1 on a CUDA error.  A
- * stream whose mode byte is not 3 or 6 yields zeros for its request and
- * counts one device error. */
+ * stream whose mode byte is not 3, 6 or (with tables) 5 yields zeros for
+ * its request and counts one device error, as do top16 entries found out
+ * of order. */
 KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_attn_request* reqs, unsigned long long count,
                                                 unsigned long long group, unsigned long long workspace_ptr,
                                                 unsigned long long workspace_bytes, unsigned long long stream_ptr);

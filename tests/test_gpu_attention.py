@@ -31,10 +31,35 @@ def bf16_to_f32(words):
     return (words.astype(np.uint32) << 16).view(np.float32)
 
 
+BOOKS = np.stack([np.arange(116, 132), np.arange(117, 133)]).astype(np.uint8)  # K, V exponents
+TABLE = np.frombuffer(S.build_top16_tables(bytes(BOOKS.reshape(-1))), np.uint8)
+
+
+def top16_words(rng, shape, escape_rate, hot=None):
+    """Words whose exponents come from the plane's 16-entry book, except
+    escapes at `escape_rate` (half of them large: exponent 136, about 512,
+    so that an unpatched escape shows), plus all of `hot` (a boolean mask)."""
+    plane = np.zeros(shape, np.int64)
+    plane[1] = 1
+    exp = BOOKS[plane, rng.integers(0, 16, shape)].astype(np.int64)
+    esc = rng.random(shape) < escape_rate
+    if hot is not None:
+        esc |= hot
+    exp[esc] = np.where(rng.random(int(esc.sum())) < 0.5, 110, 136)
+    return ((rng.integers(0, 2, shape) << 15) | (exp << 7) | rng.integers(0, 128, shape)).astype(np.uint16)
+
+
 def request(seed, ctx, layer, mode):
     """Words [2, blocks*16, 8, 128] of one request (config[0] distribution,
-    stale values in the unused tail of the last block) and its stream."""
+    stale values in the unused tail of the last block; for top16, exponents
+    from a 16-entry book per plane with 0.3% escapes) and its stream."""
     blocks = -(-ctx // BT)
+    if mode == 5:
+        rng = np.random.Generator(np.random.PCG64(seed))
+        words = top16_words(rng, (2, blocks * BT, HEADS, DIM), 0.003)
+        res, stream = oracle.encode_top16(words.reshape(-1), TABLE)
+        assert stream[0] == 5
+        return words, stream[:res]
     words = W.draw_tokens(seed, W.channel_scales(layer), blocks * BT)
     if mode == 3:
         res, stream = oracle.encode_mode(words.reshape(-1), bits=6)
@@ -61,23 +86,33 @@ def reference(q, words, ctx, group):
 
 
 def place(stream, aligned):
-    """Upload a stream at an address 15 mod 16 (planes on 16-byte
-    boundaries) or at a 16-byte aligned one (planes 1 byte past them)."""
-    if aligned:
+    """Upload a stream at an address 15 mod 16 (fixed6 and raw planes on
+    16-byte boundaries), at 11 mod 16 (aligned=11: top16 planes on them), or
+    at a 16-byte aligned one (planes past them)."""
+    if aligned is True:
         buf = S.attention_stream_buffer(stream.size, "cuda")
+        buf.copy_(torch.from_numpy(stream.copy()))
+        return buf
+    if aligned:
+        raw = torch.empty(stream.size + 32, dtype=torch.uint8, device="cuda")
+        start = (aligned - raw.data_ptr()) % 16
+        buf = raw[start:start + stream.size]
         buf.copy_(torch.from_numpy(stream.copy()))
         return buf
     return torch.from_numpy(stream.copy()).cuda()
 
 
-def run(ctxs, modes, group=4, seed=0, aligned=False):
+def run(ctxs, modes, group=4, seed=0, aligned=False, reqs=None):
     rng = np.random.Generator(np.random.PCG64(seed))
-    reqs = [request(seed * 1000 + i, c, i % 4, m) for i, (c, m) in enumerate(zip(ctxs, modes))]
+    if reqs is None:
+        reqs = [request(seed * 1000 + i, c, i % 4, m) for i, (c, m) in enumerate(zip(ctxs, modes))]
     q = W.bf16_bits(rng.standard_normal((len(ctxs), HEADS * group, DIM)).astype(np.float32))
     q_t = torch.from_numpy(q.view(np.int16)).cuda().view(torch.bfloat16)
     out = torch.full_like(q_t, float("nan"))
     streams = [place(s, aligned) for _, s in reqs]
-    assert S.attention_decode(q_t, streams, ctxs, out) == len(ctxs)
+    table = torch.from_numpy(TABLE.copy()).cuda()
+    tables = [table if m == 5 else None for m in modes] if 5 in modes else None
+    assert S.attention_decode(q_t, streams, ctxs, out, tables=tables) == len(ctxs)
     torch.cuda.synchronize()
     got = bf16_to_f32(out.view(torch.int16).cpu().numpy().view(np.uint16))
     for i, ((words, _), ctx) in enumerate(zip(reqs, ctxs)):
@@ -111,6 +146,32 @@ def test_batch_like_config4():
     rng = np.random.Generator(np.random.PCG64(4))
     ctxs = [int(x) for x in np.exp(rng.uniform(np.log(1024), np.log(8192), size=8))]
     run(ctxs, [3] * 8, seed=4)
+
+
+@pytest.mark.parametrize("aligned", [False, True, 11])
+def test_top16_streams(aligned):
+    """top16 streams (mode 5, with the layer's table): body and nibbles
+    decoded into the fragments, escapes patched from the sorted entries."""
+    run([1, 37, 16, 300, 1029], [5] * 5, seed=6, aligned=aligned)
+
+
+def test_top16_fixed6_and_raw_streams_in_one_batch():
+    run([200, 75, 1000, 33], [5, 3, 6, 5], seed=7)
+    run([64, 64], [3, 3], seed=8, reqs=[request(8000, 64, 0, 3), request(8001, 64, 1, 3)])
+
+
+def test_top16_stage_with_more_escapes_than_it_holds():
+    """A block plane with about 6000 escapes (more than a stage keeps; the
+    rest come from the stream) in a stream still within capacity."""
+    ctx = 64 * BT
+    rng = np.random.Generator(np.random.PCG64(9))
+    shape = (2, ctx, HEADS, DIM)
+    hot = np.zeros(shape, bool)
+    hot[0, 3 * BT:4 * BT] = rng.random((BT, HEADS, DIM)) < 0.37  # the K plane of block 3
+    words = top16_words(rng, shape, 0.0005, hot=hot)
+    res, stream = oracle.encode_top16(words.reshape(-1), TABLE)
+    assert stream[0] == 5 and int(hot.sum()) > 5088
+    run([ctx], [5], seed=9, reqs=[(words, stream[:res])])
 
 
 def test_declines_bad_shapes():

@@ -1040,8 +1040,12 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
     total += q.blocks;
   }
   unsigned grid = 0;
-  if (grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems>, kAttnSmemBytes, kAttnMaxCtas, &grid, kAttnThreads) < 0)
-    return false;
+  bool top16 = false;
+  for (uint64_t r = 0; r < count; ++r) top16 = top16 || reqs[r].tables_ptr != 0;
+  const long long geometry =
+      top16 ? grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems, true>, kAttnSmemBytes, kAttnMaxCtas, &grid, kAttnThreads)
+            : grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems, false>, kAttnSmemBytes, kAttnMaxCtas, &grid, kAttnThreads);
+  if (geometry < 0) return false;
   const uint64_t ctas = std::min<uint64_t>(std::min<uint64_t>(grid, total), kAttnMaxCtas);
   b = AttnLaunch{};
   for (uint64_t r = 0; r < count; ++r) {
@@ -1052,6 +1056,7 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
     a.n = 2 * q.blocks * kAttnBlockWords;
     a.q = reinterpret_cast<const uint16_t*>(q.q_ptr);
     a.out = reinterpret_cast<uint16_t*>(q.out_ptr);
+    a.tables = reinterpret_cast<const uint8_t*>(q.tables_ptr);
     a.ctx = static_cast<uint32_t>(q.ctx_tokens);
   }
   uint32_t items = 0;
@@ -1105,8 +1110,14 @@ extern "C" KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_at
     return 0;
   const cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   b.partials = reinterpret_cast<float*>(workspace_ptr + 16);
+  bool top16 = false;
+  for (uint32_t r = 0; r < b.reqs; ++r) top16 = top16 || b.req[r].tables != nullptr;
   long long prof = prof_begin(stream);
-  AttnKernel<kAttnMaxReqs, kAttnMaxItems><<<b.ctas, kAttnThreads, kAttnSmemBytes, stream>>>(b);
+  if (top16) {
+    AttnKernel<kAttnMaxReqs, kAttnMaxItems, true><<<b.ctas, kAttnThreads, kAttnSmemBytes, stream>>>(b);
+  } else {
+    AttnKernel<kAttnMaxReqs, kAttnMaxItems, false><<<b.ctas, kAttnThreads, kAttnSmemBytes, stream>>>(b);
+  }
   prof_end(prof, "AttnKernel", stream);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return Fail("AttnKernel", st);
@@ -1126,7 +1137,7 @@ extern "C" KVQ_API long long kvq_splitzip_device_errors() {
   return static_cast<long long>(value);
 }
 
-extern "C" KVQ_API long long kvq_splitzip_abi_version() { return 2; }
+extern "C" KVQ_API long long kvq_splitzip_abi_version() { return 3; }
 
 extern "C" KVQ_API long long kvq_splitzip_profile_enable(int on) {
   std::lock_guard<std::mutex> lock(g_prof_mu);

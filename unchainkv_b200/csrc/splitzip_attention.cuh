@@ -75,6 +75,7 @@ struct AttnReq {
   uint64_t n;             // words of the stream: 2 * blocks * kAttnBlockWords
   const uint16_t* q;      // bf16 [kv_heads * group][128]
   uint16_t* out;          // bf16 [kv_heads * group][128]
+  const uint8_t* tables;  // the layer's 544-byte top16 table (books at 512, 528), or null
   uint32_t ctx;           // valid tokens (the last block may be partial)
   uint32_t first_item;
   uint32_t items;
@@ -110,7 +111,10 @@ struct AttnDesc {
   uint32_t pad_y;
   uint32_t valid;  // valid tokens of the block
   uint32_t unused;
-  uint8_t pal[64];  // fixed6 palette of the request
+  uint32_t esc_first;  // top16: the stage's escapes are entries [esc_first, esc_first + esc_count)
+  uint32_t esc_count;
+  uint32_t pad2[2];
+  uint8_t pal[64];  // fixed6 palette of the request; top16: the plane's 16 book exponents
 };
 
 using AttnRing = Ring<kAttnStages>;
@@ -285,9 +289,99 @@ __device__ __forceinline__ uint32_t raw_word_pair(const AttnDesc& d, const uint8
   return w[0];
 }
 
+// ---- top16 streams (the kTop16 kernel).  A stage holds the block plane's
+// body rows (one byte a word) in place of the low-byte rows and its nibble
+// rows (512 bytes a token) in place of the code rows.  Its tail holds the
+// stage's escapes, written by the producer from the stream's sorted entries:
+// a bitmap of the block plane's 16384 words, the escapes before each bitmap
+// word (u16), and the escaped exponents in position order.
+constexpr uint32_t kAttnNibblePitch = kAttnRowWords / 2;
+constexpr uint32_t kAttnEscBitmap = 24640;
+constexpr uint32_t kAttnEscPrefix = kAttnEscBitmap + kAttnBlockWords / 8;
+constexpr uint32_t kAttnEscExps = kAttnEscPrefix + 2 * (kAttnBlockWords / 32);
+constexpr uint32_t kAttnEscExpCap = kAttnStageBytes - kAttnEscExps;  // exponents held in the stage
+static_assert(kAttnCodesOffset + 16 + kAttnBlockTokens * kAttnNibblePitch <= kAttnEscBitmap, "nibble rows");
+static_assert(kAttnEscExps + 1024 <= kAttnStageBytes, "escape exponents");
+
+__device__ __forceinline__ const uint8_t* nibble_row(const uint8_t* stage, uint32_t t) {
+  return stage + kAttnCodesOffset + t * kAttnNibblePitch;
+}
+
+// The top16 inputs of NP word pairs of token t from word `dim` of the row:
+// body bytes B (NP / 2 words) and nibbles N (NP / 4 words).
+template <int NP>
+__device__ __forceinline__ void top16_load(const AttnDesc& d, const uint8_t* stage, uint32_t t, uint32_t dim,
+                                           uint32_t (&B)[NP / 2], uint32_t (&N)[NP / 4]) {
+  const uint8_t* body = low_row(stage, t) + dim;
+  const uint8_t* nib = nibble_row(stage, t) + dim / 2;
+  if ((d.pad_x | d.pad_y) == 0) {  // the stream's regions start on 16-byte boundaries
+#pragma unroll
+    for (int j = 0; j < NP / 8; ++j) {
+      const uint4 v = reinterpret_cast<const uint4*>(body)[j];
+      B[4 * j] = v.x; B[4 * j + 1] = v.y; B[4 * j + 2] = v.z; B[4 * j + 3] = v.w;
+    }
+    if constexpr (NP == 16) {  // 16 nibble bytes, 16-byte aligned
+      const uint4 v = *reinterpret_cast<const uint4*>(nib);
+      N[0] = v.x; N[1] = v.y; N[2] = v.z; N[3] = v.w;
+    } else {  // 8 nibble bytes, 8-byte aligned
+      const uint2 v = *reinterpret_cast<const uint2*>(nib);
+      N[0] = v.x; N[1] = v.y;
+    }
+  } else {
+    smem_read_words<NP / 2>(body, d.pad_x, B);
+    smem_read_words<NP / 4>(nib, d.pad_y, N);
+  }
+}
+
+// A top16 word pair: body bytes of words 4q..4q+3 in bw, their book
+// exponents in e4; `upper` takes words 4q+2, 4q+3 instead of 4q, 4q+1.
+__device__ __forceinline__ uint32_t top16_pair(uint32_t bw, uint32_t e4, bool upper) {
+  const uint32_t body2 = __byte_perm(bw, 0, upper ? 0x3322 : 0x1100);
+  const uint32_t ex = __byte_perm(e4, 0, upper ? 0x4342 : 0x4140) << 7;
+  return (body2 & 0x807F807Fu) | ex;
+}
+
+// Exponent of the stage's escape of rank r (its place in the stage's slice
+// of the entries): from the stage, or from the stream past its capacity.
+__device__ __forceinline__ uint32_t esc_exp(const uint8_t* stage, const uint8_t* entries, uint32_t first,
+                                            uint32_t r) {
+  return r < kAttnEscExpCap ? stage[kAttnEscExps + r] : __ldg(entries + 5ull * (first + r) + 4);
+}
+
+// The escaped words of a word pair: bits2 (bit 0: the low word, bit 1: the
+// high word), rank0 = the stage rank of the low word's escape, or of the
+// high word's when only it escaped.  The exponent field (bits 7..14 of
+// each bf16 word) is replaced, as the reference's patch does.
+__device__ __forceinline__ uint32_t top16_patch(uint32_t w, uint32_t bits2, uint32_t rank0, const uint8_t* stage,
+                                                const uint8_t* entries, uint32_t first) {
+  if (bits2 & 1u) w = (w & ~0x7F80u) | (esc_exp(stage, entries, first, rank0) << 7);
+  if (bits2 & 2u) w = (w & ~0x7F800000u) | (esc_exp(stage, entries, first, rank0 + (bits2 & 1u)) << 23);
+  return w;
+}
+
+// First entry index in [0, total) whose position is >= target (total if
+// none), entries sorted by position; warp-wide, 32 positions per round.
+__device__ __forceinline__ uint32_t entries_lower_bound(const uint8_t* entries, uint32_t total, uint64_t target) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t lo = 0, hi = total;  // the answer lies in [lo, hi]
+  for (int round = 0; round < 8 && hi - lo > 32; ++round) {
+    const uint32_t step = (hi - lo + 31) / 32;
+    const uint32_t idx = lo + (lane + 1) * step - 1;
+    const bool below = idx < hi && entry_pos(entries, idx) < target;
+    const uint32_t k = __popc(__ballot_sync(kFull, below));
+    const uint32_t nlo = lo + k * step;
+    hi = max(nlo, min(hi, lo + (k + 1) * step - 1));
+    lo = nlo;
+  }
+  const uint32_t idx = lo + lane;
+  const bool below = idx < hi && entry_pos(entries, idx) < target;
+  return lo + __popc(__ballot_sync(kFull, below));
+}
+
 // 17 warps, one CTA per SM: a sub-partition hosting 5 of them allows 96
 // registers per thread.
-template <int kMaxR, int kMaxI>
+// kTop16: also reads top16 streams (mode 5), with the requests' tables.
+template <int kMaxR, int kMaxI, bool kTop16>
 __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint32_t pair[4096];
@@ -325,10 +419,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
       const AttnItem& I = b.item[item];
       const AttnReq& Q = b.req[I.req];
       uint32_t mode = __ldg(Q.stream);
-      const uint64_t need = mode == 3 ? 65 + Q.n + 3 * ((Q.n + 3) / 4) : mode == 6 ? 1 + 2 * Q.n : 0;
+      const uint64_t cap = (Q.n + 199) / 200;
+      const uint64_t need = mode == 3 ? 65 + Q.n + 3 * ((Q.n + 3) / 4)
+                            : mode == 6 ? 1 + 2 * Q.n
+                            : (kTop16 && mode == 5 && Q.tables != nullptr) ? 5 + Q.n + (Q.n + 1) / 2 + 5 * cap
+                                                                         : 0;
       if (need == 0 || need > Q.stream_bytes) {
         if (lane == 0) raise_error(nullptr);
         mode = 0;
+      }
+      // top16: the stream's escape entries (sorted by position) and one
+      // cursor per plane, at the first entry of the item's first block
+      const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
+      uint32_t esc_total = 0, cursor[2] = {0, 0};
+      uint32_t books = 0;  // lane l: book byte l & 15 of plane l >> 4
+      if (kTop16 && mode == 5) {
+        esc_total = static_cast<uint32_t>(min(static_cast<uint64_t>(load_u32le(Q.stream + 1)), cap));
+        cursor[0] = entries_lower_bound(entries, esc_total, static_cast<uint64_t>(I.block0) * kAttnBlockWords);
+        cursor[1] = entries_lower_bound(entries, esc_total,
+                                        Q.n / 2 + static_cast<uint64_t>(I.block0) * kAttnBlockWords);
+        books = __ldg(Q.tables + 512 + lane);
       }
       const uint32_t pal = mode == 3 ? (static_cast<uint32_t>(__ldg(Q.stream + 1 + 2 * lane)) |
                                         (static_cast<uint32_t>(__ldg(Q.stream + 2 + 2 * lane)) << 8))
@@ -357,6 +467,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
           off = 1 + 2 * wt;
           len = 2 * kAttnRowWords * kRows;
           dst = stage + t * kAttnRawPitch;
+        } else if (kTop16 && mode == 5 && copies) {  // body rows, nibble rows
+          off = lane < 16 ? 5 + wt : 5 + Q.n + wt / 2;
+          len = (lane < 16 ? kAttnRowWords : kAttnRowWords / 2) * kRows;
+          dst = lane < 16 ? stage + t * kAttnLowPitch : stage + kAttnCodesOffset + t * kAttnNibblePitch;
         }
         const RowCopy c = plan_row_copy(Q.stream, Q.stream_bytes, off, len);
         const uint32_t total = warp_sum(c.bulk);
@@ -365,18 +479,70 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
         issue_row_copy(c, dst, &R.full[p.s]);
         const uint32_t pad = c.pad;
         const uint32_t pad_y = __shfl_sync(kFull, pad, 16);
+        if (kTop16 && mode == 5) {
+          // the block plane's escapes: entries [first, first + count) from
+          // the plane's cursor, then the stage's bitmap, prefix and exponents
+          const uint64_t w_start = plane * (Q.n / 2) + static_cast<uint64_t>(blk) * kAttnBlockWords;
+          const uint64_t w_end = w_start + kAttnBlockWords;
+          const uint32_t first = cursor[plane];
+          uint32_t count = 0;
+          for (;;) {
+            const uint32_t i = first + count + lane;
+            const uint32_t in = __ballot_sync(kFull, i < esc_total && entry_pos(entries, i) < w_end);
+            if ((in & (in + 1)) != 0 && lane == 0) raise_error(nullptr);  // entries out of order
+            count += __popc(in);
+            if (in != kFull) break;
+          }
+          cursor[plane] = first + count;
+          uint4* zero = reinterpret_cast<uint4*>(stage + kAttnEscBitmap);
+#pragma unroll
+          for (int k = 0; k < static_cast<int>(kAttnBlockWords / 8 / 16 / 32); ++k) zero[lane + 32 * k] = make_uint4(0, 0, 0, 0);
+          __syncwarp();
+          uint32_t* bm = reinterpret_cast<uint32_t*>(stage + kAttnEscBitmap);
+          for (uint32_t j = lane; j < count; j += 32) {
+            const uint64_t at = entry_pos(entries, first + j) - w_start;
+            if (at < kAttnBlockWords) atomicOr(&bm[at >> 5], 1u << (at & 31));
+            if (j < kAttnEscExpCap) stage[kAttnEscExps + j] = __ldg(entries + 5ull * (first + j) + 4);
+          }
+          __syncwarp();
+          uint32_t cnt[16], sum = 0;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            cnt[k] = __popc(bm[16 * lane + k]);
+            sum += cnt[k];
+          }
+          uint32_t incl = sum;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(kFull, incl, o);
+            if (lane >= static_cast<uint32_t>(o)) incl += v;
+          }
+          uint16_t* pf = reinterpret_cast<uint16_t*>(stage + kAttnEscPrefix);
+          uint32_t run = incl - sum;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            pf[16 * lane + k] = static_cast<uint16_t>(run);
+            run += cnt[k];
+          }
+          if (lane == 0) {
+            d.esc_first = first;
+            d.esc_count = count;
+          }
+          const uint32_t book = __shfl_sync(kFull, books, 16 * plane + (lane & 15));
+          if (lane < 16) d.pal[lane] = static_cast<uint8_t>(book);
+        }
         if (lane == 0) {
           d.item = item;
           d.block = blk;
           d.plane = plane;
           d.mode = mode;
           d.pad_x = pad;
-          d.pad_y = mode == 3 ? pad_y : 0u;
+          d.pad_y = (mode == 3 || mode == 5) ? pad_y : 0u;
           const uint32_t first = blk * kAttnBlockTokens;
           d.valid = Q.ctx > first ? min(Q.ctx - first, static_cast<uint32_t>(kAttnBlockTokens)) : 0u;
         }
-        reinterpret_cast<uint16_t*>(d.pal)[lane] = static_cast<uint16_t>(pal);
-        __syncwarp();  // the lanes' palette and edge-byte stores precede lane 0's release
+        if (mode != 5) reinterpret_cast<uint16_t*>(d.pal)[lane] = static_cast<uint16_t>(pal);
+        __syncwarp();  // the lanes' palette, escape and edge-byte stores precede lane 0's release
         if (lane == 0) mbar_arrive(&R.full[p.s]);
         p.next();
       }
@@ -442,6 +608,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
             mma_bf16((kk & 1) ? sd : sc, raw_word_pair(d, stage, gid, dim, 2 * kk),
                      raw_word_pair(d, stage, gid + 8, dim, 2 * kk), raw_word_pair(d, stage, gid, dim, 2 * kk + 1),
                      raw_word_pair(d, stage, gid + 8, dim, 2 * kk + 1), qb[2 * kk], qb[2 * kk + 1]);
+        } else if (kTop16 && d.mode == 5) {
+          const uint4 bv = *reinterpret_cast<const uint4*>(d.pal);
+          const uint32_t bk[4] = {bv.x, bv.y, bv.z, bv.w};
+          uint32_t B0[8], N0[4], B1[8], N1[4];
+          top16_load<16>(d, stage, gid, dim, B0, N0);
+          top16_load<16>(d, stage, gid + 8, dim, B1, N1);
+          // escape bits of the lane's 32 dims of each token, and the escapes before them
+          const uint32_t w0 = (gid * kAttnRowWords + dim) >> 5, w1 = w0 + 8 * kAttnRowWords / 32;
+          const uint32_t* bm = reinterpret_cast<const uint32_t*>(stage + kAttnEscBitmap);
+          const uint16_t* pf = reinterpret_cast<const uint16_t*>(stage + kAttnEscPrefix);
+          const uint32_t r0 = bm[w0], r1 = bm[w1];
+          const uint32_t p0 = r0 ? pf[w0] : 0u, p1 = r1 ? pf[w1] : 0u;
+          const AttnReq& Q = b.req[I.req];
+          const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t e0 = book_exps4(bk, (N0[kk >> 1] >> (16 * (kk & 1))) & 0xFFFFu);
+            const uint32_t e1 = book_exps4(bk, (N1[kk >> 1] >> (16 * (kk & 1))) & 0xFFFFu);
+            uint32_t a0 = top16_pair(B0[kk], e0, false), a2 = top16_pair(B0[kk], e0, true);
+            uint32_t a1 = top16_pair(B1[kk], e1, false), a3 = top16_pair(B1[kk], e1, true);
+            if (((r0 | r1) >> (4 * kk)) & 0xFu) {
+              const uint32_t below = (1u << (4 * kk)) - 1u;
+              a0 = top16_patch(a0, (r0 >> (4 * kk)) & 3u, p0 + __popc(r0 & below), stage, entries, d.esc_first);
+              a2 = top16_patch(a2, (r0 >> (4 * kk + 2)) & 3u, p0 + __popc(r0 & (below | (3u << (4 * kk)))), stage,
+                               entries, d.esc_first);
+              a1 = top16_patch(a1, (r1 >> (4 * kk)) & 3u, p1 + __popc(r1 & below), stage, entries, d.esc_first);
+              a3 = top16_patch(a3, (r1 >> (4 * kk + 2)) & 3u, p1 + __popc(r1 & (below | (3u << (4 * kk)))), stage,
+                               entries, d.esc_first);
+            }
+            mma_bf16((kk & 1) ? sd : sc, a0, a1, a2, a3, qb[2 * kk], qb[2 * kk + 1]);
+          }
         }  // else: a stream this kernel does not read (the producer raised an error): S^T = 0
         const uint32_t valid = d.valid;
         consumer_release(R, p);
@@ -562,6 +759,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
           for (int m = 0; m < 8; ++m)
             mma_step(m, raw_word_pair(d, stage, t0, dim, m), raw_word_pair(d, stage, t0 + 1, dim, m),
                      raw_word_pair(d, stage, t2, dim, m), raw_word_pair(d, stage, t2 + 1, dim, m));
+        } else if (kTop16 && d.mode == 5) {
+          const uint4 bv = *reinterpret_cast<const uint4*>(d.pal);
+          const uint32_t bk[4] = {bv.x, bv.y, bv.z, bv.w};
+          const uint32_t tok[4] = {t0, t0 + 1, t2, t2 + 1};
+          uint32_t B[4][4], N[4][2], r[4], pre[4];
+          const uint32_t* bm = reinterpret_cast<const uint32_t*>(stage + kAttnEscBitmap);
+          const uint16_t* pf = reinterpret_cast<const uint16_t*>(stage + kAttnEscPrefix);
+          const uint32_t half = 16 * (gid & 1);  // the lane's 16 dims are this half of a bitmap word
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            top16_load<8>(d, stage, tok[j], dim, B[j], N[j]);
+            const uint32_t wi = (tok[j] * kAttnRowWords + dim) >> 5;
+            const uint32_t word = bm[wi];
+            r[j] = (word >> half) & 0xFFFFu;
+            pre[j] = r[j] ? pf[wi] + (half ? __popc(word & 0xFFFFu) : 0u) : 0u;
+          }
+          const AttnReq& Q = b.req[I.req];
+          const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            uint32_t v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t e = book_exps4(bk, (N[j][m >> 2] >> (16 * ((m >> 1) & 1))) & 0xFFFFu);
+              v[j] = top16_pair(B[j][m >> 1], e, (m & 1) != 0);
+              const uint32_t bits2 = (r[j] >> (2 * m)) & 3u;
+              if (bits2) v[j] = top16_patch(v[j], bits2, pre[j] + __popc(r[j] & ((1u << (2 * m)) - 1u)), stage,
+                                           entries, d.esc_first);
+            }
+            mma_step(m, v[0], v[1], v[2], v[3]);
+          }
         }
       }
       consumer_release(R, p);

@@ -107,7 +107,7 @@ class KvqAttnRequest(ctypes.Structure):
 
     _fields_ = [
         (name, ctypes.c_ulonglong)
-        for name in ("stream_ptr", "stream_bytes", "blocks", "ctx_tokens", "q_ptr", "out_ptr")
+        for name in ("stream_ptr", "stream_bytes", "blocks", "ctx_tokens", "q_ptr", "out_ptr", "tables_ptr")
     ]
 
 
@@ -569,7 +569,7 @@ def attention_stream_buffer(nbytes: int, device):
     return raw[start : start + nbytes]
 
 
-def attention_requests(q, streams, ctx_tokens, out):
+def attention_requests(q, streams, ctx_tokens, out, tables=None):
     """The ``kvq_splitzip_attn_request`` array of a batch (see attention_decode)."""
     reqs = (KvqAttnRequest * len(streams))()
     for i, (stream, ctx) in enumerate(zip(streams, ctx_tokens)):
@@ -580,10 +580,12 @@ def attention_requests(q, streams, ctx_tokens, out):
         r.blocks = (int(ctx) + ATTN_BLOCK_TOKENS - 1) // ATTN_BLOCK_TOKENS
         r.q_ptr = q[i].data_ptr()
         r.out_ptr = out[i].data_ptr()
+        table = tables[i] if tables is not None else None
+        r.tables_ptr = table.data_ptr() if table is not None else 0
     return reqs
 
 
-def attention_decode(q, streams, ctx_tokens, out, workspace=None, stream=None) -> int | None:
+def attention_decode(q, streams, ctx_tokens, out, workspace=None, stream=None, tables=None) -> int | None:
     """Decode attention straight over splitzip streams (extension: the
     reference decodes each stream into its paged cache and attends over the
     bf16 copy, scripts/bench_codec_attention.py:155-157).
@@ -591,7 +593,11 @@ def attention_decode(q, streams, ctx_tokens, out, workspace=None, stream=None) -
     ``q`` and ``out``: bf16 CUDA tensors [requests, 8 * group, 128] (q head
     ``kv_head * group + i`` uses kv head ``kv_head``).  ``streams``: per
     request a uint8 CUDA tensor holding that request's layer stream (fixed6
-    mode 3 or raw mode 6) of ceil(ctx/16) paged blocks of [16, 8, 128].
+    mode 3, raw mode 6, or top16 mode 5) of ceil(ctx/16) paged blocks of
+    [16, 8, 128].  ``tables``: per request the layer's 544-byte top16 table
+    (a uint8 CUDA tensor) or None; a top16 stream needs its table, and its
+    escape entries sorted by position (as this library's encoders write
+    them).
     ``ctx_tokens``: valid tokens per request.  ``out[r, h]`` =
     softmax(q[r, h] K^T / sqrt(128)) V, fp32 accumulation.  Returns the number
     of requests, or None when the batch is declined."""
@@ -606,7 +612,9 @@ def attention_decode(q, streams, ctx_tokens, out, workspace=None, stream=None) -
     if len(streams) != q.shape[0] or len(ctx_tokens) != q.shape[0]:
         return None
     group = heads // ATTN_KV_HEADS
-    reqs = attention_requests(q, streams, ctx_tokens, out)
+    if tables is not None and len(tables) != q.shape[0]:
+        return None
+    reqs = attention_requests(q, streams, ctx_tokens, out, tables)
     need = lib.kvq_splitzip_attention_workspace_bytes(reqs, len(streams), group)
     if need <= 0:
         return None
