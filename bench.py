@@ -57,6 +57,9 @@ def parse_args():
     p.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
+    p.add_argument("--attn-streams", choices=("fixed6", "top16"), default="fixed6",
+                   help="c4: the stream form attended (top16: book-drawn exponents with 0.3%% escapes, since "
+                        "the configs[0] distribution overflows top16)")
     p.add_argument("--layers", type=int, default=None,
                    help="override the layer count (small ncu captures only; the bench line uses the config's)")
     return p.parse_args()
@@ -632,10 +635,51 @@ def b200_arm(args):
 # ------------------------------------------------------------- attention
 
 
-def attention_inputs(cfg, device, shard):
-    """per request a fixed6 stream of its one-layer K/V (device
-    draw of the configs[0] distribution, encoded by the library) placed on a
-    plane boundary, contexts and a bf16 N(0,1) query batch."""
+ATTN_TOP16_BOOKS = bytes(range(117, 133)) + bytes(range(118, 134))  # K, V exponents of the top16 streams
+
+
+def attention_top16_stream(cfg, blocks, r, shard, table, device):
+    """A top16 stream of one request's K/V: exponents drawn from the plane's
+    16-entry book, 0.3% escapes (exponents 105 and 135), random signs and
+    mantissas; encoded by the library, placed so that its planes sit on
+    16-byte boundaries."""
+    import torch
+
+    from unchainkv_b200 import splitzip_cuda as S
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7000 + r + 100000 * shard)
+    shape = (2, blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim)
+    books = torch.tensor(list(ATTN_TOP16_BOOKS), dtype=torch.int32, device=device).view(2, 1, 1, 1, 1, 16)
+    code = torch.randint(0, 16, shape + (1,), generator=gen, device=device)
+    exp = torch.gather(books.expand(shape + (16,)), -1, code).squeeze(-1)
+    esc = torch.rand(shape, generator=gen, device=device) < 0.003
+    big = torch.rand(shape, generator=gen, device=device) < 0.5
+    exp = torch.where(esc, torch.where(big, 135, 105), exp)
+    sign = torch.randint(0, 2, shape, generator=gen, device=device, dtype=torch.int32)
+    mant = torch.randint(0, 128, shape, generator=gen, device=device, dtype=torch.int32)
+    words = ((sign << 15) | (exp << 7) | mant).to(torch.int16).view(torch.bfloat16).contiguous()
+    n = words.numel()
+    buf = torch.zeros(S.top16_capacity(n) + 16, dtype=torch.uint8, device=device)
+    if not S.encode_top16_batch([S.make_job(words, None, buf, None, table, block_start=0, block_count=blocks)]):
+        raise RuntimeError("top16 encode declined: " + S._load().kvq_splitzip_last_error().decode())
+    torch.cuda.synchronize()
+    if int(buf[0].item()) != 5:
+        raise RuntimeError("the top16 attention data did not give a top16 stream")
+    size = S.stream_bytes(5, n)
+    raw = torch.empty(size + 32, dtype=torch.uint8, device=device)
+    start = (11 - raw.data_ptr()) % 16  # body and nibble planes on 16-byte boundaries
+    stream = raw[start:start + size]
+    stream.copy_(buf[:size])
+    return stream
+
+
+def attention_inputs(cfg, device, shard, codec="fixed6"):
+    """per request a stream of its one-layer K/V placed on a
+    plane boundary, contexts, a bf16 N(0,1) query batch and the per-request
+    tables (None for fixed6).  fixed6: device draw of the configs[0]
+    distribution, encoded by the library; top16: see
+    attention_top16_stream."""
     import torch
 
     from unchainkv_b200 import splitzip_cuda as S
@@ -643,6 +687,14 @@ def attention_inputs(cfg, device, shard):
 
     ctxs = W.attention_contexts(cfg)
     zero_tables = torch.zeros(544, dtype=torch.uint8, device=device)
+    if codec == "top16":
+        table = torch.frombuffer(bytearray(S.build_top16_tables(ATTN_TOP16_BOOKS)), dtype=torch.uint8).to(device)
+        streams = [attention_top16_stream(cfg, -(-ctx // cfg.block_tokens), r, shard, table, device)
+                   for r, ctx in enumerate(ctxs)]
+        gen = torch.Generator(device=device)
+        gen.manual_seed(4005 + shard)
+        q = torch.randn((cfg.requests, cfg.kv_heads * cfg.group, cfg.head_dim), generator=gen, device=device)
+        return ctxs, streams, q.to(torch.bfloat16), [table] * len(ctxs)
     streams = []
     for r, ctx in enumerate(ctxs):
         blocks = -(-ctx // cfg.block_tokens)
@@ -664,10 +716,10 @@ def attention_inputs(cfg, device, shard):
     gen = torch.Generator(device=device)
     gen.manual_seed(4005 + shard)
     q = torch.randn((cfg.requests, cfg.kv_heads * cfg.group, cfg.head_dim), generator=gen, device=device)
-    return ctxs, streams, q.to(torch.bfloat16)
+    return ctxs, streams, q.to(torch.bfloat16), None
 
 
-def attention_check(cfg, ctxs, streams, q, out, r=0):
+def attention_check(cfg, ctxs, streams, q, out, r=0, tables=None):
     """Request r against fp32 attention over its stream decoded by the codec."""
     import torch
 
@@ -676,8 +728,8 @@ def attention_check(cfg, ctxs, streams, q, out, r=0):
     blocks = -(-ctxs[r] // cfg.block_tokens)
     kv = torch.zeros((2, blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim), dtype=torch.bfloat16,
                      device=q.device)
-    job = S.make_job(kv, None, streams[r], streams[r].numel(), torch.zeros(544, dtype=torch.uint8, device=q.device),
-                     block_start=0, block_count=blocks)
+    table = tables[r] if tables is not None else torch.zeros(544, dtype=torch.uint8, device=q.device)
+    job = S.make_job(kv, None, streams[r], streams[r].numel(), table, block_start=0, block_count=blocks)
     if not S.decode_auto_batch([job]):
         raise RuntimeError("reference decode declined")
     k = kv[0].reshape(-1, cfg.kv_heads, cfg.head_dim)[: ctxs[r]].float()
@@ -751,21 +803,21 @@ def attention_arm(args):
     if not S.available():
         raise RuntimeError(f"splitzip library missing: {S.load_error()}")
     cfg = W.CONFIGS["c4"]
-    ctxs, streams, q = attention_inputs(cfg, device, rank)
+    ctxs, streams, q, tables = attention_inputs(cfg, device, rank, args.attn_streams)
     out = torch.empty_like(q)
     lib = S._load()
-    reqs = S.attention_requests(q, streams, ctxs, out)
+    reqs = S.attention_requests(q, streams, ctxs, out, tables)
     ws = torch.empty(lib.kvq_splitzip_attention_workspace_bytes(reqs, len(ctxs), cfg.group), dtype=torch.uint8,
                      device=device)
     stream = torch.cuda.current_stream(device)
 
     def step():
-        if S.attention_decode(q, streams, ctxs, out, workspace=ws) != len(ctxs):
+        if S.attention_decode(q, streams, ctxs, out, workspace=ws, tables=tables) != len(ctxs):
             raise RuntimeError("attention declined: " + lib.kvq_splitzip_last_error().decode())
 
     step()
     torch.cuda.synchronize()
-    attention_check(cfg, ctxs, streams, q, out)
+    attention_check(cfg, ctxs, streams, q, out, tables=tables)
 
     def barrier():
         if world > 1:
@@ -838,7 +890,8 @@ def attention_arm(args):
     dom = kernels["AttnKernel"]
     roofline = {"bound": "hbm", "kernel": "AttnKernel", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": round(dom["gbs"] / peak, 4), "peak_kind": peak_kind,
-                "traffic": ncu_traffic(args.workload, "AttnKernel"), "alg_bytes_per_launch": dom["alg_bytes_per_launch"]}
+                "traffic": ncu_traffic(args.workload, "AttnKernel") if args.attn_streams == "fixed6" else None,
+                "alg_bytes_per_launch": dom["alg_bytes_per_launch"]}
     cpu = None
     if not args.no_cpu_baseline:
         gbs, threads, sample = attention_cpu_gbs(cfg)
@@ -856,8 +909,12 @@ def attention_arm(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16 (fp32 accumulation)",
-        "data": "synthetic (seeded device draw of the configs[0] distribution, fixed6 streams)",
-        "config": {"workload": cfg.name, "requests": cfg.requests, "q_heads": cfg.kv_heads * cfg.group,
+        "data": ("synthetic (seeded device draw of the configs[0] distribution, fixed6 streams)"
+                 if args.attn_streams == "fixed6" else
+                 "synthetic (seeded device draw: exponents from a 16-entry book per plane, 0.3% escapes, "
+                 "top16 streams)"),
+        "config": {"workload": cfg.name, "streams": args.attn_streams, "requests": cfg.requests,
+                   "q_heads": cfg.kv_heads * cfg.group,
                    "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens,
                    "context_tokens": [cfg.min_tokens, cfg.max_tokens], "tokens_per_step": sum(ctxs),
                    "stream_bytes_per_step": stream_bytes, "raw_kv_bytes_per_step": raw,

@@ -342,9 +342,12 @@ __device__ __forceinline__ uint32_t top16_pair(uint32_t bw, uint32_t e4, bool up
 }
 
 // Exponent of the stage's escape of rank r (its place in the stage's slice
-// of the entries): from the stage, or from the stream past its capacity.
+// of `count` entries): from the stage, or from the stream past the stage's
+// room.  A rank outside the slice reads nothing: it cannot come from tables
+// built from the slice, and the stream is never read past it.
 __device__ __forceinline__ uint32_t esc_exp(const uint8_t* stage, const uint8_t* entries, uint32_t first,
-                                            uint32_t r) {
+                                            uint32_t count, uint32_t r) {
+  if (r >= count) return 0;
   return r < kAttnEscExpCap ? stage[kAttnEscExps + r] : __ldg(entries + 5ull * (first + r) + 4);
 }
 
@@ -353,9 +356,9 @@ __device__ __forceinline__ uint32_t esc_exp(const uint8_t* stage, const uint8_t*
 // high word's when only it escaped.  The exponent field (bits 7..14 of
 // each bf16 word) is replaced, as the reference's patch does.
 __device__ __forceinline__ uint32_t top16_patch(uint32_t w, uint32_t bits2, uint32_t rank0, const uint8_t* stage,
-                                                const uint8_t* entries, uint32_t first) {
-  if (bits2 & 1u) w = (w & ~0x7F80u) | (esc_exp(stage, entries, first, rank0) << 7);
-  if (bits2 & 2u) w = (w & ~0x7F800000u) | (esc_exp(stage, entries, first, rank0 + (bits2 & 1u)) << 23);
+                                                const uint8_t* entries, uint32_t first, uint32_t count) {
+  if (bits2 & 1u) w = (w & ~0x7F80u) | (esc_exp(stage, entries, first, count, rank0) << 7);
+  if (bits2 & 2u) w = (w & ~0x7F800000u) | (esc_exp(stage, entries, first, count, rank0 + (bits2 & 1u)) << 23);
   return w;
 }
 
@@ -483,27 +486,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
           // the block plane's escapes: entries [first, first + count) from
           // the plane's cursor, then the stage's bitmap, prefix and exponents
           const uint64_t w_start = plane * (Q.n / 2) + static_cast<uint64_t>(blk) * kAttnBlockWords;
-          const uint64_t w_end = w_start + kAttnBlockWords;
           const uint32_t first = cursor[plane];
-          uint32_t count = 0;
-          for (;;) {
-            const uint32_t i = first + count + lane;
-            const uint32_t in = __ballot_sync(kFull, i < esc_total && entry_pos(entries, i) < w_end);
-            if ((in & (in + 1)) != 0 && lane == 0) raise_error(nullptr);  // entries out of order
-            count += __popc(in);
-            if (in != kFull) break;
-          }
-          cursor[plane] = first + count;
           uint4* zero = reinterpret_cast<uint4*>(stage + kAttnEscBitmap);
 #pragma unroll
           for (int k = 0; k < static_cast<int>(kAttnBlockWords / 8 / 16 / 32); ++k) zero[lane + 32 * k] = make_uint4(0, 0, 0, 0);
           __syncwarp();
+          // chunks of 32 entries from the cursor, each read once (position
+          // and exponent), until the first at or past the block plane's end
           uint32_t* bm = reinterpret_cast<uint32_t*>(stage + kAttnEscBitmap);
-          for (uint32_t j = lane; j < count; j += 32) {
-            const uint64_t at = entry_pos(entries, first + j) - w_start;
-            if (at < kAttnBlockWords) atomicOr(&bm[at >> 5], 1u << (at & 31));
-            if (j < kAttnEscExpCap) stage[kAttnEscExps + j] = __ldg(entries + 5ull * (first + j) + 4);
+          uint32_t count = 0;
+          for (;;) {
+            const uint32_t i = first + count + lane;
+            uint64_t at = ~0ull;
+            uint32_t ex = 0;
+            if (i < esc_total) {
+              at = entry_pos(entries, i) - w_start;
+              ex = __ldg(entries + 5ull * i + 4);
+            }
+            const bool in = i < esc_total && at < kAttnBlockWords;
+            const uint32_t bal = __ballot_sync(kFull, in);
+            if ((bal & (bal + 1)) != 0 && lane == 0) raise_error(nullptr);  // entries out of order
+            if (in) {
+              atomicOr(&bm[at >> 5], 1u << (at & 31));
+              if (count + lane < kAttnEscExpCap) stage[kAttnEscExps + count + lane] = static_cast<uint8_t>(ex);
+            }
+            count += __popc(bal);
+            if (bal != kFull) break;
           }
+          cursor[plane] = first + count;
           __syncwarp();
           uint32_t cnt[16], sum = 0;
 #pragma unroll
@@ -630,12 +640,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
             uint32_t a1 = top16_pair(B1[kk], e1, false), a3 = top16_pair(B1[kk], e1, true);
             if (((r0 | r1) >> (4 * kk)) & 0xFu) {
               const uint32_t below = (1u << (4 * kk)) - 1u;
-              a0 = top16_patch(a0, (r0 >> (4 * kk)) & 3u, p0 + __popc(r0 & below), stage, entries, d.esc_first);
+              a0 = top16_patch(a0, (r0 >> (4 * kk)) & 3u, p0 + __popc(r0 & below), stage, entries, d.esc_first, d.esc_count);
               a2 = top16_patch(a2, (r0 >> (4 * kk + 2)) & 3u, p0 + __popc(r0 & (below | (3u << (4 * kk)))), stage,
-                               entries, d.esc_first);
-              a1 = top16_patch(a1, (r1 >> (4 * kk)) & 3u, p1 + __popc(r1 & below), stage, entries, d.esc_first);
+                               entries, d.esc_first, d.esc_count);
+              a1 = top16_patch(a1, (r1 >> (4 * kk)) & 3u, p1 + __popc(r1 & below), stage, entries, d.esc_first, d.esc_count);
               a3 = top16_patch(a3, (r1 >> (4 * kk + 2)) & 3u, p1 + __popc(r1 & (below | (3u << (4 * kk)))), stage,
-                               entries, d.esc_first);
+                               entries, d.esc_first, d.esc_count);
             }
             mma_bf16((kk & 1) ? sd : sc, a0, a1, a2, a3, qb[2 * kk], qb[2 * kk + 1]);
           }
@@ -786,7 +796,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
               v[j] = top16_pair(B[j][m >> 1], e, (m & 1) != 0);
               const uint32_t bits2 = (r[j] >> (2 * m)) & 3u;
               if (bits2) v[j] = top16_patch(v[j], bits2, pre[j] + __popc(r[j] & ((1u << (2 * m)) - 1u)), stage,
-                                           entries, d.esc_first);
+                                           entries, d.esc_first, d.esc_count);
             }
             mma_step(m, v[0], v[1], v[2], v[3]);
           }
