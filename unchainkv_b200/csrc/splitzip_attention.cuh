@@ -294,7 +294,8 @@ __device__ __forceinline__ uint32_t raw_word_pair(const AttnDesc& d, const uint8
 // rows (512 bytes a token) in place of the code rows.  Its tail holds the
 // stage's escapes, written by the producer from the stream's sorted entries:
 // a bitmap of the block plane's 16384 words, the escapes before each bitmap
-// word (u16), and the escaped exponents in position order.
+// word that holds one (u16; the other words' slots are never read), and the
+// escaped exponents in position order.
 constexpr uint32_t kAttnNibblePitch = kAttnRowWords / 2;
 constexpr uint32_t kAttnEscBitmap = 24640;
 constexpr uint32_t kAttnEscPrefix = kAttnEscBitmap + kAttnBlockWords / 8;
@@ -494,7 +495,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
           // chunks of 32 entries from the cursor, each read once (position
           // and exponent), until the first at or past the block plane's end
           uint32_t* bm = reinterpret_cast<uint32_t*>(stage + kAttnEscBitmap);
-          uint32_t count = 0;
+          uint16_t* pf = reinterpret_cast<uint16_t*>(stage + kAttnEscPrefix);
+          uint32_t count = 0, last_word = 0xFFFFFFFFu;
           for (;;) {
             const uint32_t i = first + count + lane;
             uint64_t at = ~0ull;
@@ -506,34 +508,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
             const bool in = i < esc_total && at < kAttnBlockWords;
             const uint32_t bal = __ballot_sync(kFull, in);
             if ((bal & (bal + 1)) != 0 && lane == 0) raise_error(nullptr);  // entries out of order
+            // the escapes before a bitmap word are the rank of its first
+            // entry; only words that hold escapes are ever read
+            const uint32_t word = in ? static_cast<uint32_t>(at >> 5) : 0xFFFFFFFFu;
+            const uint32_t up = __shfl_up_sync(kFull, word, 1);
+            const uint32_t before = lane == 0 ? last_word : up;
             if (in) {
-              atomicOr(&bm[at >> 5], 1u << (at & 31));
+              atomicOr(&bm[word], 1u << (at & 31));
+              if (word != before) pf[word] = static_cast<uint16_t>(count + lane);
               if (count + lane < kAttnEscExpCap) stage[kAttnEscExps + count + lane] = static_cast<uint8_t>(ex);
             }
+            last_word = __shfl_sync(kFull, word, 31);
             count += __popc(bal);
             if (bal != kFull) break;
           }
           cursor[plane] = first + count;
-          __syncwarp();
-          uint32_t cnt[16], sum = 0;
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            cnt[k] = __popc(bm[16 * lane + k]);
-            sum += cnt[k];
-          }
-          uint32_t incl = sum;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t v = __shfl_up_sync(kFull, incl, o);
-            if (lane >= static_cast<uint32_t>(o)) incl += v;
-          }
-          uint16_t* pf = reinterpret_cast<uint16_t*>(stage + kAttnEscPrefix);
-          uint32_t run = incl - sum;
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            pf[16 * lane + k] = static_cast<uint16_t>(run);
-            run += cnt[k];
-          }
           if (lane == 0) {
             d.esc_first = first;
             d.esc_count = count;
