@@ -2,11 +2,12 @@
 
 kvq_splitzip_bf16_encode_top16_noalloc serves callers that cannot allocate
 device memory or cannot leave spare bytes past the stream in their buffer:
-code under CUDA graph capture, serving engines that give nearly all of HBM to
-their KV pool, and runtimes that size stream buffers exactly.  Its scratch is
-a static device array shared by all calls, so the test makes two calls in a
-row (the second finds the first call's leftovers in the array) and compares
-both, byte for byte, with kvq_splitzip_bf16_encode_top16 through the C ABI.
+serving engines that give nearly all of HBM to their KV pool, paths that must
+not call cudaMalloc / cudaFree (they can synchronise the device), and runtimes
+that size stream buffers exactly.  Its scratch is a static device array shared
+by all calls, so the test makes two calls in a row (the second finds the first
+call's leftovers in the array) and compares both, byte for byte, with
+kvq_splitzip_bf16_encode_top16 through the C ABI.
 This file is collected last on purpose and needs nothing from other tests.
 """
 

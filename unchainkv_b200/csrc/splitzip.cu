@@ -1200,26 +1200,28 @@ extern "C" KVQ_API long long kvq_splitzip_profile_launches(int i) {
 // buffer.
 //
 // Some callers cannot allocate device memory on the encode path:
-// - code being captured into a CUDA graph, where allocation is not allowed
-//   and every address must stay fixed across replays;
 // - serving engines that hand nearly all of HBM to their own paged KV pool
 //   (vLLM's gpu_memory_utilization), where a transient allocation can fail;
+// - latency-critical paths that must not call cudaMalloc / cudaFree, which
+//   can synchronise the device;
 // - plugins whose host runtime owns device memory and sizes each stream
 //   buffer exactly to the stream, leaving no spare bytes past it for the
 //   scratch kvq_splitzip_bf16_encode_top16 keeps there.
-// This variant keeps its tile-scan scratch in a fixed device array of this
-// library instead.  The array is part of the module image: every GPU that
-// loads the library holds it until process exit, and no call here (or in the
-// kernel) allocates or frees memory.
+// This variant keeps the escape counts of its statistics pass in a fixed
+// device array of this library instead.  The array is part of the module
+// image: every GPU that loads the library holds it until process exit, and
+// no call here (or in the kernels) allocates or frees memory.
 // ---------------------------------------------------------------------
 
 namespace {
 
 // Largest `count` the static scratch covers: 2^27 words (256 MiB of raw bf16,
-// 16384 tiles); the array is 16 + 8*512 + 8*16384 = 135184 bytes.
+// 16384 tiles); the array holds the escape total and error flag, 512 group
+// sums and a u16 count per (tile, warp): 64 + 8*512 + 16*16384 = 266304 bytes.
 constexpr uint64_t kNoAllocMaxWords = 1ull << 27;
 constexpr uint64_t kNoAllocTiles = (kNoAllocMaxWords + kTileWords - 1) / kTileWords;
 constexpr uint64_t kNoAllocScratchBytes = auto_scratch_bytes(kNoAllocTiles);
+static_assert(kNoAllocScratchBytes == 266304, "the documented size of the no-alloc scratch");
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
