@@ -64,3 +64,15 @@ def test_declines_without_touching_the_device():
     assert lib.kvq_splitzip_bf16_encode_top16(16, 16, 4096, 100, 16, 0) == 0
     # count beyond the 32-bit position field
     assert lib.kvq_splitzip_bf16_encode_top16(16, 16, 1 << 32, 1 << 40, 16, 0) == 0
+
+
+def test_attention_request_layout_matches_the_header():
+    """ABI revision 3: kvq_splitzip_attn_request gained tables_ptr; the
+    Python mirror's struct must have the header's fields in its order."""
+    lib = splitzip_cuda._load()
+    assert lib.kvq_splitzip_abi_version() == 3
+    text = (ROOT / "include" / "unchain_kv_splitzip.h").read_text()
+    body = re.search(r"typedef struct kvq_splitzip_attn_request \{(.*?)\}", text, re.S).group(1)
+    fields = re.findall(r"unsigned long long (\w+);", body)
+    assert [name for name, _ in splitzip_cuda.KvqAttnRequest._fields_] == fields
+    assert ctypes.sizeof(splitzip_cuda.KvqAttnRequest) == 8 * len(fields) == 56
