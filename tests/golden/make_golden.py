@@ -2,8 +2,8 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
 Run from the repository root, in a checkout where the reference tree is
-available (default ``/root/reference``, override with
-``UNCHAIN_KV_REFERENCE_ROOT``)::
+available (its location is ``UNCHAIN_KV_REFERENCE_ROOT``, or the default
+``REFERENCE`` below)::
 
     python tests/golden/make_golden.py
 
