@@ -139,6 +139,8 @@ def test_streams_placed_on_plane_boundaries(modes):
 def test_group_sizes():
     run([300, 40], [3, 3], group=1, seed=2)
     run([300, 40], [3, 3], group=8, seed=3)
+    run([300, 40], [5, 5], group=1, seed=10)
+    run([300, 40], [5, 5], group=8, seed=11, aligned=11)
 
 
 def test_batch_like_config4():
