@@ -1043,7 +1043,7 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
   bool top16 = false;
   for (uint64_t r = 0; r < count; ++r) top16 = top16 || reqs[r].tables_ptr != 0;
   const long long geometry =
-      top16 ? grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems, true>, kAttnSmemBytes, kAttnMaxCtas, &grid, kAttnThreads)
+      top16 ? grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems, true>, kAttnSmemBytes, kAttnMaxCtas, &grid, kAttnThreads + 32)
             : grid_for(AttnKernel<kAttnMaxReqs, kAttnMaxItems, false>, kAttnSmemBytes, kAttnMaxCtas, &grid, kAttnThreads);
   if (geometry < 0) return false;
   const uint64_t ctas = std::min<uint64_t>(std::min<uint64_t>(grid, total), kAttnMaxCtas);
@@ -1114,7 +1114,8 @@ extern "C" KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_at
   for (uint32_t r = 0; r < b.reqs; ++r) top16 = top16 || b.req[r].tables != nullptr;
   long long prof = prof_begin(stream);
   if (top16) {
-    AttnKernel<kAttnMaxReqs, kAttnMaxItems, true><<<b.ctas, kAttnThreads, kAttnSmemBytes, stream>>>(b);
+    // + the escape warp
+    AttnKernel<kAttnMaxReqs, kAttnMaxItems, true><<<b.ctas, kAttnThreads + 32, kAttnSmemBytes, stream>>>(b);
   } else {
     AttnKernel<kAttnMaxReqs, kAttnMaxItems, false><<<b.ctas, kAttnThreads, kAttnSmemBytes, stream>>>(b);
   }

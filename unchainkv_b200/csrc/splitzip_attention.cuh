@@ -387,7 +387,8 @@ __device__ __forceinline__ uint32_t entries_lower_bound(const uint8_t* entries, 
 // registers per thread.
 // kTop16: also reads top16 streams (mode 5), with the requests' tables.
 template <int kMaxR, int kMaxI, bool kTop16>
-__global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
+__global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
+    AttnKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ __align__(16) uint32_t pair[4096];
   __shared__ __align__(16) float4 scores[kAttnKvHeads][2][32];  // S^T fragments, two slots per head
@@ -399,7 +400,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
   const int warp = tid >> 5;
   if (tid == 0) {
     for (int i = 0; i < kAttnStages; ++i) {
-      mbar_init(&R.full[i], 1);  // lane 0 of the producer, after the warp's copies are issued
+      // lane 0 of the producer, after the warp's copies are issued (and of
+      // the escape warp, after the stage's escape tables)
+      mbar_init(&R.full[i], kTop16 ? 2 : 1);
       mbar_init(&R.empty[i], kAttnKvHeads);
     }
   }
@@ -432,18 +435,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
       if (need == 0 || need > Q.stream_bytes) {
         if (lane == 0) raise_error(nullptr);
         mode = 0;
-      }
-      // top16: the stream's escape entries (sorted by position) and one
-      // cursor per plane, at the first entry of the item's first block
-      const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
-      uint32_t esc_total = 0, cursor[2] = {0, 0};
-      uint32_t books = 0;  // lane l: book byte l & 15 of plane l >> 4
-      if (kTop16 && mode == 5) {
-        esc_total = static_cast<uint32_t>(min(static_cast<uint64_t>(load_u32le(Q.stream + 1)), cap));
-        cursor[0] = entries_lower_bound(entries, esc_total, static_cast<uint64_t>(I.block0) * kAttnBlockWords);
-        cursor[1] = entries_lower_bound(entries, esc_total,
-                                        Q.n / 2 + static_cast<uint64_t>(I.block0) * kAttnBlockWords);
-        books = __ldg(Q.tables + 512 + lane);
       }
       const uint32_t pal = mode == 3 ? (static_cast<uint32_t>(__ldg(Q.stream + 1 + 2 * lane)) |
                                         (static_cast<uint32_t>(__ldg(Q.stream + 2 + 2 * lane)) << 8))
@@ -484,14 +475,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
         issue_row_copy(c, dst, &R.full[p.s]);
         const uint32_t pad = c.pad;
         const uint32_t pad_y = __shfl_sync(kFull, pad, 16);
-        if (kTop16 && mode == 5) {
+        if (lane == 0) {
+          d.item = item;
+          d.block = blk;
+          d.plane = plane;
+          d.mode = mode;
+          d.pad_x = pad;
+          d.pad_y = (mode == 3 || mode == 5) ? pad_y : 0u;
+          const uint32_t first = blk * kAttnBlockTokens;
+          d.valid = Q.ctx > first ? min(Q.ctx - first, static_cast<uint32_t>(kAttnBlockTokens)) : 0u;
+        }
+        if (mode != 5) reinterpret_cast<uint16_t*>(d.pal)[lane] = static_cast<uint16_t>(pal);
+        __syncwarp();  // the lanes' palette, escape and edge-byte stores precede lane 0's release
+        if (lane == 0) mbar_arrive(&R.full[p.s]);
+        p.next();
+      }
+    }
+    return;
+  }
+
+  if (kTop16 && warp == kAttnConsumerWarps + 1) {
+    // ------------------------------------------------------- escape warp
+    // For each stage of a top16 item: the block plane's escapes from the
+    // stream's sorted entries, written into the stage's tail while the
+    // producer stages the next copies.  It takes the stages in the
+    // producer's order, waits for their release like the producer, and is
+    // the second arrival on every stage's full barrier.
+    AttnPos p;
+    for (uint32_t item = i_begin; item < i_end; ++item) {
+      const AttnItem& I = b.item[item];
+      const AttnReq& Q = b.req[I.req];
+      uint32_t mode = __ldg(Q.stream);
+      const uint64_t cap = (Q.n + 199) / 200;
+      if (mode != 5 || Q.tables == nullptr || 5 + Q.n + (Q.n + 1) / 2 + 5 * cap > Q.stream_bytes) mode = 0;
+      // the entries (sorted by position) and one cursor per plane, at the
+      // first entry of the item's first block
+      const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
+      uint32_t esc_total = 0, cursor[2] = {0, 0};
+      uint32_t books = 0;  // lane l: book byte l & 15 of plane l >> 4
+      if (mode == 5) {
+        esc_total = static_cast<uint32_t>(min(static_cast<uint64_t>(load_u32le(Q.stream + 1)), cap));
+        cursor[0] = entries_lower_bound(entries, esc_total, static_cast<uint64_t>(I.block0) * kAttnBlockWords);
+        cursor[1] = entries_lower_bound(entries, esc_total,
+                                        Q.n / 2 + static_cast<uint64_t>(I.block0) * kAttnBlockWords);
+        books = __ldg(Q.tables + 512 + lane);
+      }
+      for (uint32_t k = 0; k < 2 * I.blocks; ++k) {
+        const uint32_t blk = I.block0 + (k >> 1), plane = k & 1;
+        producer_acquire(R, p, nullptr);
+        AttnDesc& d = D[p.s];
+        uint8_t* stage = ring + p.s * kAttnStageBytes;
+        if (mode == 5) {
           // the block plane's escapes: entries [first, first + count) from
           // the plane's cursor, then the stage's bitmap, prefix and exponents
           const uint64_t w_start = plane * (Q.n / 2) + static_cast<uint64_t>(blk) * kAttnBlockWords;
           const uint32_t first = cursor[plane];
           uint4* zero = reinterpret_cast<uint4*>(stage + kAttnEscBitmap);
 #pragma unroll
-          for (int k = 0; k < static_cast<int>(kAttnBlockWords / 8 / 16 / 32); ++k) zero[lane + 32 * k] = make_uint4(0, 0, 0, 0);
+          for (int z = 0; z < static_cast<int>(kAttnBlockWords / 8 / 16 / 32); ++z) zero[lane + 32 * z] = make_uint4(0, 0, 0, 0);
           __syncwarp();
           // chunks of 32 entries from the cursor, each read once (position
           // and exponent), until the first at or past the block plane's end
@@ -531,18 +572,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) AttnKernel(const __grid_const
           const uint32_t book = __shfl_sync(kFull, books, 16 * plane + (lane & 15));
           if (lane < 16) d.pal[lane] = static_cast<uint8_t>(book);
         }
-        if (lane == 0) {
-          d.item = item;
-          d.block = blk;
-          d.plane = plane;
-          d.mode = mode;
-          d.pad_x = pad;
-          d.pad_y = (mode == 3 || mode == 5) ? pad_y : 0u;
-          const uint32_t first = blk * kAttnBlockTokens;
-          d.valid = Q.ctx > first ? min(Q.ctx - first, static_cast<uint32_t>(kAttnBlockTokens)) : 0u;
-        }
-        if (mode != 5) reinterpret_cast<uint16_t*>(d.pal)[lane] = static_cast<uint16_t>(pal);
-        __syncwarp();  // the lanes' palette, escape and edge-byte stores precede lane 0's release
+        __syncwarp();  // the lanes' table stores precede lane 0's arrival
         if (lane == 0) mbar_arrive(&R.full[p.s]);
         p.next();
       }
