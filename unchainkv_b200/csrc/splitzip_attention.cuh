@@ -15,8 +15,9 @@
 //   - producer warp: for each block, stages the K plane block (16 tokens x
 //     8 heads x 128 dims), then the V plane block, into a ring of shared
 //     memory stages by TMA (the rows' low bytes and 6-bit codes for fixed6,
-//     their words for raw, their body bytes and 4-bit codes for top16, plus,
-//     for top16, the block plane's escapes from the stream's sorted entries);
+//     their words for raw, their body bytes and 4-bit codes for top16);
+//   - escape warp (top16 kernels only): writes each top16 stage's escape
+//     tables (from the stream's sorted entries) into the stage's tail;
 //   - K warp h (kv head h): decodes its head's slice of each K block
 //     straight into the A fragments of S^T = K Q^T (16 tokens x g q heads,
 //     one m16n8k16 bf16 MMA per 16 dims) and hands the S^T fragments to the
