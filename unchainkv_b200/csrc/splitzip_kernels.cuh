@@ -547,6 +547,11 @@ __device__ __forceinline__ void write_top16_header(uint8_t* dst, uint64_t total,
 // explicit top16 encode counts every tile: an overflowing stream still holds
 // the first `cap` escapes, so every tile's offset must be exact.
 __device__ __forceinline__ uint32_t presence_index(uint32_t h) { return h ^ ((h >> 5) & 4u); }
+template <uint32_t kOff> struct StatsPlane { static constexpr uint32_t kOffset = kOff; };
+
+// Sign-and-exponent index (the word's bits 7..15) with the sign copied into
+// bank bit 4 (byte bit 6), for the 512-entry stats tables.
+__device__ __forceinline__ uint32_t stats_index(uint32_t i9) { return i9 ^ ((i9 >> 2) & 0x40u); }
 
 enum StatsKind { kStatsPresence = 0, kStatsAuto = 1, kStatsTop16 = 2 };
 
@@ -555,14 +560,19 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
   constexpr bool kStats = kKind != kStatsPresence;
   constexpr bool kPresence = kKind != kStatsTop16;
   extern __shared__ __align__(128) uint8_t ring[];
-  __shared__ __align__(16) uint8_t spres[256];
-  __shared__ uint8_t sesc[512];  // 1 where the exponent has no top16 code
+  // Presence is kept per high byte (256 entries) when only presence is wanted,
+  // and per sign-and-exponent (512 entries) when escapes are counted too: one
+  // 9-bit index then serves both tables.  Both layouts put the sign into a
+  // bank bit (stats_index, presence_index), so +e and -e land in other banks.
+  __shared__ __align__(16) uint8_t spres[kStats ? 512 : 256];
+  __shared__ __align__(16) uint8_t sesc[1024];  // [plane][stats_index]: 1 where the exponent has no top16 code
   __shared__ EncRing R;
   __shared__ EncDesc D[kEncStages];
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  if (tid < 64) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
+  constexpr int kPresWords = sizeof(spres) / 4;
+  if (tid < kPresWords) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
   ring_init(R);
   __syncthreads();
   int pres_job = -1, table_job = -1;
@@ -570,10 +580,13 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
   // (consumers only; every warp is past its last presence store)
   auto flush = [&](const EncJob& P) {
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(P.scratch + (kStats ? 16 : 0));
-    const uint32_t bits = __ballot_sync(kFull, spres[presence_index(tid)] != 0);
+    // high byte h covers the sign-and-exponent pair 2h, 2h + 1 (one u16)
+    const bool seen = kStats ? *reinterpret_cast<const uint16_t*>(spres + stats_index(2u * tid)) != 0
+                             : spres[presence_index(tid)] != 0;
+    const uint32_t bits = __ballot_sync(kFull, seen);
     if (lane == 0 && bits) atomicOr(&bitmap[warp], bits);
     consumer_sync();
-    if (tid < 64) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
+    if (tid < kPresWords) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
   };
   // aux = 1 when the job's escapes already exceed its top16 capacity
   auto over_cap = [](const EncJob& J, uint32_t, EncDesc& d) {
@@ -590,7 +603,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
         pres_job = j;
       }
       if (kStats && j != table_job) {
-        for (int i = tid; i < 512; i += kThreads) sesc[i] = __ldg(J.tables + i) == 255u;
+        for (int i = tid; i < 1024; i += kThreads)
+          sesc[(i & 512) | stats_index(i & 511)] = __ldg(J.tables + ((i >> 1) & 256) + (i & 255)) == 255u;
         table_job = j;
       }
       consumer_sync();
@@ -600,30 +614,42 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     const bool count = kStats && !skip_escapes;
     uint32_t escapes = 0;
     if (len == kTileWords && (t0 >= J.half || t0 + kTileWords <= J.half)) {
-      // whole tile in one plane: table offset fixed, no bounds
-      const uint32_t poff = t0 >= J.half ? 256u : 0u;
+      // whole tile in one plane: no bounds, and the plane's escape table is a
+      // constant offset (one copy of the loop per plane)
+      auto scan = [&](auto plane) {
+        constexpr uint32_t kOff = decltype(plane)::kOffset;
 #pragma unroll
-      for (int s = 0; s < kStepsPerWarp; ++s) {
-        const uint16_t* w = sin + (warp * kStepsPerWarp + s) * kStepWords + 8 * lane;
-        const uint4 v0 = *reinterpret_cast<const uint4*>(w);
-        const uint4 v1 = *reinterpret_cast<const uint4*>(w + 256);
-        const uint32_t x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        if (kPresence) {
+        for (int s = 0; s < kStepsPerWarp; ++s) {
+          const uint16_t* w = sin + (warp * kStepsPerWarp + s) * kStepWords + 8 * lane;
+          const uint4 v0 = *reinterpret_cast<const uint4*>(w);
+          const uint4 v1 = *reinterpret_cast<const uint4*>(w + 256);
+          const uint32_t x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+          if (!kStats) {
 #pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            const uint32_t y = x[p] ^ ((x[p] >> 5) & 0x04000400u);
-            spres[__byte_perm(y, 0, 0x4441)] = 1;
-            spres[y >> 24] = 1;
+            for (int p = 0; p < 8; ++p) {
+              const uint32_t y = x[p] ^ ((x[p] >> 5) & 0x04000400u);
+              spres[__byte_perm(y, 0, 0x4441)] = 1;
+              spres[y >> 24] = 1;
+            }
+          } else {
+#pragma unroll
+            for (int p = 0; p < 8; ++p) {
+              // stats_index of both words at once: bits 7..15 (even word), 23..31 (odd)
+              const uint32_t y = x[p] ^ ((x[p] >> 2) & 0x20002000u);
+              const uint32_t e = (y >> 7) & 0x1FFu, o = y >> 23;
+              if (kPresence) {
+                spres[e] = 1;
+                spres[o] = 1;
+              }
+              if (count) escapes += sesc[kOff + e] + sesc[kOff + o];
+            }
           }
         }
-        if (count) {
-          // exponent bytes: byte 1 of x << 1 (even word), x >> 23 (odd word)
-          const uint8_t* tb = poff ? sesc + 256 : sesc;
-#pragma unroll
-          for (int p = 0; p < 8; ++p)
-            escapes += tb[__byte_perm(x[p] << 1, 0, 0x4441)] + tb[(x[p] >> 23) & 0xFFu];
-        }
-      }
+      };
+      if (!kStats || t0 < J.half)
+        scan(StatsPlane<0>{});
+      else
+        scan(StatsPlane<512>{});
     } else {
 #pragma unroll
       for (int s = 0; s < kStepsPerWarp; ++s) {
@@ -633,8 +659,13 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
         const uint64_t g = t0 + w0;
         for (uint32_t i = 0; i < valid; ++i) {
           const uint32_t w = sin[w0 + i];
-          if (kPresence) spres[presence_index(w >> 8)] = 1;
-          if (count) escapes += sesc[((g + i) >= J.half ? 256 : 0) + ((w >> 7) & 0xFFu)];
+          if (!kStats) {
+            spres[presence_index(w >> 8)] = 1;
+          } else {
+            const uint32_t si = stats_index(w >> 7);
+            if (kPresence) spres[si] = 1;
+            if (count) escapes += sesc[((g + i) >= J.half ? 512 : 0) + si];
+          }
         }
       }
     }
