@@ -611,7 +611,7 @@ def b200_arm(args):
             "head_dim": cfg.head_dim, "block_tokens": cfg.block_tokens, "pool_blocks": P["pool"],
             "jobs_per_step": J, "raw_bytes_per_step": raw_bytes, "encoded_bytes_per_step": encoded_total,
             "policy": "device-chosen codec per job (top16 -> fixed6 -> raw)",
-            "l2": "inputs larger than L2 (raw KV per step 512 MiB+)",
+            "l2": f"inputs larger than L2 (raw KV per step {raw_bytes / 2**20:.0f} MiB, L2 126 MB)",
             "parallelism": f"independent per-GPU shards x{world} (no collective)",
         },
         "encode_gbs_per_gpu": round(raw_bytes / (ms_enc * 1e-3) / 1e9, 2),
