@@ -589,8 +589,18 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     if (tid < kPresWords) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
   };
   // aux = 1 when the job's escapes already exceed its top16 capacity
-  auto over_cap = [](const EncJob& J, uint32_t, EncDesc& d) {
-    const bool over = kKind == kStatsAuto && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap;
+  // (the total only grows, so a job once seen over stays over: the producer
+  // remembers it and skips the global load for its remaining tiles)
+  const EncJob* over_job = nullptr;  // producer warp: the job last seen over its capacity
+  auto over_cap = [&over_job](const EncJob& J, uint32_t, EncDesc& d) {
+    bool over = false;
+    if (kKind == kStatsAuto) {
+      over = &J == over_job;
+      if (!over && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap) {
+        over = true;
+        over_job = &J;
+      }
+    }
     if ((threadIdx.x & 31) == 0) d.aux = over;
   };
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
