@@ -296,8 +296,9 @@ KVQ_API long long kvq_splitzip_abi_version(void);
  * loads it until exit.  Needs only the reference's capacity
  * (align4(encoded) + 8).  count above 2^27 words (134,217,728) returns -1
  * with a message in kvq_splitzip_last_error().  The first call on a device
- * looks up the array's device address with that device current; make it
- * before any stream capture.  All calls share the array (each clears it
+ * looks up the array's device address with that device current; if the
+ * lookup fails, the call returns -1 with the CUDA error in
+ * kvq_splitzip_last_error().  All calls share the array (each clears it
  * first): calls that overlap on the GPU, e.g. on concurrent streams, race. */
 KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned long long src_ptr,
                                                          unsigned long long dst_ptr,
