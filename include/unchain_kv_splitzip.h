@@ -286,20 +286,23 @@ KVQ_API long long kvq_splitzip_device_errors(void);
 KVQ_API long long kvq_splitzip_abi_version(void);
 
 /* top16 encode that allocates nothing (no counterpart in the reference).
- * Same arguments, stream bytes and return values as
- * kvq_splitzip_bf16_encode_top16, for callers that cannot allocate device
- * memory or leave no spare bytes past the stream (serving engines that give
- * nearly all of HBM to their KV pool, paths that must not call cudaMalloc /
- * cudaFree because those can synchronise the device, runtimes that size
- * stream buffers exactly): the escape counts of its statistics pass live in
- * a 266,304-byte static device array of this library, held by every GPU that
- * loads it until exit.  Needs only the reference's capacity
- * (align4(encoded) + 8).  count above 2^27 words (134,217,728) returns -1
- * with a message in kvq_splitzip_last_error().  The first call on a device
- * looks up the array's device address with that device current; if the
- * lookup fails, the call returns -1 with the CUDA error in
- * kvq_splitzip_last_error().  All calls share the array (each clears it
- * first): calls that overlap on the GPU, e.g. on concurrent streams, race. */
+ * Same arguments, capacity rule (align4(encoded) + 8), stream bytes and
+ * return values as kvq_splitzip_bf16_encode_top16, for callers that cannot
+ * allocate device memory while they encode: serving engines that give nearly
+ * all of HBM to their paged KV pool (a transient allocation can fail there)
+ * and paths that must not call cudaMalloc / cudaFree (those can synchronise
+ * the device).  The escape counts of its statistics pass live in a
+ * 266,304-byte static device array of this library, held by every GPU that
+ * loads it until exit, so it writes no byte of the caller's buffer past the
+ * stream.  count above 2^27 words (134,217,728) returns -1 with a message in
+ * kvq_splitzip_last_error().  The first call on a device looks up the
+ * array's device address with that device current and keeps it for the
+ * process; if the lookup fails, the call returns -1 with the CUDA error in
+ * kvq_splitzip_last_error().  A process that resets a device
+ * (cudaDeviceReset) must not call this entry point on that device again: the
+ * kept address belongs to the old context.  All calls share the array (each
+ * clears it first): calls that overlap on the GPU, e.g. on concurrent
+ * streams, race. */
 KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned long long src_ptr,
                                                          unsigned long long dst_ptr,
                                                          unsigned long long count,

@@ -23,7 +23,9 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "libsplitzip_oracle.so"
 REF_SO = HERE / "_ref" / "libref_splitzip_cuda.so"
-REFERENCE_ROOT = Path(os.environ.get("UNCHAIN_KV_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: UNCHAIN_KV_REFERENCE_ROOT, else a checkout named
+# `reference` beside this repository.
+REFERENCE_ROOT = Path(os.environ.get("UNCHAIN_KV_REFERENCE_ROOT") or HERE.parents[1] / "reference")
 REFERENCE_CU = REFERENCE_ROOT / "native" / "unchain_kv" / "kvq_splitzip_cuda.cu"
 
 

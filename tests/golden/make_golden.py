@@ -45,7 +45,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REFERENCE = Path(os.environ.get("UNCHAIN_KV_REFERENCE_ROOT", "/root/reference"))
+# the reference checkout: UNCHAIN_KV_REFERENCE_ROOT, else one named
+# `reference` beside this repository
+REFERENCE = Path(os.environ.get("UNCHAIN_KV_REFERENCE_ROOT") or REPO.parent / "reference")
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REFERENCE / "src"))
 os.environ["UNCHAIN_KV_SPLITZIP_NATIVE_DECODE"] = "0"

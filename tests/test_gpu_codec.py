@@ -88,12 +88,40 @@ def test_top16_encode_declines_like_reference():
     assert gpu_encode_top16(np.zeros(21, np.uint16), tables)[0] == 0   # does not compress
     n = 1 << 16
     enc = oracle.top16_encoded_bytes(n)
-    # room for the stream plus this implementation's per-tile escape counts
+    # the reference's rule: align4(encoded) + 8 <= capacity (.cu:390-394)
     words = np.zeros(n, np.uint16)
     need = splitzip_cuda.top16_capacity(n)
+    assert need == (enc + 3) // 4 * 4 + 8
     assert gpu_encode_top16(words, tables, capacity=need)[0] == enc
     assert gpu_encode_top16(words, tables, capacity=need - 1)[0] == 0
     assert gpu_encode_top16(words, tables, capacity=enc + 4)[0] == 0
+
+
+@pytest.mark.parametrize("n", [22, 47, 1000, 8192, 8192 + 30, 8192 + 47, 8192 + 63, 5 * 8192 + 4096, 1 << 20])
+@pytest.mark.parametrize("rate", [0.002, 0.0049, 0.03])
+@pytest.mark.parametrize("shift", [0, 3, 11])
+def test_top16_encode_at_the_reference_capacity(n, rate, shift):
+    """A buffer of exactly align4(encoded) + 8 bytes, at any byte alignment:
+    the stream equals the oracle's, and no byte past the buffer changes (the
+    encoder keeps its per-tile counts inside the stream's own regions)."""
+    rng = np.random.Generator(np.random.PCG64(n * 13 + shift + int(rate * 1e4)))
+    tables = tables_for(n % 32)
+    words = book_words(rng, (n,), splitzip_cuda._DEFAULT_TOP16_CODEBOOKS[(n % 32) * 32:][:32], rate)
+    cap = splitzip_cuda.top16_capacity(n)
+    expected_res, expected = oracle.encode_top16(words, tables, capacity=cap)
+    assert expected_res == oracle.top16_encoded_bytes(n)
+    src = words_dev(words.reshape(-1))
+    arena = torch.full((cap + 64,), 0xA5, dtype=torch.uint8, device="cuda")
+    out = arena[shift:shift + cap]
+    tab = dev(tables)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # the second call finds the first one's bytes in the buffer
+        res = lib().kvq_splitzip_bf16_encode_top16(src.data_ptr(), out.data_ptr(), n, cap, tab.data_ptr(), stream)
+        torch.cuda.synchronize()
+        assert res == expected_res
+        got = arena.cpu().numpy()
+        assert np.array_equal(got[shift:shift + res], expected), np.flatnonzero(got[shift:shift + res] != expected)[:8]
+        assert (got[:shift] == 0xA5).all() and (got[shift + cap:] == 0xA5).all()
 
 
 @pytest.mark.parametrize("shape,pool", [((16, 8, 128), 96), ((16, 1, 128), 300), ((3, 5), 50), ((16, 2, 64), 40)])

@@ -1,13 +1,16 @@
 """The top16 encoder that allocates nothing, checked against the standard one.
 
-kvq_splitzip_bf16_encode_top16_noalloc serves callers that cannot allocate
-device memory or cannot leave spare bytes past the stream in their buffer:
-serving engines that give nearly all of HBM to their KV pool, paths that must
-not call cudaMalloc / cudaFree (they can synchronise the device), and runtimes
-that size stream buffers exactly.  Its scratch is a static device array shared
-by all calls, so the test makes two calls in a row (the second finds the first
-call's leftovers in the array) and compares both, byte for byte, with
-kvq_splitzip_bf16_encode_top16 through the C ABI.
+Some callers cannot allocate device memory while they encode: a serving
+engine that gives nearly all of HBM to its paged KV pool (a transient
+allocation can fail there), or a path that must not call cudaMalloc /
+cudaFree because those can synchronise the device.
+kvq_splitzip_bf16_encode_top16_noalloc keeps the escape counts of its
+statistics pass in a static device array of the library and writes no byte
+past the stream.  The array is shared by all calls, so the test makes several
+calls in a row (each finds the previous call's leftovers in the array): in
+capacity, then over capacity (a mode-255 stream), then in capacity again.
+Each stream is compared byte for byte with kvq_splitzip_bf16_encode_top16
+through the C ABI and with the CPU oracle.
 This file is collected last on purpose and needs nothing from other tests.
 """
 
@@ -16,6 +19,7 @@ import pytest
 
 torch = pytest.importorskip("torch")
 
+from oracle import oracle  # noqa: E402
 from unchainkv_b200 import splitzip_cuda  # noqa: E402
 
 pytestmark = [
@@ -48,16 +52,16 @@ def test_noalloc_encode_matches_standard_entry_point_on_two_calls():
     lib = splitzip_cuda._load()
     assert lib is not None, splitzip_cuda.load_error()
     stream = torch.cuda.current_stream().cuda_stream
-    cases = [(11, 3 * 8192 + 77, 1, 0.003), (12, 1 << 20, 2, 0.0045)]
+    # in capacity, over capacity (2% escapes against 0.5%), in capacity again
+    cases = [(11, 3 * 8192 + 77, 1, 0.003), (13, (1 << 20) + 96, 3, 0.02), (12, 1 << 20, 2, 0.0045)]
     for seed, n, layer, rate in cases:
         words, tables = make_input(seed, n, layer, rate)
         src = torch.from_numpy(words.view(np.int16)).cuda()
         tab = torch.from_numpy(tables).cuda()
         encoded = top16_bytes(n)
-        # the standard encoder keeps its scratch past the stream: a roomy buffer
-        standard = torch.full((2 * n + 4096,), 0xEE, dtype=torch.uint8, device="cuda")
-        # the no-alloc encoder needs only the reference's capacity rule
+        # both encoders take a buffer sized by the reference's rule
         tight = ((encoded + 3) & ~3) + 8
+        standard = torch.full((tight,), 0xEE, dtype=torch.uint8, device="cuda")
         noalloc = torch.full((tight,), 0x77, dtype=torch.uint8, device="cuda")
         r_std = lib.kvq_splitzip_bf16_encode_top16(src.data_ptr(), standard.data_ptr(), n, standard.numel(),
                                                    tab.data_ptr(), stream)
@@ -68,13 +72,12 @@ def test_noalloc_encode_matches_standard_entry_point_on_two_calls():
         assert r_na == encoded, splitzip_cuda._load().kvq_splitzip_last_error()
         got = noalloc.cpu().numpy()
         assert np.array_equal(got[:encoded], standard.cpu().numpy()[:encoded])
-        assert int(got[0]) == 5
+        # the CPU oracle's canonical stream, overflow form included
+        res, expected = oracle.encode_top16(words, tables, capacity=tight)
+        assert res == encoded and np.array_equal(got[:encoded], expected)
+        assert int(got[0]) == (255 if rate > 0.005 else 5)
         # nothing past the stream was touched
         assert (got[encoded:] == 0x77).all()
-        # the standard encoder declines that tight buffer (it has no room
-        # for its scratch); the no-alloc one is what such callers use
-        assert lib.kvq_splitzip_bf16_encode_top16(src.data_ptr(), noalloc.data_ptr(), n, noalloc.numel(),
-                                                  tab.data_ptr(), stream) == 0
 
 
 def test_noalloc_encode_rejects_counts_beyond_its_static_maximum():

@@ -220,23 +220,21 @@ EncJob base_job(const uint16_t* src, const Layout& L, uint8_t* dst, const uint8_
   return j;
 }
 
-// top16: the reference's rules (.cu:385-395) plus room for the escape
-// counts of the statistics pass (the auto encode's layout, without the
-// bitmap).  The unused escape slots are cleared by the encode kernel.
+// top16: exactly the reference's rules (.cu:385-395).  The statistics pass
+// keeps its per-tile counts inside the stream's own body region (and, for a
+// last tile of fewer than 47 words, in the reference's 8 scratch bytes at
+// align4(encoded)), so nothing else past the stream is needed and nothing
+// is cleared beforehand; the encode kernel clears the unused escape slots.
 bool prepare_top16(const uint16_t* src, const Layout& L, uint8_t* dst, uint64_t capacity,
                    const uint8_t* tables, Prepared& p) {
   const uint64_t n = L.n;
   if (!src || !dst || !tables || n == 0 || n > 0xFFFFFFFFULL) return false;
   const uint64_t encoded = top16_size(n);
   if (encoded >= n * 2 || ((encoded + 3) & ~3ULL) + 8 > capacity) return false;
-  const uint64_t tiles = tiles_for(n);
-  const uint64_t so = align16_from(dst, encoded);
-  const uint64_t scratch = auto_scratch_bytes(tiles);
-  if (so + scratch > capacity) return false;
   p.job = base_job(src, L, dst, tables);
-  p.job.scratch = dst + so;
-  p.zero_ptr = dst + so;
-  p.zero_bytes = scratch;
+  p.job.scratch = nullptr;
+  p.zero_ptr = nullptr;
+  p.zero_bytes = 0;
   p.result = encoded;
   return true;
 }
@@ -300,7 +298,7 @@ void prepare_decode(const uint8_t* src, uint64_t src_bytes, uint16_t* dst, const
 
 // ------------------------------------------------------------------ launch
 
-enum class EncOp { kTop16, kFixed6, kFixed5, kAuto };
+enum class EncOp { kTop16, kTop16Scratch, kFixed6, kFixed5, kAuto };
 
 template <int kMax>
 long long launch_zero(const std::vector<Prepared>& jobs, size_t first, size_t count,
@@ -344,11 +342,27 @@ template <int kMax>
 long long launch_encode_kernels(EncOp op, const EncBatch<kMax>& b, uint32_t tiles, cudaStream_t stream) {
   switch (op) {
     case EncOp::kTop16: {
-      // escape counts of every tile, then the top16 streams at known offsets
+      // escape counts of every tile into its record in the stream, their
+      // scan per job (+ header), then the top16 streams at known offsets
+      long long rc =
+          launch_persistent(PresenceKernel<kMax, kStatsTop16Rec>, "Top16StatsKernel", kEncSmemBytes, b, tiles, stream);
+      if (rc < 0) return rc;
+      const long long prof = prof_begin(stream);
+      Top16ScanKernel<kMax><<<b.jobs, kScanThreads, 0, stream>>>(b);
+      prof_end(prof, "Top16ScanKernel", stream);
+      const cudaError_t st = cudaGetLastError();
+      if (st != cudaSuccess) return Fail("Top16ScanKernel", st);
+      return launch_persistent(EncodeAutoKernel<kMax, kEncTop16Rec>, "EncodeTop16Kernel", kEncSmemBytes, b, tiles,
+                               stream);
+    }
+    case EncOp::kTop16Scratch: {
+      // escape counts of every tile into the scratch array, then the top16
+      // streams at known offsets
       const long long rc =
           launch_persistent(PresenceKernel<kMax, kStatsTop16>, "Top16StatsKernel", kEncSmemBytes, b, tiles, stream);
       if (rc < 0) return rc;
-      return launch_persistent(EncodeAutoKernel<kMax, true>, "EncodeTop16Kernel", kEncSmemBytes, b, tiles, stream);
+      return launch_persistent(EncodeAutoKernel<kMax, kEncTop16Scratch>, "EncodeTop16Kernel", kEncSmemBytes, b,
+                               tiles, stream);
     }
     case EncOp::kFixed6:
     case EncOp::kFixed5: {
@@ -363,7 +377,7 @@ long long launch_encode_kernels(EncOp op, const EncBatch<kMax>& b, uint32_t tile
       const long long rc =
           launch_persistent(PresenceKernel<kMax, kStatsAuto>, "StatsKernel", kEncSmemBytes, b, tiles, stream);
       if (rc < 0) return rc;
-      return launch_persistent(EncodeAutoKernel<kMax, false>, "EncodeAutoKernel", kEncSmemBytes, b, tiles, stream);
+      return launch_persistent(EncodeAutoKernel<kMax, kEncAuto>, "EncodeAutoKernel", kEncSmemBytes, b, tiles, stream);
     }
   }
   return 0;
@@ -372,8 +386,10 @@ long long launch_encode_kernels(EncOp op, const EncBatch<kMax>& b, uint32_t tile
 template <int kMax>
 long long launch_encode(EncOp op, const std::vector<Prepared>& jobs, size_t first, size_t count,
                         cudaStream_t stream) {
-  const long long rc = launch_zero<kMax>(jobs, first, count, stream);
-  if (rc < 0) return rc;
+  if (op != EncOp::kTop16) {  // the top16 encode keeps no scratch to clear
+    const long long rc = launch_zero<kMax>(jobs, first, count, stream);
+    if (rc < 0) return rc;
+  }
   EncBatch<kMax> b{};
   b.jobs = static_cast<uint32_t>(count);
   uint32_t tiles = 0;
@@ -1197,21 +1213,19 @@ extern "C" KVQ_API long long kvq_splitzip_profile_launches(int i) {
 }
 
 // ---------------------------------------------------------------------
-// top16 encode that allocates nothing and needs no scratch in the caller's
+// top16 encode that allocates nothing and keeps no scratch in the caller's
 // buffer.
 //
 // Some callers cannot allocate device memory on the encode path:
 // - serving engines that hand nearly all of HBM to their own paged KV pool
 //   (vLLM's gpu_memory_utilization), where a transient allocation can fail;
 // - latency-critical paths that must not call cudaMalloc / cudaFree, which
-//   can synchronise the device;
-// - plugins whose host runtime owns device memory and sizes each stream
-//   buffer exactly to the stream, leaving no spare bytes past it for the
-//   scratch kvq_splitzip_bf16_encode_top16 keeps there.
+//   can synchronise the device.
 // This variant keeps the escape counts of its statistics pass in a fixed
-// device array of this library instead.  The array is part of the module
-// image: every GPU that loads the library holds it until process exit, and
-// no call here (or in the kernels) allocates or frees memory.
+// device array of this library, so it writes no byte past the stream.  The
+// array is part of the module image: every GPU that loads the library holds
+// it until process exit, and no call here (or in the kernels) allocates or
+// frees memory.
 // ---------------------------------------------------------------------
 
 namespace {
@@ -1229,7 +1243,8 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 // Device address of g_noalloc_scratch on each device.  Host code cannot use
 // the symbol itself (it names a host-side shadow); the address is looked up
 // once per device, with that device current, the first time this entry point
-// runs on it.
+// runs on it, and kept for the process (a device reset invalidates it; the
+// header says so).
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_address[kNoAllocMaxDevices] = {};
@@ -1296,6 +1311,6 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned lon
   // encode kernel clears the stream's unused escape slots).
   const cudaError_t st = cudaMemsetAsync(scratch, 0, auto_scratch_bytes(b.job[0].tiles), stream);
   if (st != cudaSuccess) return Fail("cudaMemsetAsync", st);
-  const long long rc = launch_encode_kernels(EncOp::kTop16, b, b.job[0].tiles, stream);
+  const long long rc = launch_encode_kernels(EncOp::kTop16Scratch, b, b.job[0].tiles, stream);
   return rc < 0 ? rc : static_cast<long long>(encoded);
 }

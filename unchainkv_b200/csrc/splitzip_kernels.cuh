@@ -136,6 +136,43 @@ __host__ __device__ constexpr uint64_t auto_scratch_bytes(uint64_t tiles) {
 }
 constexpr uint64_t kFixedScratchBytes = 36;
 
+// Scratch of the reference-ABI top16 encode, kept inside the stream itself:
+// the reference's capacity rule (align4(encoded) + 8, kvq_splitzip_cuda.cu:
+// 390-394) leaves no room past the stream for per-tile counts.  Tile t's
+// 32-byte count record is the first 16-byte aligned slot of the tile's own
+// body region; only the encode of tile t overwrites it, after that tile's
+// producer has read it.  A last tile too short to hold one (it then holds
+// the words of warp 0 alone) keeps a 4-byte record in the reference's own
+// scratch bytes at align4(encoded).
+//   stats pass: u16[8] at +0 = escapes of each warp's run of the tile;
+//   scan pass:  u16[8] at +0 = escapes of the tile before each warp's run,
+//               u32 at +16 = escapes of the job before the tile; header;
+//   encode:     the producer copies the record into the stage descriptor.
+constexpr uint64_t kTailRecord = ~0ull;
+__host__ __device__ constexpr uint64_t top16_stream_bytes(uint64_t n) {
+  return 5 + n + (n + 1) / 2 + 5 * ((n + 199) / 200);
+}
+__host__ __device__ constexpr uint64_t top16_tail_offset(uint64_t n) { return (top16_stream_bytes(n) + 3) & ~3ull; }
+__host__ __device__ inline uint64_t top16_record_offset(uint64_t dst_addr, uint64_t n, uint64_t t) {
+  const uint64_t body = 5 + t * kTileWords;
+  const uint64_t left = n - t * kTileWords;
+  const uint64_t len = left < kTileWords ? left : kTileWords;
+  const uint64_t off = ((dst_addr + body + 15) & ~15ull) - dst_addr;
+  return off + 32 <= body + len ? off : kTailRecord;
+}
+
+// Little-endian u32 at any byte address.
+__device__ __forceinline__ uint32_t ld_u32_bytes(const uint8_t* p) {
+  return p[0] | (static_cast<uint32_t>(p[1]) << 8) | (static_cast<uint32_t>(p[2]) << 16) |
+         (static_cast<uint32_t>(p[3]) << 24);
+}
+__device__ __forceinline__ void st_u32_bytes(uint8_t* p, uint32_t v) {
+  p[0] = static_cast<uint8_t>(v);
+  p[1] = static_cast<uint8_t>(v >> 8);
+  p[2] = static_cast<uint8_t>(v >> 16);
+  p[3] = static_cast<uint8_t>(v >> 24);
+}
+
 __device__ unsigned int g_device_errors;
 
 __device__ __forceinline__ void raise_error(uint32_t* flag) {
@@ -535,7 +572,10 @@ __device__ __forceinline__ void write_top16_header(uint8_t* dst, uint64_t total,
 //   kStatsAuto: the bitmap and the top16 escape count of every tile (-> tile
 //     count per warp, group sum, job total; each warp adds its own share, so
 //     no CTA barrier is needed for the counts), for the auto encode;
-//   kStatsTop16: the escape counts alone, for the explicit top16 encode.
+//   kStatsTop16: the escape counts alone into the scratch array (the top16
+//     encode that allocates nothing);
+//   kStatsTop16Rec: the escape counts alone into each tile's record inside
+//     the stream (the reference-ABI top16 encode).
 //
 // The presence table holds high byte h at index h ^ (sign << 2), so that a
 // value and its negation (which share every other bit of h) fall in
@@ -553,12 +593,12 @@ template <uint32_t kOff> struct StatsPlane { static constexpr uint32_t kOffset =
 // bank bit 4 (byte bit 6), for the 512-entry stats tables.
 __device__ __forceinline__ uint32_t stats_index(uint32_t i9) { return i9 ^ ((i9 >> 2) & 0x40u); }
 
-enum StatsKind { kStatsPresence = 0, kStatsAuto = 1, kStatsTop16 = 2 };
+enum StatsKind { kStatsPresence = 0, kStatsAuto = 1, kStatsTop16 = 2, kStatsTop16Rec = 3 };
 
 template <int kMax, int kKind>
 __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_constant__ EncBatch<kMax> b) {
   constexpr bool kStats = kKind != kStatsPresence;
-  constexpr bool kPresence = kKind != kStatsTop16;
+  constexpr bool kPresence = kKind != kStatsTop16 && kKind != kStatsTop16Rec;
   extern __shared__ __align__(128) uint8_t ring[];
   // Presence is kept per high byte (256 entries) when only presence is wanted,
   // and per sign-and-exponent (512 entries) when escapes are counted too: one
@@ -679,7 +719,17 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
         }
       }
     }
-    if (count) {
+    if (kKind == kStatsTop16Rec) {
+      // every warp writes its count (the record is not cleared beforehand)
+      escapes = warp_sum(escapes);
+      if (lane == 0) {
+        const uint64_t off = top16_record_offset(reinterpret_cast<uint64_t>(J.dst), J.n, tile);
+        if (off != kTailRecord)
+          reinterpret_cast<uint16_t*>(J.dst + off)[warp] = static_cast<uint16_t>(escapes);
+        else if (warp == 0)
+          st_u32_bytes(J.dst + top16_tail_offset(J.n), escapes);
+      }
+    } else if (count) {
       escapes = warp_sum(escapes);
       if (lane == 0 && escapes) {
         uint64_t* groups = reinterpret_cast<uint64_t*>(J.scratch + 64);
@@ -907,14 +957,19 @@ __device__ __forceinline__ void raw_tile_body(const EncJob& J, uint64_t t0, uint
 // fallback order (vllm_connector.py:3104-3118, 4557-4633): top16 if the
 // escapes fit, else fixed6 if <= 64 high bytes, else raw mode 6 when the
 // buffer holds it, else a fixed6 overflow stream (mode 255) for the host.
-// With kTop16Only (the explicit top16 encode, after a kStatsTop16 pass)
-// every job is coded as top16; one whose escapes exceed its capacity gets
-// the reference's overflow form (mode byte 255, count = cap, the first cap
-// escapes).
+// The top16 variants (the explicit top16 encode) code every job as top16;
+// one whose escapes exceed its capacity gets the reference's overflow form
+// (mode byte 255, count = cap, the first cap escapes).  kEncTop16Scratch
+// follows a kStatsTop16 pass (counts in the scratch array); kEncTop16Rec
+// follows kStatsTop16Rec + Top16ScanKernel (per-tile records in the stream,
+// header already written).
 enum AutoKind { kAutoTop16 = 0, kAutoFixed6 = 1, kAutoRaw = 2, kAutoOverflow = 3 };
+enum EncVariant { kEncAuto = 0, kEncTop16Scratch = 1, kEncTop16Rec = 2 };
 
-template <int kMax, bool kTop16Only>
+template <int kMax, int kVariant>
 __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_constant__ EncBatch<kMax> b) {
+  constexpr bool kTop16Only = kVariant != kEncAuto;
+  constexpr bool kRec = kVariant == kEncTop16Rec;
   extern __shared__ __align__(128) uint8_t ring[];
   __shared__ uint32_t stbl[512];
   __shared__ uint8_t srank[256];
@@ -940,6 +995,31 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   uint4 win = make_uint4(0, 0, 0, 0);
   auto prefix_hook = [&](const EncJob& J, uint32_t tile, EncDesc& d) {
     const int lane = threadIdx.x & 31;
+    if constexpr (kRec) {
+      if (&J != hook_job) {
+        hook_job = &J;
+        // the scan pass wrote the header: count = min(escapes, cap)
+        zlo0 = 5ull * ld_u32_bytes(J.dst + 1);
+        zhi = 5 * J.cap;
+        zshare = zlo0 < zhi ? (zhi - zlo0 + J.tiles - 1) / J.tiles : 0;
+      }
+      const uint64_t off = top16_record_offset(reinterpret_cast<uint64_t>(J.dst), J.n, tile);
+      uint32_t wpre = 0;
+      uint32_t prefix;
+      if (off == kTailRecord) {
+        prefix = ld_u32_bytes(J.dst + top16_tail_offset(J.n));
+      } else {
+        if (lane < kWarps) wpre = reinterpret_cast<const uint16_t*>(J.dst + off)[lane];
+        prefix = *reinterpret_cast<const uint32_t*>(J.dst + off + 16);
+      }
+      if (lane == 0) d.prefix = prefix;
+      if (lane < kWarps) d.wpre[lane] = wpre;
+      uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
+      const uint64_t a = min(zhi, zlo0 + zshare * tile);
+      const uint64_t e = min(zhi, a + zshare);
+      for (uint64_t i = a + lane; i < e; i += 32) entries[i] = 0;
+      return;
+    }
     const uint16_t* counts = reinterpret_cast<const uint16_t*>(J.scratch + auto_counts_offset(J.tiles));
     auto load_win = [&](uint32_t first) {
       win_first = first;
@@ -1006,8 +1086,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
       uint32_t distinct = 0, rank = 0;
       bool present = false;
       if (!kTop16Only) palette_ranks(reinterpret_cast<const uint32_t*>(J.scratch + 16), srank, distinct, present, rank);
-      escapes = *reinterpret_cast<const uint32_t*>(J.scratch);
-      const bool err = ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch + 4)) != 0;
+      escapes = kRec ? 0 : *reinterpret_cast<const uint32_t*>(J.scratch);
+      const bool err = !kRec && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch + 4)) != 0;
       kind = kTop16Only ? kAutoTop16
            : err ? kAutoOverflow
            : escapes <= J.cap ? kAutoTop16
@@ -1017,7 +1097,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
         // the CTA holding tile 0 writes the header
         if (tile == 0) {
           if (kTop16Only) {
-            if (tid == 0) write_top16_header(J.dst, escapes, J.cap, err);
+            if (!kRec && tid == 0) write_top16_header(J.dst, escapes, J.cap, err);
           } else if (kind == kAutoOverflow) write_fixed_header<6>(J.dst, distinct > 64 ? distinct : 65, present, rank, true);
           else if (kind == kAutoFixed6) write_fixed_header<6>(J.dst, distinct, present, rank, false);
           else if (kind == kAutoRaw && tid == 0) J.dst[0] = 6;
@@ -1044,6 +1124,95 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
     top16_tile_body(J, t0, len, sin, stbl, masks);
     warp_write_escapes(J, t0, sin, masks, desc.prefix + desc.wpre[tid >> 5]);
   }, prefix_hook);
+}
+
+// Exclusive scan of the per-tile escape counts of each job (one CTA per
+// job), between the kStatsTop16Rec pass and EncodeAutoKernel<., kEncTop16Rec>:
+// every record gets the escapes of the job before its tile and of the tile
+// before each warp's run, and thread 0 writes the stream header (mode 5, or
+// 255 when the escapes exceed the capacity; the count clamped to it).
+constexpr int kScanThreads = 256;
+constexpr int kScanTilesPerThread = 4;
+
+template <int kMax>
+__global__ void __launch_bounds__(kScanThreads) Top16ScanKernel(const __grid_constant__ EncBatch<kMax> b) {
+  __shared__ uint32_t wsum[kScanThreads / 32];
+  const uint32_t j = blockIdx.x;
+  if (j >= b.jobs) return;
+  const EncJob& J = b.job[j];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const uint64_t addr = reinterpret_cast<uint64_t>(J.dst);
+  constexpr uint32_t kChunk = kScanThreads * kScanTilesPerThread;
+  uint32_t carry = 0;
+  for (uint32_t base = 0; base < J.tiles; base += kChunk) {
+    // this thread's kScanTilesPerThread consecutive tiles
+    uint32_t tot[kScanTilesPerThread];
+    uint4 rec[kScanTilesPerThread];
+    uint64_t off[kScanTilesPerThread];
+    uint32_t mine = 0;
+#pragma unroll
+    for (int k = 0; k < kScanTilesPerThread; ++k) {
+      const uint32_t t = base + tid * kScanTilesPerThread + k;
+      rec[k] = make_uint4(0, 0, 0, 0);
+      off[k] = kTailRecord;
+      tot[k] = 0;
+      if (t < J.tiles) {
+        off[k] = top16_record_offset(addr, J.n, t);
+        if (off[k] != kTailRecord) {
+          rec[k] = *reinterpret_cast<const uint4*>(J.dst + off[k]);
+          const uint32_t pairs = (rec[k].x + rec[k].y) + (rec[k].z + rec[k].w);  // two u16 sums, each < 2^16
+          tot[k] = (pairs & 0xFFFFu) + (pairs >> 16);
+        } else {
+          tot[k] = ld_u32_bytes(J.dst + top16_tail_offset(J.n));
+        }
+      }
+      mine += tot[k];
+    }
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    uint32_t before = carry, chunk = 0;
+#pragma unroll
+    for (int w = 0; w < kScanThreads / 32; ++w) {
+      if (w < warp) before += wsum[w];
+      chunk += wsum[w];
+    }
+    before += incl - mine;
+#pragma unroll
+    for (int k = 0; k < kScanTilesPerThread; ++k) {
+      const uint32_t t = base + tid * kScanTilesPerThread + k;
+      if (t < J.tiles) {
+        if (off[k] != kTailRecord) {
+          // escapes of the tile before each warp's run, as u16
+          const uint32_t c[kWarps] = {rec[k].x & 0xFFFFu, rec[k].x >> 16, rec[k].y & 0xFFFFu, rec[k].y >> 16,
+                                      rec[k].z & 0xFFFFu, rec[k].z >> 16, rec[k].w & 0xFFFFu, rec[k].w >> 16};
+          uint32_t p[kWarps];
+          uint32_t run = 0;
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) {
+            p[w] = run;
+            run += c[w];
+          }
+          *reinterpret_cast<uint4*>(J.dst + off[k]) =
+              make_uint4(p[0] | (p[1] << 16), p[2] | (p[3] << 16), p[4] | (p[5] << 16), p[6] | (p[7] << 16));
+          *reinterpret_cast<uint32_t*>(J.dst + off[k] + 16) = before;
+        } else {
+          st_u32_bytes(J.dst + top16_tail_offset(J.n), before);
+        }
+      }
+      before += tot[k];
+    }
+    carry += chunk;
+    __syncthreads();  // wsum is reused by the next chunk
+  }
+  if (tid == 0) write_top16_header(J.dst, carry, J.cap, false);
 }
 
 // ------------------------------------------------------------ calibration

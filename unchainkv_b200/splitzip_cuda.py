@@ -678,13 +678,11 @@ def torchop_capacity(n: int) -> int:
 
 
 def top16_capacity(n: int) -> int:
-    """Stream-buffer bytes for the top16 encoders (kvq_splitzip_bf16_encode_top16
-    and its _blocks / _batch forms) with a 16-byte aligned buffer: the stream,
-    then from its next 16-byte boundary the escape counts of the statistics
-    pass.  The _noalloc form needs only the reference's rule."""
-    tiles = (n + 8191) // 8192
-    scratch = 64 + (8 * ((tiles + 31) // 32) + 15) // 16 * 16 + 16 * tiles
-    return (top16_stream_bytes(n) + 15) // 16 * 16 + scratch
+    """Least stream-buffer bytes the top16 encoders accept
+    (kvq_splitzip_bf16_encode_top16 and its _blocks / _batch / _noalloc
+    forms): the reference's rule, align4(stream) + 8
+    (native/unchain_kv/kvq_splitzip_cuda.cu:390-394)."""
+    return (top16_stream_bytes(n) + 3) // 4 * 4 + 8
 
 
 def auto_capacity(n: int, raw: bool = True) -> int:
