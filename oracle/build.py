@@ -2,6 +2,9 @@
 
 * ``oracle/_build/libsplitzip_oracle.so``: the C restatement in
   ``splitzip_oracle.c`` (gcc, OpenMP).
+* ``baseline/_ref``: the reference's own Python package installed from the
+  checkout, with its wrapper tests (``reference_tests/``): the GPU tests run
+  them against this repository's library.
 * ``oracle/_ref/libref_splitzip_cuda.so``: the reference's own CUDA codec
   compiled unchanged from ``native/unchain_kv/kvq_splitzip_cuda.cu`` where it
   lies in the reference checkout (nvcc, sm_100a).  The GPU tests use it to
@@ -69,9 +72,44 @@ def build_reference(force: bool = False) -> Path | None:
     return REF_SO
 
 
+REF_PACKAGE = HERE.parent / "baseline" / "_ref"
+REF_TESTS = REF_PACKAGE / "reference_tests"
+REFERENCE_WRAPPER = REFERENCE_ROOT / "src" / "unchain_kv" / "splitzip_cuda.py"
+REFERENCE_WRAPPER_TESTS = REFERENCE_ROOT / "tests" / "test_splitzip_cuda.py"
+
+
+def build_reference_package(force: bool = False) -> Path | None:
+    """Install the reference's own Python package (pure Python, no
+    dependencies) into baseline/_ref with an offline pip, from a temporary
+    copy of the checkout (its build writes into the source tree), and put the
+    reference's wrapper tests beside it in baseline/_ref/reference_tests.
+    The GPU tests run those tests, and the reference's ctypes wrapper, against
+    this repository's library (UNCHAIN_KV_SPLITZIP_LIB).  Only when the
+    checkout is present; the GPU box reuses the copy that travelled."""
+    installed = REF_PACKAGE / "unchain_kv" / "splitzip_cuda.py"
+    if not REFERENCE_WRAPPER.exists():
+        return REF_PACKAGE if installed.exists() else None
+    if force or _stale(installed, REFERENCE_WRAPPER) or not (REF_TESTS / REFERENCE_WRAPPER_TESTS.name).exists():
+        import sys
+        import tempfile
+
+        with tempfile.TemporaryDirectory() as tmp:
+            src = Path(tmp) / "reference"
+            shutil.copytree(REFERENCE_ROOT, src, ignore=shutil.ignore_patterns(".git", "build", "*.egg-info"))
+            subprocess.run(
+                [sys.executable, "-m", "pip", "install", "--quiet", "--no-index", "--no-deps",
+                 "--no-build-isolation", "--upgrade", "--target", str(REF_PACKAGE), str(src)],
+                check=True,
+            )
+        REF_TESTS.mkdir(parents=True, exist_ok=True)
+        shutil.copy2(REFERENCE_WRAPPER_TESTS, REF_TESTS / REFERENCE_WRAPPER_TESTS.name)
+    return REF_PACKAGE
+
+
 def build(force: bool = False) -> None:
     build_oracle(force)
     build_reference(force)
+    build_reference_package(force)
 
 
 if __name__ == "__main__":

@@ -188,6 +188,35 @@ def decode_modes_blocks(stream, cache, block_ids, block_start: int = 0):
         block_start, _ptr(ids)))
 
 
+def encode_auto_blocks(cache, block_ids, tables, raw_ok: bool = True, threads: int | None = None) -> np.ndarray:
+    """The reference producer's codec chain on one job, in canonical form:
+    top16 when the escapes fit its capacity (vllm_connector.py:3104-3118),
+    else fixed6 when at most 64 high bytes occur, else raw mode 6 ([6] + the
+    words) when ``raw_ok`` (vllm_connector.py:4557-4633), else the fixed6
+    overflow stream (mode 255).  Multi-threaded (OpenMP) over the job's
+    words.  Returns the stream bytes."""
+    cache = _u16(cache)
+    plane_stride = int(np.prod(cache.shape[1:]))
+    block_words = int(np.prod(cache.shape[2:]))
+    ids = np.ascontiguousarray(block_ids, dtype=np.int64)
+    n = 2 * len(ids) * block_words
+    threads = threads or max_threads()
+    tables = np.ascontiguousarray(tables, dtype=np.uint8)
+    out = np.zeros(2 * n + 4096, dtype=np.uint8)
+    res = lib().orc_encode_top16_blocks_mt(_ptr(cache), plane_stride, block_words, block_words, _ptr(ids), 0,
+                                           len(ids), _ptr(out), out.size, _ptr(tables), threads)
+    if res > 0 and out[0] == 5:
+        return out[:res].copy()
+    res = lib().orc_encode_mode_blocks_mt(_ptr(cache), plane_stride, block_words, block_words, _ptr(ids), 0,
+                                          len(ids), _ptr(out), out.size, 6, threads)
+    if res > 0 and out[0] == 3:
+        return out[:res].copy()
+    if raw_ok:
+        words = np.ascontiguousarray(cache[:, ids]).reshape(-1)
+        return np.concatenate([np.array([6], dtype=np.uint8), words.view(np.uint8)])
+    return out[:max(int(res), 0)].copy()
+
+
 def max_threads() -> int:
     return int(lib().orc_max_threads())
 
