@@ -279,8 +279,30 @@ KVQ_API long long kvq_splitzip_top16_tables_from_histograms(unsigned long long h
                                                            unsigned long long stream_ptr);
 
 /* Count of device-side bounded waits that ran out on the current device
- * since load (0 in normal operation).  Synchronous; -1 on CUDA error. */
+ * since load or the last reset (0 in normal operation).  Synchronous; -1 on
+ * CUDA error.  A wait that runs out while a stream is encoded also gives
+ * that stream a mode-255 header (no receiver decodes it).  Replaces the
+ * reference's unbounded spin (kvq_splitzip_cuda.cu:51-55), which has no
+ * status. */
 KVQ_API long long kvq_splitzip_device_errors(void);
+
+/* Reset that count to 0 on the current device.  Synchronous; 0, or -1 on
+ * CUDA error. */
+KVQ_API long long kvq_splitzip_device_errors_reset(void);
+
+/* Test hook of the bounded waits (no counterpart in the reference): the
+ * encode of kvq_splitzip_bf16_encode_mode with its statistics pass built
+ * with a limit of 4 tries per wait and its producer leaving the full barrier
+ * of tile `skip_tile` (8192-word tiles) one arrival short.  That wait runs
+ * out: the count above grows, the stream gets a mode-255 header, the call
+ * returns like kvq_splitzip_bf16_encode_mode.  Nothing faults or waits
+ * without a limit. */
+KVQ_API long long kvq_splitzip_test_encode_mode_skip_arrival(unsigned long long src_ptr,
+                                                             unsigned long long dst_ptr,
+                                                             unsigned long long count,
+                                                             unsigned long long capacity,
+                                                             unsigned long long stream_ptr, int bits,
+                                                             unsigned long long skip_tile);
 
 /* ABI revision of the extension entry points. */
 KVQ_API long long kvq_splitzip_abi_version(void);

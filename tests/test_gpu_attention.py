@@ -143,11 +143,14 @@ def test_group_sizes():
     run([300, 40], [5, 5], group=8, seed=11, aligned=11)
 
 
-def test_batch_like_config4():
-    """configs[4] in small: 8 requests, contexts log-uniform in [1024, 8192]."""
-    rng = np.random.Generator(np.random.PCG64(4))
-    ctxs = [int(x) for x in np.exp(rng.uniform(np.log(1024), np.log(8192), size=8))]
-    run(ctxs, [3] * 8, seed=4)
+def test_batch_of_config4():
+    """configs[4] at full size: 32 requests, contexts log-uniform in
+    [1024, 8192] (the benchmark's seeded contexts), fixed6 streams of the
+    configs[0] distribution, 32 q heads over 8 kv heads."""
+    ctxs = W.attention_contexts(W.CONFIGS["c4"])
+    assert len(ctxs) == 32 and min(ctxs) >= 1024 and max(ctxs) <= 8192
+    run(ctxs, [3] * 32, seed=4)
+    run(ctxs, [5] * 32, seed=12)
 
 
 @pytest.mark.parametrize("aligned", [False, True, 11])

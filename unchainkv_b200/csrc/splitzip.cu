@@ -252,6 +252,7 @@ bool prepare_fixed(const uint16_t* src, const Layout& L, uint8_t* dst, uint64_t 
   if ((reinterpret_cast<uintptr_t>(dst) + so) % 4) return false;
   p.job = base_job(src, L, dst, nullptr);
   p.job.scratch = dst + so;
+  p.job.error = reinterpret_cast<uint32_t*>(dst + so + 32);
   p.zero_ptr = dst + so;
   p.zero_bytes = kFixedScratchBytes;
   p.result = encoded;
@@ -275,6 +276,7 @@ bool prepare_auto(const uint16_t* src, const Layout& L, uint8_t* dst, uint64_t c
   p.job = base_job(src, L, dst, tables);
   p.job.raw_ok = raw_ok;
   p.job.scratch = dst + (raw_ok ? raw_so : so);
+  p.job.error = reinterpret_cast<uint32_t*>(p.job.scratch + 4);
   p.zero_ptr = p.job.scratch;
   p.zero_bytes = scratch;  // totals, bitmap, group sums and tile counts start at zero
   p.result = raw_ok ? 1 + 2 * n : compressed;
@@ -436,8 +438,9 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
     return rc;
   } else {
     if (rc < 0) return rc;
-    // the escaped words of the top16 streams, one thread per entry; the grid
-    // covers the largest job's capacity, the jobs go one after another
+    // the escaped words of the top16 streams, one thread per entry: grid
+    // rows are the jobs (all patched at once), each row covers the largest
+    // job's capacity (at most 4 x SMs blocks, striding beyond)
     static thread_local PatchBatch<kMax> pb;
     pb.jobs = b.jobs;
     uint64_t entries = 0;
@@ -452,7 +455,7 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
     const uint64_t blocks =
         std::max<uint64_t>(1, std::min<uint64_t>((entries + 255) / 256, static_cast<uint64_t>(sms) * 4));
     const long long prof = prof_begin(stream);
-    EscapePatchKernel<kMax, kMode><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(pb);
+    EscapePatchKernel<kMax, kMode><<<dim3(static_cast<unsigned>(blocks), b.jobs), 256, 0, stream>>>(pb);
     prof_end(prof, "EscapePatchKernel", stream);
     st = cudaGetLastError();
     return st == cudaSuccess ? 0 : Fail("EscapePatchKernel", st);
@@ -1154,6 +1157,49 @@ extern "C" KVQ_API long long kvq_splitzip_device_errors() {
   return static_cast<long long>(value);
 }
 
+extern "C" KVQ_API long long kvq_splitzip_device_errors_reset() {
+  const unsigned int zero = 0;
+  const cudaError_t st = cudaMemcpyToSymbol(ukv::g_device_errors, &zero, sizeof(zero));
+  if (st != cudaSuccess) return Fail("cudaMemcpyToSymbol", st);
+  return 0;
+}
+
+// Test hook of the bounded waits: the fixed6/fixed5 encode of
+// kvq_splitzip_bf16_encode_mode, with its statistics pass instantiated with
+// a limit of 4 tries per wait instead of 4096, and its producer leaving the
+// full barrier of tile `skip_tile` one arrival short.  The consumers' wait
+// for that stage runs out (at most 2 x 4 suspended tries of up to 1 ms):
+// the kernel counts it in kvq_splitzip_device_errors(), marks the job, and
+// carries on; the encode then writes a mode-255 header, which no receiver
+// decodes.  Nothing faults or waits without a limit.  Same arguments and
+// return values as kvq_splitzip_bf16_encode_mode otherwise.
+extern "C" KVQ_API long long kvq_splitzip_test_encode_mode_skip_arrival(
+    unsigned long long src_ptr, unsigned long long dst_ptr, unsigned long long count,
+    unsigned long long capacity, unsigned long long stream_ptr, int bits, unsigned long long skip_tile) {
+  if (src_ptr == 0 || dst_ptr == 0 || count == 0 || (bits != 5 && bits != 6)) return 0;
+  std::vector<Prepared> p(1);
+  if (!prepare_fixed(reinterpret_cast<const uint16_t*>(src_ptr), flat_layout(count),
+                     reinterpret_cast<uint8_t*>(dst_ptr), capacity, bits, p[0]))
+    return 0;
+  const auto stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  long long rc = launch_zero<1>(p, 0, 1, stream);
+  if (rc < 0) return rc;
+  EncBatch<1> b{};
+  b.jobs = 1;
+  b.skip_tile = static_cast<uint32_t>(std::min<unsigned long long>(skip_tile, 0xFFFFFFFFull));
+  b.job[0] = p[0].job;
+  b.tile_start[0] = 0;
+  b.tile_start[1] = b.job[0].tiles;
+  rc = launch_persistent(PresenceKernel<1, kStatsPresence, 4, true>, "PresenceKernel", kEncSmemBytes, b,
+                         b.job[0].tiles, stream);
+  if (rc < 0) return rc;
+  rc = bits == 6 ? launch_persistent(EncodeFixedKernel<1, 6>, "EncodeFixed6Kernel", kEncSmemBytes, b,
+                                     b.job[0].tiles, stream)
+                 : launch_persistent(EncodeFixedKernel<1, 5>, "EncodeFixed5Kernel", kEncSmemBytes, b,
+                                     b.job[0].tiles, stream);
+  return rc < 0 ? rc : static_cast<long long>(p[0].result);
+}
+
 extern "C" KVQ_API long long kvq_splitzip_abi_version() { return 3; }
 
 extern "C" KVQ_API long long kvq_splitzip_profile_enable(int on) {
@@ -1304,6 +1350,7 @@ extern "C" KVQ_API long long kvq_splitzip_bf16_encode_top16_noalloc(unsigned lon
   b.job[0] = base_job(reinterpret_cast<const uint16_t*>(src_ptr), flat_layout(n), dst,
                       reinterpret_cast<const uint8_t*>(tables_ptr));
   b.job[0].scratch = static_cast<uint8_t*>(scratch);
+  b.job[0].error = reinterpret_cast<uint32_t*>(b.job[0].scratch + 4);
   b.tile_start[0] = 0;
   b.tile_start[1] = b.job[0].tiles;
   // Every call shares the array and finds the previous call's contents in

@@ -107,11 +107,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, ui
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase: at most kBarrierTries suspended tries of
-// up to 1 ms each.  Returns false if the limit ran out.
+// Bounded wait on an mbarrier phase: at most kTries suspended tries of up to
+// 1 ms each (kBarrierTries in every product kernel; a test-only
+// instantiation uses a few).  Returns false if the limit ran out.
 constexpr uint32_t kBarrierTries = 4096;
+template <uint32_t kTries = kBarrierTries>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kBarrierTries; ++i) {
+  for (uint32_t i = 0; i < kTries; ++i) {
     if (mbar_try_wait(bar, parity, 1000000u)) return true;
   }
   return false;

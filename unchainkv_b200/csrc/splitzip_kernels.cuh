@@ -42,6 +42,7 @@ struct EncJob {
   Layout L;
   uint8_t* dst;
   uint8_t* scratch;
+  uint32_t* error;  // set to 1 when a wait of this job's tiles ran out (or null)
   uint64_t n;
   uint64_t half;
   uint64_t cap;  // top16 escape capacity ceil(n/200)
@@ -55,6 +56,7 @@ struct EncJob {
 template <int kMax>
 struct EncBatch {
   uint32_t jobs;
+  uint32_t skip_tile;  // test-only instantiations: the tile whose full-barrier arrival is skipped
   uint32_t tile_start[kMax + 1];
   EncJob job[kMax];
 };
@@ -180,6 +182,24 @@ __device__ __forceinline__ void raise_error(uint32_t* flag) {
   atomicAdd(&g_device_errors, 1u);
 }
 
+// A wait of this tile ran out in the encode pass: the stream's mode byte
+// becomes 255, which no receiver decodes (lane 0 of the late warp; the job's
+// error flag is already set).
+__device__ __forceinline__ void mark_stream_late(const EncJob& J) {
+  __threadfence();
+  J.dst[0] = 255;
+}
+
+// After the header write (thread 0 of the CTA that wrote it): a wait that ran
+// out in the stats pass, or in this pass before the header landed, set the
+// job's flag; the fences order this re-check against mark_stream_late, so
+// whichever store comes last is 255.
+__device__ __forceinline__ void recheck_header(const EncJob& J) {
+  if (J.error == nullptr) return;
+  __threadfence();
+  if (ld_volatile_u32(J.error) != 0) J.dst[0] = 255;
+}
+
 __device__ __forceinline__ uint32_t tile_len(uint64_t n, uint64_t t0) {
   return static_cast<uint32_t>(n - t0 < kTileWords ? n - t0 : kTileWords);
 }
@@ -236,6 +256,7 @@ struct RingPos {
   uint32_t k = 0;
   int s = 0;
   uint32_t phase = 0;
+  bool late = false;  // consumer: the wait for the current stage (or its producer's) ran out
   __device__ __forceinline__ void next() {
     ++k;
     if (++s == S) {
@@ -246,18 +267,22 @@ struct RingPos {
 };
 
 // Bounded wait for a ring barrier phase.  A timeout raises the error flag and
-// waits once more so that no copy is left in flight.
-__device__ __forceinline__ void wait_stage(uint64_t* bar, uint32_t parity, uint32_t* error) {
-  if (!mbar_wait(bar, parity)) {
+// waits once more so that no copy is left in flight.  Returns true when the
+// wait ran out.
+template <uint32_t kTries = kBarrierTries>
+__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity, uint32_t* error) {
+  if (!mbar_wait<kTries>(bar, parity)) {
     raise_error(error);
-    mbar_wait(bar, parity);
+    mbar_wait<kTries>(bar, parity);
+    return true;
   }
+  return false;
 }
 
 // Producer: wait until every consumer warp released the stage's previous use.
-template <int S>
-__device__ __forceinline__ void producer_acquire(Ring<S>& R, const RingPos<S>& p, uint32_t* error) {
-  if (p.k >= S) wait_stage(&R.empty[p.s], p.phase ^ 1u, error);
+template <int S, uint32_t kTries = kBarrierTries>
+__device__ __forceinline__ bool producer_acquire(Ring<S>& R, const RingPos<S>& p, uint32_t* error) {
+  return p.k >= S && wait_stage<kTries>(&R.empty[p.s], p.phase ^ 1u, error);
 }
 
 // Producer, every lane: publish the stage (after its descriptor writes).
@@ -266,9 +291,9 @@ __device__ __forceinline__ void producer_commit(Ring<S>& R, const RingPos<S>& p)
   mbar_arrive(&R.full[p.s]);
 }
 
-template <int S>
-__device__ __forceinline__ void consumer_wait(Ring<S>& R, const RingPos<S>& p, uint32_t* error) {
-  wait_stage(&R.full[p.s], p.phase, error);
+template <int S, uint32_t kTries = kBarrierTries>
+__device__ __forceinline__ bool consumer_wait(Ring<S>& R, const RingPos<S>& p, uint32_t* error) {
+  return wait_stage<kTries>(&R.full[p.s], p.phase, error);
 }
 
 // Consumer warp: done with the stage (all lanes' reads precede lane 0's arrive).
@@ -294,7 +319,7 @@ struct EncDesc {
   uint32_t tile;
   uint32_t job;
   uint32_t aux;
-  uint32_t unused;
+  uint32_t late;  // the producer's wait for this stage ran out
   uint64_t prefix;        // auto top16: escapes of the job before this tile
   uint32_t wpre[kWarps];  // auto top16: escapes of the tile before each warp's run
 };
@@ -310,7 +335,7 @@ struct NoAux {
 // (increasing; >= total ends) into the ring.  A bulk-capable layout takes one
 // TMA copy per contiguous run, the runs spread over the 32 lanes; any other
 // is gathered word by word by the 32 lanes.
-template <int kMax, typename Next, typename Aux = NoAux>
+template <int kMax, uint32_t kTries = kBarrierTries, bool kSkipTest = false, typename Next, typename Aux = NoAux>
 __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R, EncDesc* D,
                                                 Next&& next_tile, Aux aux = Aux()) {
   const int lane = threadIdx.x & 31;
@@ -318,7 +343,7 @@ __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t
   EncPos p;
   int ji = 0;
   for (;;) {
-    producer_acquire(R, p, nullptr);
+    const bool late = producer_acquire<kEncStages, kTries>(R, p, nullptr);
     const uint32_t t = next_tile();
     if (t >= total) {
       if (lane == 0) D[p.s].tile = kEndTile;
@@ -333,6 +358,7 @@ __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t
     if (lane == 0) {
       D[p.s].tile = t;
       D[p.s].job = static_cast<uint32_t>(ji);
+      D[p.s].late = late;
     }
     if (J.bulk != 0) {
       stage_words_tma(J.src, J.L, t0, len, sin, &R.full[p.s]);
@@ -340,7 +366,12 @@ __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t
       gather_words_warp(J.src, J.L, t0, len, sin);
     }
     aux(J, t - b.tile_start[ji], D[p.s]);
-    producer_commit(R, p);
+    if (kSkipTest && t == b.skip_tile && lane == 31) {
+      // test-only: this stage's full barrier stays one arrival short, so the
+      // consumers' bounded wait for it runs out
+    } else {
+      producer_commit(R, p);
+    }
     p.next();
   }
 }
@@ -353,15 +384,19 @@ struct ChunkTiles {
 
 // Consumer warps of the encode kernels: fn(job, job_index, tile, words,
 // ring position, descriptor) for every staged tile until the end descriptor.
-template <int kMax, typename Fn>
+template <int kMax, uint32_t kTries = kBarrierTries, typename Fn>
 __device__ __forceinline__ void encode_consumer(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R,
                                                 const EncDesc* D, Fn&& fn) {
   EncPos p;
   for (;;) {
-    consumer_wait(R, p, nullptr);
+    const bool late = consumer_wait<kEncStages, kTries>(R, p, nullptr);
     const EncDesc& d = D[p.s];  // read in place; the stage is released after fn
     if (d.tile == kEndTile) return;
     const EncJob& J = b.job[d.job];
+    // a wait that ran out marks the job's stream (the encode then writes
+    // the mode-255 header, which no receiver decodes)
+    p.late = late || d.late != 0;
+    if (p.late && J.error != nullptr && (threadIdx.x & 31) == 0) atomicOr(J.error, 1u);
     fn(J, static_cast<int>(d.job), d.tile - b.tile_start[d.job],
        reinterpret_cast<const uint16_t*>(ring + p.s * kEncStageBytes), p, d);
     consumer_release(R, p);
@@ -370,15 +405,15 @@ __device__ __forceinline__ void encode_consumer(const EncBatch<kMax>& b, uint8_t
 }
 
 // Chunk-scheduled encode kernel body: producer warp + consumer warps.
-template <int kMax, typename Fn, typename Aux = NoAux>
+template <int kMax, uint32_t kTries = kBarrierTries, bool kSkipTest = false, typename Fn, typename Aux = NoAux>
 __device__ __forceinline__ void encode_pipeline(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R, EncDesc* D,
                                                 Fn&& fn, Aux aux = Aux()) {
   if ((threadIdx.x >> 5) == kProducerWarp) {
     const Chunk c = cta_chunk(b.tile_start[b.jobs]);
-    encode_producer<kMax>(b, ring, R, D, ChunkTiles{c.first, c.last}, aux);
+    encode_producer<kMax, kTries, kSkipTest>(b, ring, R, D, ChunkTiles{c.first, c.last}, aux);
     return;
   }
-  encode_consumer<kMax>(b, ring, R, D, fn);
+  encode_consumer<kMax, kTries>(b, ring, R, D, fn);
 }
 
 // ------------------------------------------------------------ top16 encode
@@ -595,7 +630,7 @@ __device__ __forceinline__ uint32_t stats_index(uint32_t i9) { return i9 ^ ((i9 
 
 enum StatsKind { kStatsPresence = 0, kStatsAuto = 1, kStatsTop16 = 2, kStatsTop16Rec = 3 };
 
-template <int kMax, int kKind>
+template <int kMax, int kKind, uint32_t kTries = kBarrierTries, bool kSkipTest = false>
 __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_constant__ EncBatch<kMax> b) {
   constexpr bool kStats = kKind != kStatsPresence;
   constexpr bool kPresence = kKind != kStatsTop16 && kKind != kStatsTop16Rec;
@@ -643,8 +678,9 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     }
     if ((threadIdx.x & 31) == 0) d.aux = over;
   };
-  encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos&, const EncDesc& desc) {
+  encode_pipeline<kMax, kTries, kSkipTest>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile,
+                                                               const uint16_t* sin, const EncPos& pos,
+                                                               const EncDesc& desc) {
     const uint32_t skip_escapes = desc.aux;
     if (j != pres_job || (kStats && j != table_job)) {  // uniform across the consumers
       consumer_sync();
@@ -720,14 +756,17 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
       }
     }
     if (kKind == kStatsTop16Rec) {
-      // every warp writes its count (the record is not cleared beforehand)
+      // every warp writes its count (the record is not cleared beforehand);
+      // after a wait that ran out it writes a count no run can have (a run
+      // holds at most 1024 words), which the scan turns into a mode-255
+      // header
       escapes = warp_sum(escapes);
       if (lane == 0) {
         const uint64_t off = top16_record_offset(reinterpret_cast<uint64_t>(J.dst), J.n, tile);
         if (off != kTailRecord)
-          reinterpret_cast<uint16_t*>(J.dst + off)[warp] = static_cast<uint16_t>(escapes);
+          reinterpret_cast<uint16_t*>(J.dst + off)[warp] = pos.late ? 0xFFFFu : static_cast<uint16_t>(escapes);
         else if (warp == 0)
-          st_u32_bytes(J.dst + top16_tail_offset(J.n), escapes);
+          st_u32_bytes(J.dst + top16_tail_offset(J.n), pos.late ? 0xFFFFFFFFu : escapes);
       }
     } else if (count) {
       escapes = warp_sum(escapes);
@@ -898,14 +937,18 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeFixedKernel(const __grid
   int rank_job = -1;
   bool skip = false;
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos&, const EncDesc&) {
+                                           const EncPos& pos, const EncDesc&) {
+    if (pos.late && (threadIdx.x & 31) == 0) mark_stream_late(J);
     if (j != rank_job) {  // uniform across the consumers
       consumer_sync();    // every warp is done with the previous ranks
       uint32_t distinct, rank;
       bool present;
       palette_ranks(reinterpret_cast<const uint32_t*>(J.scratch), srank, distinct, present, rank);
       uint32_t* error = reinterpret_cast<uint32_t*>(J.scratch + 32);
-      if (tile == 0) write_fixed_header<kBits>(J.dst, distinct, present, rank, ld_volatile_u32(error) != 0);
+      if (tile == 0) {
+        write_fixed_header<kBits>(J.dst, distinct, present, rank, ld_volatile_u32(error) != 0);
+        if (threadIdx.x == 0) recheck_header(J);
+      }
       skip = distinct > kLimit;
       rank_job = j;
       consumer_sync();
@@ -1080,7 +1123,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
     for (uint64_t i = a + lane; i < e; i += 32) entries[i] = 0;
   };
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
-                                           const EncPos& p, const EncDesc& desc) {
+                                           const EncPos& pos, const EncDesc& desc) {
+    if (pos.late && (tid & 31) == 0) mark_stream_late(J);
     if (j != setup_job) {  // uniform across the consumers
       consumer_sync();     // every warp is done with the previous ranks/table
       uint32_t distinct = 0, rank = 0;
@@ -1102,6 +1146,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
           else if (kind == kAutoFixed6) write_fixed_header<6>(J.dst, distinct, present, rank, false);
           else if (kind == kAutoRaw && tid == 0) J.dst[0] = 6;
           else if (kind == kAutoTop16 && tid == 0) write_top16_header(J.dst, escapes, J.cap, false);
+          if (tid == 0) recheck_header(J);
         }
       }
       if (kind == kAutoTop16) load_top16_table(J.tables, stbl);
@@ -1130,7 +1175,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
 // job), between the kStatsTop16Rec pass and EncodeAutoKernel<., kEncTop16Rec>:
 // every record gets the escapes of the job before its tile and of the tile
 // before each warp's run, and thread 0 writes the stream header (mode 5, or
-// 255 when the escapes exceed the capacity; the count clamped to it).
+// 255 when the escapes exceed the capacity or a wait of the stats pass ran
+// out; the count clamped to the capacity).
 constexpr int kScanThreads = 256;
 constexpr int kScanTilesPerThread = 4;
 
@@ -1146,12 +1192,14 @@ __global__ void __launch_bounds__(kScanThreads) Top16ScanKernel(const __grid_con
   const uint64_t addr = reinterpret_cast<uint64_t>(J.dst);
   constexpr uint32_t kChunk = kScanThreads * kScanTilesPerThread;
   uint32_t carry = 0;
+  bool failed = false;
   for (uint32_t base = 0; base < J.tiles; base += kChunk) {
     // this thread's kScanTilesPerThread consecutive tiles
     uint32_t tot[kScanTilesPerThread];
     uint4 rec[kScanTilesPerThread];
     uint64_t off[kScanTilesPerThread];
     uint32_t mine = 0;
+    bool bad = false;  // a count no warp run can have: a wait of the stats pass ran out
 #pragma unroll
     for (int k = 0; k < kScanTilesPerThread; ++k) {
       const uint32_t t = base + tid * kScanTilesPerThread + k;
@@ -1162,10 +1210,15 @@ __global__ void __launch_bounds__(kScanThreads) Top16ScanKernel(const __grid_con
         off[k] = top16_record_offset(addr, J.n, t);
         if (off[k] != kTailRecord) {
           rec[k] = *reinterpret_cast<const uint4*>(J.dst + off[k]);
+          const uint32_t w[4] = {rec[k].x, rec[k].y, rec[k].z, rec[k].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            bad |= (w[q] & 0xFFFFu) > kStepsPerWarp * kStepWords || (w[q] >> 16) > kStepsPerWarp * kStepWords;
           const uint32_t pairs = (rec[k].x + rec[k].y) + (rec[k].z + rec[k].w);  // two u16 sums, each < 2^16
           tot[k] = (pairs & 0xFFFFu) + (pairs >> 16);
         } else {
           tot[k] = ld_u32_bytes(J.dst + top16_tail_offset(J.n));
+          bad |= tot[k] > kStepsPerWarp * kStepWords;
         }
       }
       mine += tot[k];
@@ -1210,9 +1263,9 @@ __global__ void __launch_bounds__(kScanThreads) Top16ScanKernel(const __grid_con
       before += tot[k];
     }
     carry += chunk;
-    __syncthreads();  // wsum is reused by the next chunk
+    failed |= __syncthreads_or(bad) != 0;  // also: wsum is reused by the next chunk
   }
-  if (tid == 0) write_top16_header(J.dst, carry, J.cap, false);
+  if (tid == 0) write_top16_header(J.dst, carry, J.cap, failed);
 }
 
 // ------------------------------------------------------------ calibration
@@ -1675,29 +1728,22 @@ struct PatchBatch {
 
 template <int kMax, int kMode>
 __global__ void __launch_bounds__(256) EscapePatchKernel(const __grid_constant__ PatchBatch<kMax> b) {
-  const uint64_t first = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // blockIdx.y is the job: every job's entries are patched at once; the
+  // blocks of a job stride over the entries its stream holds
+  const uint32_t j = blockIdx.y;
+  if (j >= b.jobs) return;
+  const DecJob& J = b.job[j];
+  if (job_mode<kMode>(J) != 5) return;
+  const uint64_t count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
+  const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  // the top16 jobs, 32 at a time (lane k reads job base + k's mode byte, all
-  // in flight together); for each, the grid strides over the entries its
-  // stream holds
-  const uint32_t lane = threadIdx.x & 31;
-  for (uint32_t base = 0; base < b.jobs; base += 32) {
-    const uint32_t mine = base + lane;
-    uint32_t jobs = __ballot_sync(kFull, mine < b.jobs && job_mode<kMode>(b.job[mine]) == 5);
-    while (jobs) {
-      const DecJob& J = b.job[base + __ffs(jobs) - 1];
-      jobs &= jobs - 1;
-      const uint64_t count = min(static_cast<uint64_t>(load_u32le(J.src + 1)), J.cap);
-      const uint8_t* entries = J.src + 5 + J.n + (J.n + 1) / 2;
-      for (uint64_t i = first; i < count; i += stride) {
-        const uint32_t q = entry_pos(entries, i);
-        if (q >= J.n) continue;
-        const uint32_t body = __ldg(J.src + 5 + q);
-        const uint32_t w =
-            (body & 0x7Fu) | ((body & 0x80u) << 8) | (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7);
-        J.dst[layout_addr(J.L, q)] = static_cast<uint16_t>(w);
-      }
-    }
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+    const uint32_t q = entry_pos(entries, i);
+    if (q >= J.n) continue;
+    const uint32_t body = __ldg(J.src + 5 + q);
+    const uint32_t w =
+        (body & 0x7Fu) | ((body & 0x80u) << 8) | (static_cast<uint32_t>(__ldg(entries + i * 5 + 4)) << 7);
+    J.dst[layout_addr(J.L, q)] = static_cast<uint16_t>(w);
   }
 }
 

@@ -73,6 +73,8 @@ _SIGNATURES = {
     "kvq_splitzip_bf16_encode_top16_noalloc": [_U64] * 6,
     "kvq_splitzip_top16_tables_from_histograms": [_U64] * 5,
     "kvq_splitzip_device_errors": [],
+    "kvq_splitzip_device_errors_reset": [],
+    "kvq_splitzip_test_encode_mode_skip_arrival": [_U64] * 5 + [ctypes.c_int, _U64],
     "kvq_splitzip_abi_version": [],
 }
 _BATCH_SIGNATURES = {
@@ -543,12 +545,19 @@ def _decode_top16_with(lib, source, out, block_ids, layout, tables):
 
 
 def device_errors() -> int:
-    """Device-side bounded waits that ran out since load (0 normally)."""
+    """Device-side bounded waits that ran out since load or the last
+    device_errors_reset() (0 normally)."""
     lib = _require_lib()
     value = lib.kvq_splitzip_device_errors()
     if value < 0:
         _raise_last(lib, "splitzip device error query failed")
     return int(value)
+
+
+def device_errors_reset() -> None:
+    lib = _require_lib()
+    if lib.kvq_splitzip_device_errors_reset() < 0:
+        _raise_last(lib, "splitzip device error reset failed")
 
 
 # ------------------------------------------------------ decode attention
