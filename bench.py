@@ -126,6 +126,15 @@ class JsonOut:
         os.write(self.fd, (json.dumps(line) + "\n").encode())
 
 
+def host_threads() -> int:
+    """Host threads this process may use (torchrun sets OMP_NUM_THREADS=1 for
+    its ranks; the CPU legs pass their thread count explicitly instead)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def rounded(x, k=3):
     return None if x is None else round(float(x), k)
 
@@ -257,7 +266,11 @@ class Ctx:
         if self.world > 1:
             import datetime
 
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
+            # NCCL's INFO lines (on stderr, see JsonOut) name each
+            # communicator's rank count; a quieter level set by the image is
+            # raised to INFO
+            if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+                os.environ["NCCL_DEBUG"] = "INFO"
             os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.device)
         from unchainkv_b200 import splitzip_cuda as S
@@ -533,7 +546,7 @@ def oracle_parity(ctx, P, sizes, max_jobs=None):
 
             words = P["src"][l][:, P["src_t"][r]].view(torch.int16).cpu().numpy().view(np.uint16)
             ids = np.arange(words.shape[1], dtype=np.int64)
-        expected = oracle.encode_auto_blocks(words, ids, tables[l])
+        expected = oracle.encode_auto_blocks(words, ids, tables[l], threads=host_threads())
         got = host_streams[o:o + len(expected)]
         if sizes[i] != len(expected) or not np.array_equal(got, expected):
             bad = np.flatnonzero(got != expected)[:4].tolist() if got.size == expected.size else "length"
@@ -607,7 +620,7 @@ def codec_run(ctx, cfg, L, min_ms, *, parity_jobs=None, e2e=True, cpu=True, cloc
     enc_gbs = raw_bytes / (ms_enc * 1e-3) / 1e9
     dec_gbs = raw_bytes / (ms_dec * 1e-3) / 1e9
     cpu_line = None
-    if cpu and not args.no_cpu_baseline and ctx.rank == 0:
+    if cpu and not args.no_cpu_baseline and ctx.world == 1:  # rank 0 at N=1 only
         cpu_line = cpu_baseline(cfg, max(1, args.cpu_layers), shard=P["shard"])
     out = {
         "value": round(ctx.world * raw_bytes / (ms_step * 1e-3) / 1e9, 3),
@@ -988,10 +1001,16 @@ def attention_cpu_gbs(cfg, requests: int = 2, repeats: int = 3):
     rng = np.random.Generator(np.random.PCG64(4005))
     q = rng.standard_normal((requests, cfg.kv_heads, cfg.group, cfg.head_dim)).astype(np.float32)
 
+    threads = host_threads()
+    lib = oracle.lib()
+
     def run():
         for r, (ctx, blocks, stream) in enumerate(jobs):
             cache = np.zeros((2, blocks, cfg.block_tokens, cfg.kv_heads, cfg.head_dim), np.uint16)
-            oracle.decode_fixed6_blocks(stream, cache, np.arange(blocks, dtype=np.int64))
+            bw = cfg.block_tokens * cfg.kv_heads * cfg.head_dim
+            ids = np.arange(blocks, dtype=np.int64)
+            lib.orc_decode_fixed6_blocks_mt(stream.ctypes.data, stream.size, cache.ctypes.data, 2 * blocks * bw,
+                                            blocks, bw, blocks * bw, bw, 0, ids.ctypes.data, threads)
             kv = (cache.astype(np.uint32) << 16).view(np.float32).reshape(2, -1, cfg.kv_heads, cfg.head_dim)[:, :ctx]
             s = np.einsum("hgd,thd->hgt", q[r], kv[0]) / np.sqrt(cfg.head_dim)
             s -= s.max(axis=-1, keepdims=True)
@@ -1006,7 +1025,8 @@ def attention_cpu_gbs(cfg, requests: int = 2, repeats: int = 3):
         run()
         times.append(time.perf_counter() - t)
     raw = sum(4 * ctx * cfg.kv_heads * cfg.head_dim for ctx, _, _ in jobs)
-    return raw / statistics.median(times) / 1e9, oracle.max_threads(), f"first {requests} of {cfg.requests} requests"
+    return (raw / statistics.median(times) / 1e9, threads,
+            f"first {requests} of {cfg.requests} requests (oracle decode on {threads} threads, numpy attention)")
 
 
 def attention_run(ctx, codec, min_ms, e2e=True, cpu=True, clocks=True):
@@ -1059,7 +1079,7 @@ def attention_run(ctx, codec, min_ms, e2e=True, cpu=True, clocks=True):
                     "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
                     "ms_per_step": round(e2e_ms, 4), "path": "pinned q -> attention_decode -> pinned out"}
     cpu_line = None
-    if cpu and not args.no_cpu_baseline and ctx.rank == 0:
+    if cpu and not args.no_cpu_baseline and ctx.world == 1:
         gbs, threads, sample = attention_cpu_gbs(cfg)
         cpu_line = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                     "sample": sample + ", oracle fixed6 decode then numpy fp32 attention", "cpu": cpu_model()}
@@ -1315,7 +1335,7 @@ def cpu_pipeline_gbs(cfg, layers: int, repeats: int = 3, shard: int = 0):
     from unchainkv_b200 import workloads
 
     lib = oracle.lib()
-    threads = oracle.max_threads()
+    threads = host_threads()
     jobs = cpu_jobs(cfg, layers, shard)
     bw = cfg.block_words
     largest = max(2 * len(ids) * bw for _, ids, _, _ in jobs)
