@@ -459,40 +459,65 @@ __device__ __forceinline__ void warp_store_run(uint8_t* g, const uint32_t (&D)[K
 
 // ---------------------------------------------------------------- staging
 
-// Stage words [t0, t0+len) of a bulk-capable layout (base 16-byte aligned,
-// every run a multiple of 8 words at an 8-word aligned offset) into shared
-// memory, sin[j] = word t0+j, with the 32 lanes of one warp: lane k copies
-// the k-th contiguous run of the tile (k, k+32, ... for layouts with more
-// runs), so the block-table loads of all runs are in flight together.  Each
-// lane registers its own bytes on `bar`; a ragged flat tail of < 8 words
-// goes by lane 0's plain loads.  Does not arrive on `bar`.
-__device__ __forceinline__ void stage_words_tma(const uint16_t* __restrict__ base, const Layout& L, uint64_t t0,
-                                                uint32_t len, uint16_t* sin, uint64_t* bar) {
-  const uint32_t lane = threadIdx.x & 31;
-  if (L.block_words == 0) {  // flat: one run
-    const uint32_t aligned_len = len & ~7u;
-    if (lane == 0) {
-      if (aligned_len) {
-        mbar_expect_tx(bar, aligned_len * 2);
-        bulk_g2s(sin, base + t0, aligned_len * 2, bar);
-      }
-      for (uint32_t j = aligned_len; j < len; ++j) sin[j] = base[t0 + j];
+// Lane k's run of a tile for TMA staging (runs are the intersections of the
+// tile with cache blocks; the flat layout has one, staged by lane 0): its
+// first word, global source and bytes (0: none).  The block-table load
+// happens here, so a producer can plan the next tile while the current one
+// is staged and waited for.
+struct RunPlan {
+  uint64_t s0;
+  const uint16_t* src;
+  uint32_t bytes;
+};
+
+__device__ __forceinline__ RunPlan plan_run(const uint16_t* __restrict__ base, const Layout& L, uint64_t t0,
+                                            uint32_t len, uint32_t k) {
+  RunPlan r{0, nullptr, 0};
+  if (L.block_words == 0) {
+    if (k == 0) {
+      r.s0 = t0;
+      r.src = base + t0;
+      r.bytes = (len & ~7u) * 2;
     }
+    return r;
+  }
+  const uint64_t bw = L.block_words;
+  const uint64_t first = L.bw_shift >= 0 ? t0 >> L.bw_shift : t0 / bw;  // no 64-bit division for 2^k blocks
+  const uint64_t b0 = (first + k) * bw;
+  const uint64_t s0 = b0 > t0 ? b0 : t0;
+  const uint64_t end = t0 + len;
+  if (s0 >= end) return r;
+  const uint64_t e0 = b0 + bw < end ? b0 + bw : end;
+  r.s0 = s0;
+  r.src = base + layout_addr(L, s0);
+  r.bytes = static_cast<uint32_t>((e0 - s0) * 2);
+  return r;
+}
+
+// Stage a tile by TMA given each lane's planned run (plan_run(.., lane)):
+// one bulk copy per contiguous run, registered on `bar` (no arrive); the
+// flat layout's last < 8 words go by plain loads of lane 0.  Runs past the
+// 32nd (blocks shorter than 256 words) are planned and issued here.
+__device__ __forceinline__ void issue_runs(const RunPlan& r, const uint16_t* __restrict__ base, const Layout& L,
+                                           uint64_t t0, uint32_t len, uint16_t* sin, uint64_t* bar) {
+  const uint32_t lane = threadIdx.x & 31;
+  if (r.bytes) {
+    mbar_expect_tx(bar, r.bytes);
+    bulk_g2s(sin + (r.s0 - t0), r.src, r.bytes, bar);
+  }
+  if (L.block_words == 0) {
+    if (lane == 0)
+      for (uint32_t j = len & ~7u; j < len; ++j) sin[j] = base[t0 + j];
     return;
   }
-  // runs are the intersections of the tile with cache blocks (the plane
-  // boundary is a block boundary)
-  const uint64_t bw = L.block_words;
-  const uint64_t first_block = t0 / bw;
-  const uint64_t end = t0 + len;
-  for (uint64_t k = lane;; k += 32) {
-    const uint64_t b0 = (first_block + k) * bw;
-    const uint64_t s0 = b0 > t0 ? b0 : t0;
-    if (s0 >= end) break;
-    const uint64_t e0 = b0 + bw < end ? b0 + bw : end;
-    const uint32_t bytes = static_cast<uint32_t>((e0 - s0) * 2);
-    mbar_expect_tx(bar, bytes);
-    bulk_g2s(sin + (s0 - t0), base + layout_addr(L, s0), bytes, bar);
+  // a tile meets at most ceil(8192 / bw) + 1 blocks: 32 or fewer (one per
+  // lane, planned above) once bw >= 265 words
+  if (L.block_words >= 265) return;
+  for (uint32_t k = lane + 32;; k += 32) {
+    const RunPlan x = plan_run(base, L, t0, len, k);
+    if (x.bytes == 0) break;
+    mbar_expect_tx(bar, x.bytes);
+    bulk_g2s(sin + (x.s0 - t0), x.src, x.bytes, bar);
   }
 }
 

@@ -331,56 +331,79 @@ struct NoAux {
   __device__ __forceinline__ void operator()(const Job&, uint32_t, EncDesc&) const {}
 };
 
-// Producer warp of the encode kernels: stages the tiles next_tile() yields
-// (increasing; >= total ends) into the ring.  A bulk-capable layout takes one
-// TMA copy per contiguous run, the runs spread over the 32 lanes; any other
-// is gathered word by word by the 32 lanes.
-template <int kMax, uint32_t kTries = kBarrierTries, bool kSkipTest = false, typename Next, typename Aux = NoAux>
+// Producer warp of the encode kernels: stages the tiles [first, last) of
+// this CTA's chunk into the ring, in order.  The tiles are planned 32 at a
+// time, one per lane (job, bounds and -- when the tile is one contiguous run
+// of a bulk-capable job -- its TMA source, block-table load included), so a
+// tile costs the producer a few shuffles and one copy issued by lane 0.
+// Tiles of several runs (blocks shorter than a tile) take one copy per run
+// over the 32 lanes, and other layouts are gathered word by word.
+template <int kMax, uint32_t kTries = kBarrierTries, bool kSkipTest = false, typename Aux = NoAux>
 __device__ __forceinline__ void encode_producer(const EncBatch<kMax>& b, uint8_t* ring, EncRing& R, EncDesc* D,
-                                                Next&& next_tile, Aux aux = Aux()) {
+                                                uint32_t first, uint32_t last, Aux aux = Aux()) {
   const int lane = threadIdx.x & 31;
-  const uint32_t total = b.tile_start[b.jobs];
   EncPos p;
-  int ji = 0;
-  for (;;) {
-    const bool late = producer_acquire<kEncStages, kTries>(R, p, nullptr);
-    const uint32_t t = next_tile();
-    if (t >= total) {
-      if (lane == 0) D[p.s].tile = kEndTile;
-      producer_commit(R, p);
-      return;
+  int ji = find_job<kMax>(b.tile_start, b.jobs, first);  // job of the group's first tile
+  for (uint32_t g = first; g < last; g += 32) {
+    // ---- plan tile g + lane
+    const uint32_t mine = g + lane;
+    int pj = ji;
+    uint64_t pt0 = 0;
+    uint32_t plen = 0;
+    const uint16_t* psrc = nullptr;  // non-null: a single-run tile, staged from here
+    if (mine < last) {
+      pj = advance_job<kMax>(b.tile_start, ji, mine);
+      const EncJob& J = b.job[pj];
+      pt0 = static_cast<uint64_t>(mine - b.tile_start[pj]) * kTileWords;
+      plen = tile_len(J.n, pt0);
+      if (J.bulk != 0 && (J.L.block_words == 0 || J.L.block_words % kTileWords == 0))
+        psrc = J.src + layout_addr(J.L, pt0);
     }
-    ji = advance_job<kMax>(b.tile_start, ji, t);
-    const EncJob& J = b.job[ji];
-    const uint64_t t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
-    const uint32_t len = tile_len(J.n, t0);
-    uint16_t* sin = reinterpret_cast<uint16_t*>(ring + p.s * kEncStageBytes);
-    if (lane == 0) {
-      D[p.s].tile = t;
-      D[p.s].job = static_cast<uint32_t>(ji);
-      D[p.s].late = late;
+    const uint32_t count = min(32u, last - g);
+    for (uint32_t k = 0; k < count; ++k) {
+      const uint32_t t = g + k;
+      const int tj = __shfl_sync(kFull, pj, k);
+      const uint64_t t0 = __shfl_sync(kFull, pt0, k);
+      const uint32_t len = __shfl_sync(kFull, plen, k);
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(
+          __shfl_sync(kFull, reinterpret_cast<unsigned long long>(psrc), k));
+      const bool late = producer_acquire<kEncStages, kTries>(R, p, nullptr);
+      const EncJob& J = b.job[tj];
+      uint16_t* sin = reinterpret_cast<uint16_t*>(ring + p.s * kEncStageBytes);
+      if (lane == 0) {
+        D[p.s].tile = t;
+        D[p.s].job = static_cast<uint32_t>(tj);
+        D[p.s].late = late;
+      }
+      if (src != nullptr) {
+        if (lane == 0) {
+          const uint32_t whole = len & ~7u;  // the flat layout's last < 8 words go by plain loads
+          if (whole) {
+            mbar_expect_tx(&R.full[p.s], whole * 2);
+            bulk_g2s(sin, src, whole * 2, &R.full[p.s]);
+          }
+          for (uint32_t j = whole; j < len; ++j) sin[j] = src[j];
+        }
+      } else if (J.bulk != 0) {
+        issue_runs(plan_run(J.src, J.L, t0, len, lane), J.src, J.L, t0, len, sin, &R.full[p.s]);
+      } else {
+        gather_words_warp(J.src, J.L, t0, len, sin);
+      }
+      aux(J, t - b.tile_start[tj], D[p.s]);
+      if (kSkipTest && t == b.skip_tile && lane == 31) {
+        // test-only: this stage's full barrier stays one arrival short, so the
+        // consumers' bounded wait for it runs out
+      } else {
+        producer_commit(R, p);
+      }
+      p.next();
     }
-    if (J.bulk != 0) {
-      stage_words_tma(J.src, J.L, t0, len, sin, &R.full[p.s]);
-    } else {
-      gather_words_warp(J.src, J.L, t0, len, sin);
-    }
-    aux(J, t - b.tile_start[ji], D[p.s]);
-    if (kSkipTest && t == b.skip_tile && lane == 31) {
-      // test-only: this stage's full barrier stays one arrival short, so the
-      // consumers' bounded wait for it runs out
-    } else {
-      producer_commit(R, p);
-    }
-    p.next();
+    ji = __shfl_sync(kFull, pj, count - 1);
   }
+  producer_acquire<kEncStages, kTries>(R, p, nullptr);
+  if (lane == 0) D[p.s].tile = kEndTile;
+  producer_commit(R, p);
 }
-
-// Tiles of this CTA's contiguous chunk, for encode_producer (warp-uniform).
-struct ChunkTiles {
-  uint32_t next, last;
-  __device__ __forceinline__ uint32_t operator()() { return next < last ? next++ : kEndTile; }
-};
 
 // Consumer warps of the encode kernels: fn(job, job_index, tile, words,
 // ring position, descriptor) for every staged tile until the end descriptor.
@@ -410,7 +433,7 @@ __device__ __forceinline__ void encode_pipeline(const EncBatch<kMax>& b, uint8_t
                                                 Fn&& fn, Aux aux = Aux()) {
   if ((threadIdx.x >> 5) == kProducerWarp) {
     const Chunk c = cta_chunk(b.tile_start[b.jobs]);
-    encode_producer<kMax, kTries, kSkipTest>(b, ring, R, D, ChunkTiles{c.first, c.last}, aux);
+    encode_producer<kMax, kTries, kSkipTest>(b, ring, R, D, c.first, c.last, aux);
     return;
   }
   encode_consumer<kMax, kTries>(b, ring, R, D, fn);
@@ -623,6 +646,7 @@ __device__ __forceinline__ void write_top16_header(uint8_t* dst, uint64_t total,
 // the first `cap` escapes, so every tile's offset must be exact.
 __device__ __forceinline__ uint32_t presence_index(uint32_t h) { return h ^ ((h >> 5) & 4u); }
 template <uint32_t kOff> struct StatsPlane { static constexpr uint32_t kOffset = kOff; };
+template <bool kB> struct CompileFlag { static constexpr bool kValue = kB; };
 
 // Sign-and-exponent index (the word's bits 7..15) with the sign copied into
 // bank bit 4 (byte bit 6), for the 512-entry stats tables.
@@ -666,14 +690,21 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
   // aux = 1 when the job's escapes already exceed its top16 capacity
   // (the total only grows, so a job once seen over stays over: the producer
   // remembers it and skips the global load for its remaining tiles)
+  // The total is read one tile ahead (the load's latency overlaps the next
+  // tile's staging): a job is seen over its capacity a tile later, which
+  // only means one more tile counted.
   const EncJob* over_job = nullptr;  // producer warp: the job last seen over its capacity
-  auto over_cap = [&over_job](const EncJob& J, uint32_t, EncDesc& d) {
+  const EncJob* seen_job = nullptr;  // the job whose total was read last
+  uint32_t seen_total = 0;
+  auto over_cap = [&](const EncJob& J, uint32_t, EncDesc& d) {
     bool over = false;
     if (kKind == kStatsAuto) {
-      over = &J == over_job;
-      if (!over && ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch)) > J.cap) {
-        over = true;
+      over = &J == over_job || (&J == seen_job && seen_total > J.cap);
+      if (over) {
         over_job = &J;
+      } else {
+        seen_total = ld_volatile_u32(reinterpret_cast<const uint32_t*>(J.scratch));
+        seen_job = &J;
       }
     }
     if ((threadIdx.x & 31) == 0) d.aux = over;
@@ -702,8 +733,9 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     if (len == kTileWords && (t0 >= J.half || t0 + kTileWords <= J.half)) {
       // whole tile in one plane: no bounds, and the plane's escape table is a
       // constant offset (one copy of the loop per plane)
-      auto scan = [&](auto plane) {
+      auto scan = [&](auto plane, auto counting) {
         constexpr uint32_t kOff = decltype(plane)::kOffset;
+        constexpr bool kCountHere = decltype(counting)::kValue;
 #pragma unroll
         for (int s = 0; s < kStepsPerWarp; ++s) {
           const uint16_t* w = sin + (warp * kStepsPerWarp + s) * kStepWords + 8 * lane;
@@ -727,15 +759,19 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
                 spres[e] = 1;
                 spres[o] = 1;
               }
-              if (count) escapes += sesc[kOff + e] + sesc[kOff + o];
+              if (kCountHere) escapes += sesc[kOff + e] + sesc[kOff + o];
             }
           }
         }
       };
-      if (!kStats || t0 < J.half)
-        scan(StatsPlane<0>{});
+      // one copy of the loop per plane and per counting choice: a tile that
+      // does not count issues no escape-table loads at all
+      if (!count)
+        scan(StatsPlane<0>{}, CompileFlag<false>{});
+      else if (t0 < J.half)
+        scan(StatsPlane<0>{}, CompileFlag<true>{});
       else
-        scan(StatsPlane<512>{});
+        scan(StatsPlane<512>{}, CompileFlag<true>{});
     } else {
 #pragma unroll
       for (int s = 0; s < kStepsPerWarp; ++s) {
@@ -1496,7 +1532,10 @@ __device__ __forceinline__ uint32_t job_mode(const DecJob& J) {
   return (need == 0 || need > J.src_bytes) ? 0 : mode;
 }
 
-// Producer warp of DecodeKernel.
+// Producer warp of DecodeKernel.  The next tile is planned (job, mode byte
+// once per job, the block-table loads of its steps' destinations) before
+// the current one waits for its stage, so those loads' latency overlaps the
+// staging instead of sitting between two tiles' copies.
 template <int kMax, int kMode>
 __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t* ring, DecRing& R, DecDesc* D) {
   const int lane = threadIdx.x & 31;
@@ -1505,42 +1544,59 @@ __device__ __forceinline__ void decode_producer(const DecBatch<kMax>& b, uint8_t
   int ji = find_job<kMax>(b.tile_start, b.jobs, c.first);
   int mode_job = -1;
   uint32_t mode = 0;
-  for (uint32_t t = c.first;; ++t) {
-    producer_acquire(R, p, nullptr);
-    DecDesc& d = D[p.s];
-    if (t >= c.last) {
-      if (lane == 0) d.tile = kEndTile;
-      producer_commit(R, p);
-      return;
-    }
+  struct Planned {
+    uint32_t t;
+    int ji;
+    uint32_t mode;
+    uint32_t len;
+    uint64_t t0;
+    uint16_t* q;  // this lane's step destination (lanes < kStepsPerTile)
+  };
+  auto plan = [&](uint32_t t) {
+    Planned x{t, ji, 0, 0, 0, nullptr};
+    if (t >= c.last) return x;
     ji = advance_job<kMax>(b.tile_start, ji, t);
     const DecJob& N = b.job[ji];
     if (ji != mode_job) {
       mode = job_mode<kMode>(N);
       mode_job = ji;
     }
-    const uint64_t t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
-    const uint32_t len = tile_len(N.n, t0);
+    x.ji = ji;
+    x.mode = mode;
+    x.t0 = static_cast<uint64_t>(t - b.tile_start[ji]) * kTileWords;
+    x.len = tile_len(N.n, x.t0);
+    if (lane < static_cast<int>(kStepsPerTile)) {
+      const uint32_t sb = lane * kStepWords;
+      if (mode != 0 && N.vec != 0 && sb + kStepWords <= x.len) {
+        const uint64_t g = x.t0 + sb;
+        if (layout_run(N.L, g) >= kStepWords) x.q = N.dst + layout_addr(N.L, g);
+      }
+    }
+    return x;
+  };
+  Planned cur = plan(c.first);
+  for (;;) {
+    const Planned nxt = cur.t < c.last ? plan(cur.t + 1) : cur;
+    producer_acquire(R, p, nullptr);
+    DecDesc& d = D[p.s];
+    if (cur.t >= c.last) {
+      if (lane == 0) d.tile = kEndTile;
+      producer_commit(R, p);
+      return;
+    }
     if (lane == 0) {
-      const uint2 pad = decode_stage(N, mode, t0, len, ring + p.s * kDecStageBytes, &R.full[p.s]);
-      d.tile = t;
-      d.job = static_cast<uint32_t>(ji);
-      d.mode = mode;
+      const uint2 pad = decode_stage(b.job[cur.ji], cur.mode, cur.t0, cur.len, ring + p.s * kDecStageBytes,
+                                     &R.full[p.s]);
+      d.tile = cur.t;
+      d.job = static_cast<uint32_t>(cur.ji);
+      d.mode = cur.mode;
       d.pad_x = pad.x;
       d.pad_y = pad.y;
     }
-    // destination of each 512-word step
-    uint16_t* q = nullptr;
-    if (lane < static_cast<int>(kStepsPerTile)) {
-      const uint32_t sb = lane * kStepWords;
-      if (mode != 0 && N.vec != 0 && sb + kStepWords <= len) {
-        const uint64_t g = t0 + sb;
-        if (layout_run(N.L, g) >= kStepWords) q = N.dst + layout_addr(N.L, g);
-      }
-    }
-    if (lane < static_cast<int>(kStepsPerTile)) d.step_dst[lane] = q;
+    if (lane < static_cast<int>(kStepsPerTile)) d.step_dst[lane] = cur.q;
     producer_commit(R, p);
     p.next();
+    cur = nxt;
   }
 }
 
