@@ -845,7 +845,7 @@ def top16_run(ctx, min_ms, L=None):
         prof_steps = max(1, min(args.steps, 50))
         prof = ctx.profile(lambda: (fns[e](), fns[d]()), prof_steps)
         alg = {"Top16StatsKernel": raw, "EncodeTop16Kernel": raw + size * L,
-               "Top16ScanKernel": 52 * L * ((n + 8191) // 8192),  # 32-byte records read, 20 bytes written
+               "Top16ScanKernel": 52 * L * ((n + S.TILE_WORDS - 1) // S.TILE_WORDS),  # 32-byte records read, 20 bytes written
                "StatsKernel": raw, "EncodeAutoKernel": raw + size * L,
                "DecodeTop16Kernel": size * L + raw, "DecodeAutoKernel": size * L + raw,
                "EscapePatchKernel": 8 * L * (n // 200)}

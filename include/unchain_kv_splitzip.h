@@ -80,10 +80,11 @@ KVQ_API long long kvq_splitzip_bf16_decode_fixed6(
  * top16 encode of `count` contiguous words with a 544-byte table
  * ([0,256) K exponent->code, [256,512) V, [512,528) K books, [528,544) V
  * books; code 255 = escape).  Escape entries are written in ascending
- * position order.  Scratch after the stream: the reference's 8 bytes plus
- * 16 + 8*ceil(count/8192) bytes at the next 16-byte aligned address
- * (a 2*count-byte buffer, as the reference's callers use, always fits;
- * the groups add 8*ceil(tiles/32) bytes). */
+ * position order.  Needs capacity >= align4(encoded) + 8, the reference's
+ * rule (kvq_splitzip_cuda.cu:390-394), and declines (0) below it: the
+ * statistics pass keeps each tile's escape counts inside the stream's own
+ * body region until the encode overwrites them, and a last tile of fewer
+ * than 47 words keeps its count in the 8 bytes past align4(encoded). */
 KVQ_API long long kvq_splitzip_bf16_encode_top16(unsigned long long src_ptr,
                                                  unsigned long long dst_ptr,
                                                  unsigned long long count,
@@ -184,7 +185,7 @@ KVQ_API long long kvq_splitzip_bf16_decode_fixed6_batch(const kvq_splitzip_job* 
  * align16(2n+1) + scratch, else a fixed6 overflow stream (mode 255) for the
  * host to replace with raw.  The stream's length follows from byte 0
  * (5: 5+n+ceil(n/2)+5*ceil(n/200); 3: 65+n+3*ceil(n/4); 6: 2n+1).
- * Scratch: 64 + align16(8*ceil(tiles/32)) + 16*tiles bytes (tiles = ceil(n/8192)) at
+ * Scratch: 64 + align16(8*ceil(tiles/32)) + 16*tiles bytes (tiles = ceil(n/16384)) at
  * the 16-byte aligned end of the largest form.  Returns the sum over jobs of
  * the largest form each job may produce. */
 KVQ_API long long kvq_splitzip_bf16_encode_auto_batch(const kvq_splitzip_job* jobs,
@@ -293,7 +294,7 @@ KVQ_API long long kvq_splitzip_device_errors_reset(void);
 /* Test hook of the bounded waits (no counterpart in the reference): the
  * encode of kvq_splitzip_bf16_encode_mode with its statistics pass built
  * with a limit of 4 tries per wait and its producer leaving the full barrier
- * of tile `skip_tile` (8192-word tiles) one arrival short.  That wait runs
+ * of tile `skip_tile` (16384-word tiles) one arrival short.  That wait runs
  * out: the count above grows, the stream gets a mode-255 header, the call
  * returns like kvq_splitzip_bf16_encode_mode.  Nothing faults or waits
  * without a limit. */
@@ -314,7 +315,7 @@ KVQ_API long long kvq_splitzip_abi_version(void);
  * all of HBM to their paged KV pool (a transient allocation can fail there)
  * and paths that must not call cudaMalloc / cudaFree (those can synchronise
  * the device).  The escape counts of its statistics pass live in a
- * 266,304-byte static device array of this library, held by every GPU that
+ * 133,184-byte static device array of this library, held by every GPU that
  * loads it until exit, so it writes no byte of the caller's buffer past the
  * stream.  count above 2^27 words (134,217,728) returns -1 with a message in
  * kvq_splitzip_last_error().  The first call on a device looks up the

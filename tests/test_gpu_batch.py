@@ -57,8 +57,10 @@ def job_for(kv, ids_t, buf, tables_t, stream_bytes=None):
 
 def test_top16_and_fixed6_batches_match_single_calls():
     rng = np.random.Generator(np.random.PCG64(1))
+    # blocks of 400 and 512 words: a tile meets more than 32 blocks, so the
+    # producer issues its copies in several rounds of 32 runs
     specs = [(40, (16, 8, 128), 0, 0.003), (300, (16, 1, 128), 5, 0.0045), (30, (7, 3), 9, 0.002),
-             (64, (16, 8, 128), 31, 0.0)]
+             (64, (16, 8, 128), 31, 0.0), (160, (4, 1, 100), 11, 0.003), (120, (16, 2, 16), 13, 0.004)]
     cases, jobs, bufs, keep = [], [], [], []
     for pool, shape, layer, rate in specs:
         cache, ids, tab = make_case(rng, pool, shape, layer, rate)

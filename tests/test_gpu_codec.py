@@ -70,7 +70,7 @@ def gpu_encode_top16(words: np.ndarray, tables: np.ndarray, capacity=None):
 
 # ---------------------------------------------------------------- top16 encode
 
-@pytest.mark.parametrize("n", [22, 256, 1000, 1001, 8192, 8195, 3 * 8192 + 100, 1 << 20])
+@pytest.mark.parametrize("n", [22, 256, 1000, 1001, 8192, 8195, 3 * 8192 + 100, 16384, 16384 + 3, 3 * 16384 + 100, 1 << 20])
 @pytest.mark.parametrize("rate", [0.0, 0.002, 0.0049, 0.03])
 def test_top16_encode_flat_matches_oracle(n, rate):
     rng = np.random.Generator(np.random.PCG64(n * 7 + int(rate * 1e4)))
@@ -97,7 +97,8 @@ def test_top16_encode_declines_like_reference():
     assert gpu_encode_top16(words, tables, capacity=enc + 4)[0] == 0
 
 
-@pytest.mark.parametrize("n", [22, 47, 1000, 8192, 8192 + 30, 8192 + 47, 8192 + 63, 5 * 8192 + 4096, 1 << 20])
+@pytest.mark.parametrize("n", [22, 47, 1000, 8192, 8192 + 30, 8192 + 47, 8192 + 63, 5 * 8192 + 4096, 16384 + 30,
+                               16384 + 47, 16384 + 63, 3 * 16384 + 8192, 1 << 20])
 @pytest.mark.parametrize("rate", [0.002, 0.0049, 0.03])
 @pytest.mark.parametrize("shift", [0, 3, 11])
 def test_top16_encode_at_the_reference_capacity(n, rate, shift):

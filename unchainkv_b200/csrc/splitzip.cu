@@ -1277,12 +1277,12 @@ extern "C" KVQ_API long long kvq_splitzip_profile_launches(int i) {
 namespace {
 
 // Largest `count` the static scratch covers: 2^27 words (256 MiB of raw bf16,
-// 16384 tiles); the array holds the escape total and error flag, 512 group
-// sums and a u16 count per (tile, warp): 64 + 8*512 + 16*16384 = 266304 bytes.
+// 8192 tiles); the array holds the escape total and error flag, 256 group
+// sums and a u16 count per (tile, warp): 64 + 8*256 + 16*8192 = 133184 bytes.
 constexpr uint64_t kNoAllocMaxWords = 1ull << 27;
 constexpr uint64_t kNoAllocTiles = (kNoAllocMaxWords + kTileWords - 1) / kTileWords;
 constexpr uint64_t kNoAllocScratchBytes = auto_scratch_bytes(kNoAllocTiles);
-static_assert(kNoAllocScratchBytes == 266304, "the documented size of the no-alloc scratch");
+static_assert(kNoAllocScratchBytes == 133184, "the documented size of the no-alloc scratch");
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 

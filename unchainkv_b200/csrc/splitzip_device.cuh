@@ -19,8 +19,8 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnitWords = 16;                        // words per lane per step
 constexpr int kStepWords = 32 * kUnitWords;           // 512 words per warp step
-constexpr int kStepsPerWarp = 2;
-constexpr int kTileWords = kWarps * kStepsPerWarp * kStepWords;  // 8192
+constexpr int kStepsPerWarp = 4;
+constexpr int kTileWords = kWarps * kStepsPerWarp * kStepWords;  // 16384 (32 KiB of words)
 constexpr unsigned kFull = 0xffffffffu;
 
 // ---------------------------------------------------------------- layouts
@@ -510,9 +510,9 @@ __device__ __forceinline__ void issue_runs(const RunPlan& r, const uint16_t* __r
       for (uint32_t j = len & ~7u; j < len; ++j) sin[j] = base[t0 + j];
     return;
   }
-  // a tile meets at most ceil(8192 / bw) + 1 blocks: 32 or fewer (one per
-  // lane, planned above) once bw >= 265 words
-  if (L.block_words >= 265) return;
+  // a tile meets at most ceil(kTileWords / bw) + 1 blocks: 32 or fewer (one
+  // per lane, planned above) once 31 bw >= kTileWords
+  if (L.block_words * 31 >= kTileWords) return;
   for (uint32_t k = lane + 32;; k += 32) {
     const RunPlan x = plan_run(base, L, t0, len, k);
     if (x.bytes == 0) break;

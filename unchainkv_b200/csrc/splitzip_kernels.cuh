@@ -2,14 +2,14 @@
 //
 // Every kernel takes a batch of jobs as a __grid_constant__ parameter (one
 // job = one reference ABI call: one layer of one request).  The work is the
-// 8192-word tiles of all jobs.  Kernels are persistent: the grid is sized to
-// the resident CTAs, each CTA walks a contiguous chunk of tiles, and a
-// 3-stage ring of shared-memory buffers filled by TMA bulk copies keeps the
-// next two tiles in flight while the current one is coded.  Only the top16
+// 16384-word tiles of all jobs.  Kernels are persistent: the grid is sized
+// to the resident CTAs, each CTA walks a contiguous chunk of tiles, and a
+// ring of 2 (encode) or 3 (decode) shared-memory stages filled by TMA bulk
+// copies keeps the next tiles in flight while the current one is coded.  Only the top16
 // encoder, whose escape offsets chain tile to tile, takes tiles by atomic
 // ticket instead (so every tile it waits for is held by a running CTA).
 //
-// Per tile: one CTA of 256 threads = 8 warps x 2 steps x 32 lanes x 16 words.
+// Per tile: one CTA of 256 threads = 8 warps x 4 steps x 32 lanes x 16 words.
 //   encode: 16 words per lane in registers -> body/low plane by byte_perm,
 //     codes by one shared-memory lookup per word -> warp funnel stores into
 //     the unaligned stream regions (aligned 8/4/2-byte stores);
@@ -25,9 +25,9 @@
 namespace ukv {
 
 constexpr int kMaxBatch = 96;
-constexpr int kEncStages = 4;  // ring depth of the encode kernels (16 KiB stages)
-constexpr int kDecStages = 3;  // ring depth of the decode kernel (16.1 KiB stages + descriptors)
-constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 16 KiB of words
+constexpr int kEncStages = 2;  // ring depth of the encode kernels (32 KiB stages, 3 CTAs per SM)
+constexpr int kDecStages = 3;  // ring depth of the decode kernel (32.1 KiB stages, 2 CTAs per SM)
+constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 32 KiB of words
 constexpr uint32_t kDecStageBytes = 2 * kTileWords + 128;
 constexpr uint32_t kDecCodesOffset = kTileWords + 128;  // top16/fixed6 codes inside a stage
 constexpr uint32_t kEncSmemBytes = kEncStages * kEncStageBytes;
@@ -794,8 +794,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
     if (kKind == kStatsTop16Rec) {
       // every warp writes its count (the record is not cleared beforehand);
       // after a wait that ran out it writes a count no run can have (a run
-      // holds at most 1024 words), which the scan turns into a mode-255
-      // header
+      // holds at most kStepsPerWarp * kStepWords = 2048 words), which the
+      // scan turns into a mode-255 header
       escapes = warp_sum(escapes);
       if (lane == 0) {
         const uint64_t off = top16_record_offset(reinterpret_cast<uint64_t>(J.dst), J.n, tile);
@@ -1431,6 +1431,7 @@ __global__ void __launch_bounds__(256) Top16TablesKernel(const uint32_t* __restr
 // 16-byte stores per lane at the resolved step address.
 
 constexpr uint32_t kStepsPerTile = kTileWords / kStepWords;
+static_assert(kStepsPerTile <= 32, "the producer's lanes resolve one step each");
 
 // Decode stage descriptor, written by the producer warp.
 struct DecDesc {

@@ -680,6 +680,11 @@ def stream_length(header: bytes, n: int) -> int | None:
     return None
 
 
+# Words per tile of the library's kernels (kTileWords): the auto encode's
+# statistics scratch holds a 16-byte record of escape counts per tile.
+TILE_WORDS = 16384
+
+
 def torchop_capacity(n: int) -> int:
     """Stream-buffer bytes for encode_torchop_batch: raw mode 6 (the largest
     form) plus the job's 416-byte plan."""
@@ -697,7 +702,7 @@ def top16_capacity(n: int) -> int:
 def auto_capacity(n: int, raw: bool = True) -> int:
     """Stream-buffer bytes for encode_auto_batch: room for the largest form
     (raw mode 6 when ``raw``) plus the statistics scratch."""
-    tiles = (n + 8191) // 8192
+    tiles = (n + TILE_WORDS - 1) // TILE_WORDS
     scratch = 64 + (8 * ((tiles + 31) // 32) + 15) // 16 * 16 + 16 * tiles
     largest = 1 + 2 * n if raw else max(top16_stream_bytes(n), fixed6_stream_bytes(n))
     return ((largest + 15) // 16) * 16 + scratch + 16
