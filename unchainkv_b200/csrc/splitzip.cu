@@ -113,6 +113,26 @@ struct GeometryKey {
 std::mutex g_geometry_mu;
 std::map<GeometryKey, int> g_geometry;  // resident CTAs per device
 
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while the previous kernel of the stream finishes; it waits for that
+// kernel (grid_dependency_wait) before touching global memory.  Only
+// kernels that call grid_dependency_sync() first go through here.
+template <typename Kernel, typename... Args>
+cudaError_t launch_dependent(Kernel kernel, dim3 grid, dim3 block, size_t dyn_smem, cudaStream_t stream,
+                             const Args&... args) {
+  cudaLaunchConfig_t config{};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = dyn_smem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, args...);
+}
+
 template <typename Kernel>
 long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* grid, int threads = kCtaThreads) {
   int device = 0;
@@ -320,9 +340,10 @@ long long launch_zero(const std::vector<Prepared>& jobs, size_t first, size_t co
   const unsigned bx =
       static_cast<unsigned>(std::min<uint64_t>(64, (largest / 16 + kThreads - 1) / kThreads + 1));
   const long long prof = prof_begin(stream);
-  ZeroKernel<kMax><<<dim3(bx, static_cast<unsigned>(count)), kThreads, 0, stream>>>(z);
+  cudaError_t st = launch_dependent(ZeroKernel<kMax>, dim3(bx, static_cast<unsigned>(count)), dim3(kThreads), 0,
+                                    stream, z);
   prof_end(prof, "ZeroKernel", stream);
-  const cudaError_t st = cudaGetLastError();
+  if (st == cudaSuccess) st = cudaGetLastError();
   return st == cudaSuccess ? 0 : Fail("ZeroKernel", st);
 }
 
@@ -334,9 +355,9 @@ long long launch_persistent(Kernel kernel, const char* name, size_t dyn_smem, co
   const long long rc = grid_for(kernel, dyn_smem, tiles, &grid);
   if (rc < 0) return rc;
   const long long prof = prof_begin(stream);
-  kernel<<<grid, kCtaThreads, dyn_smem, stream>>>(b);
+  cudaError_t st = launch_dependent(kernel, dim3(grid), dim3(kCtaThreads), dyn_smem, stream, b);
   prof_end(prof, name, stream);
-  const cudaError_t st = cudaGetLastError();
+  if (st == cudaSuccess) st = cudaGetLastError();
   return st == cudaSuccess ? 0 : Fail(name, st);
 }
 
@@ -350,9 +371,9 @@ long long launch_encode_kernels(EncOp op, const EncBatch<kMax>& b, uint32_t tile
           launch_persistent(PresenceKernel<kMax, kStatsTop16Rec>, "Top16StatsKernel", kEncSmemBytes, b, tiles, stream);
       if (rc < 0) return rc;
       const long long prof = prof_begin(stream);
-      Top16ScanKernel<kMax><<<b.jobs, kScanThreads, 0, stream>>>(b);
+      cudaError_t st = launch_dependent(Top16ScanKernel<kMax>, dim3(b.jobs), dim3(kScanThreads), 0, stream, b);
       prof_end(prof, "Top16ScanKernel", stream);
-      const cudaError_t st = cudaGetLastError();
+      if (st == cudaSuccess) st = cudaGetLastError();
       if (st != cudaSuccess) return Fail("Top16ScanKernel", st);
       return launch_persistent(EncodeAutoKernel<kMax, kEncTop16Rec>, "EncodeTop16Kernel", kEncSmemBytes, b, tiles,
                                stream);
@@ -455,9 +476,10 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
     const uint64_t blocks =
         std::max<uint64_t>(1, std::min<uint64_t>((entries + 255) / 256, static_cast<uint64_t>(sms) * 4));
     const long long prof = prof_begin(stream);
-    EscapePatchKernel<kMax, kMode><<<dim3(static_cast<unsigned>(blocks), b.jobs), 256, 0, stream>>>(pb);
+    st = launch_dependent(EscapePatchKernel<kMax, kMode>, dim3(static_cast<unsigned>(blocks), b.jobs), dim3(256), 0,
+                          stream, pb);
     prof_end(prof, "EscapePatchKernel", stream);
-    st = cudaGetLastError();
+    if (st == cudaSuccess) st = cudaGetLastError();
     return st == cudaSuccess ? 0 : Fail("EscapePatchKernel", st);
   }
 }

@@ -70,6 +70,20 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch.  Kernels of this library are launched so
+// that each may start while the previous kernel of its stream finishes: a
+// kernel touches nothing in global memory before grid_dependency_wait()
+// returns (the previous grid has completed and its writes are visible), and
+// every CTA calls grid_dependency_release() once it is past that point, so
+// the next kernel's CTAs can be scheduled as this grid's CTAs retire.  In a
+// launch without the attribute both are no-ops.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_release() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+__device__ __forceinline__ void grid_dependency_sync() {
+  grid_dependency_wait();
+  grid_dependency_release();
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
                : "memory");

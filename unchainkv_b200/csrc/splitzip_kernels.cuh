@@ -674,6 +674,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
   if (tid < kPresWords) reinterpret_cast<uint32_t*>(spres)[tid] = 0;
   ring_init(R);
   __syncthreads();
+  grid_dependency_sync();
   int pres_job = -1, table_job = -1;
   // OR the presence bits gathered for a job into its bitmap, then clear them
   // (consumers only; every warp is past its last presence store)
@@ -970,6 +971,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeFixedKernel(const __grid
   __shared__ EncDesc D[kEncStages];
   ring_init(R);
   __syncthreads();
+  grid_dependency_sync();
   int rank_job = -1;
   bool skip = false;
   encode_pipeline<kMax>(b, ring, R, D, [&](const EncJob& J, int j, uint32_t tile, const uint16_t* sin,
@@ -1057,6 +1059,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) EncodeAutoKernel(const __grid_
   const int tid = threadIdx.x;
   ring_init(R);
   __syncthreads();
+  grid_dependency_sync();
   int setup_job = -1;
   int kind = kAutoOverflow;
   uint64_t escapes = 0;
@@ -1219,6 +1222,7 @@ constexpr int kScanTilesPerThread = 4;
 template <int kMax>
 __global__ void __launch_bounds__(kScanThreads) Top16ScanKernel(const __grid_constant__ EncBatch<kMax> b) {
   __shared__ uint32_t wsum[kScanThreads / 32];
+  grid_dependency_sync();
   const uint32_t j = blockIdx.x;
   if (j >= b.jobs) return;
   const EncJob& J = b.job[j];
@@ -1328,6 +1332,7 @@ __global__ void __launch_bounds__(kCtaThreads, 2) ExpHistogramKernel(const __gri
   for (int i = tid; i < kWarps * 512; i += kCtaThreads) (&whist[0][0])[i] = 0;
   ring_init(R);
   __syncthreads();
+  grid_dependency_sync();
   uint32_t* mine = whist[warp & (kWarps - 1)];
   int hist_job = -1;
   auto flush = [&](const EncJob& P) {
@@ -1717,6 +1722,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
   const int warp = tid >> 5;
   ring_init(R);
   __syncthreads();
+  grid_dependency_sync();
   if (warp == kProducerWarp) {
     decode_producer<kMax, kMode>(b, ring, R, D);
     return;
@@ -1787,6 +1793,7 @@ template <int kMax, int kMode>
 __global__ void __launch_bounds__(256) EscapePatchKernel(const __grid_constant__ PatchBatch<kMax> b) {
   // blockIdx.y is the job: every job's entries are patched at once; the
   // blocks of a job stride over the entries its stream holds
+  grid_dependency_sync();
   const uint32_t j = blockIdx.y;
   if (j >= b.jobs) return;
   const DecJob& J = b.job[j];
@@ -1987,6 +1994,7 @@ __global__ void __launch_bounds__(256) WritebackKernel(const __grid_constant__ W
 
 template <int kMax>
 __global__ void __launch_bounds__(kThreads) ZeroKernel(const __grid_constant__ ZeroBatch<kMax> z) {
+  grid_dependency_sync();
   for (uint32_t r = blockIdx.y; r < z.count; r += gridDim.y) {
     uint8_t* p = z.ptr[r];
     const uint64_t bytes = z.bytes[r];

@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(kCtaThreads, 3) TorchopStatsKernel(const __gri
   else if (tid < 128) reinterpret_cast<uint32_t*>(slo)[tid - 64] = 0;
   ring_init(R);
   __syncthreads();
+  grid_dependency_sync();
   int pres_job = -1;
   auto flush = [&](const EncJob& P) {  // consumers only, every warp past its stores
     TorchopPlan* plan = plan_of(P);
