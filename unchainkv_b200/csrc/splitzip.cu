@@ -888,7 +888,8 @@ long long launch_torchop(const std::vector<Prepared>& jobs, size_t first, size_t
     b.unit_start[i] = units;
     b.job[i] = e.job[i];
     b.vec[i] = vec_ok(e.job[i].src, e.job[i].L) ? 1 : 0;
-    units += (e.job[i].n + kUnitWords - 1) / kUnitWords;
+    // whole warps per job: a warp's units store one run of each plane
+    units += ((e.job[i].n + kUnitWords - 1) / kUnitWords + 31) / 32 * 32;
   }
   b.unit_start[count] = units;
   int device = 0, sms = 0;

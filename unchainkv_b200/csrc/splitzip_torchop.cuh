@@ -22,9 +22,12 @@
 //                       code of each high byte / nibble (the job's plan);
 //   TorchopEncodeKernel one thread per 16-word unit: every plane of these
 //                       forms holds a whole number of bytes per unit (16
-//                       codes of w bits are 2w bytes), so units are
-//                       independent.
+//                       codes of w bits are 2w bytes), so a warp's 32 units
+//                       fill one contiguous run of each plane, which the
+//                       warp stores together.
 #pragma once
+
+#include <type_traits>
 
 #include "splitzip_kernels.cuh"
 
@@ -271,40 +274,95 @@ __global__ void __launch_bounds__(32) TorchopDecideKernel(const __grid_constant_
   }
 }
 
-// 16 fields of w bits (w <= 8) packed LSB first into 128 bits.
-__device__ __forceinline__ void pack16(const uint32_t (&c)[16], uint32_t w, uint64_t& lo, uint64_t& hi) {
+// 16 fields of W bits packed LSB first into (lo, hi), W a constant.
+template <int W>
+__device__ __forceinline__ void pack16w(const uint32_t (&c)[16], uint64_t& lo, uint64_t& hi) {
   lo = 0;
   hi = 0;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const uint32_t bit = i * w;
+    constexpr int kW = W;
+    const int bit = i * kW;
     const uint64_t v = c[i];
     if (bit < 64) {
       lo |= v << bit;
-      if (bit + w > 64) hi |= v >> (64 - bit);
+      if (bit + kW > 64) hi |= v >> (64 - bit);
     } else {
       hi |= v << (bit - 64);
     }
   }
 }
 
-// Bytes [0, nbytes) of a little-endian 128-bit value to p.
-__device__ __forceinline__ void put_bytes(uint8_t* p, uint64_t lo, uint64_t hi, uint32_t nbytes) {
-  for (uint32_t k = 0; k < nbytes; ++k) p[k] = static_cast<uint8_t>(k < 8 ? lo >> (8 * k) : hi >> (8 * (k - 8)));
+// A warp's run of a code plane: lane L packs the 16 fields of the warp's
+// unit L (2W bytes) and the warp stores them at g + 2W L as one contiguous
+// run, with aligned stores of the widest slot 2W allows (bytes at or past
+// g + valid are not written).
+template <int W>
+__device__ __forceinline__ void put_plane_w(uint8_t* g, uint32_t valid, const uint32_t (&c)[16], int lane) {
+  uint64_t lo, hi;
+  pack16w<W>(c, lo, hi);
+  using Slot = typename std::conditional<(2 * W) % 8 == 0, uint64_t,
+                                         typename std::conditional<(2 * W) % 4 == 0, uint32_t, uint16_t>::type>::type;
+  constexpr int S = sizeof(Slot);
+  constexpr int K = 2 * W / S;
+  Slot d[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int bit = 8 * S * k;
+    d[k] = static_cast<Slot>(bit < 64 ? lo >> bit : hi >> (bit - 64));
+  }
+  warp_store<Slot, K>(g, valid, d, lane);
 }
 
-// One thread per 16-word unit of every job, by the job's plan.
+__device__ __forceinline__ void put_plane(uint32_t w, uint8_t* g, uint32_t valid, const uint32_t (&c)[16], int lane) {
+  switch (w) {  // uniform across the warp (a job's width)
+    case 1: put_plane_w<1>(g, valid, c, lane); break;
+    case 2: put_plane_w<2>(g, valid, c, lane); break;
+    case 3: put_plane_w<3>(g, valid, c, lane); break;
+    case 4: put_plane_w<4>(g, valid, c, lane); break;
+    case 5: put_plane_w<5>(g, valid, c, lane); break;
+    case 6: put_plane_w<6>(g, valid, c, lane); break;
+    case 7: put_plane_w<7>(g, valid, c, lane); break;
+    case 8: put_plane_w<8>(g, valid, c, lane); break;
+    default: break;  // a width of 0 has no plane bytes
+  }
+}
+
+// Bytes of a plane of `plane_bytes` that a warp's run starting `at` bytes in
+// may write (the run is at most 32 units long).
+__device__ __forceinline__ uint32_t run_valid(uint64_t plane_bytes, uint64_t at, uint32_t run) {
+  return at >= plane_bytes ? 0u : static_cast<uint32_t>(min(plane_bytes - at, static_cast<uint64_t>(run)));
+}
+
+// One thread per 16-word unit of every job, by the job's plan.  A job's
+// units are padded to whole warps (the host's unit_start), so a warp's 32
+// consecutive units belong to one job, and each plane's bytes of those units
+// are one contiguous run, stored by the warp together (warp_store: aligned
+// slots, shuffles for the bytes between lanes) instead of byte by byte.
 template <int kMax>
 __global__ void __launch_bounds__(256) TorchopEncodeKernel(const __grid_constant__ TorchopBatch<kMax> b) {
-  const uint64_t total = b.unit_start[b.jobs];
-  int j = 0;
+  // each warp's copy of its job's code tables (the plan's rank, then nib_rank)
+  __shared__ __align__(16) uint8_t stab[kThreads / 32][320];
+  grid_dependency_sync();
+  const uint64_t total = b.unit_start[b.jobs];  // a multiple of 32
+  const int lane = threadIdx.x & 31;
+  uint8_t* tab = stab[threadIdx.x >> 5];
+  int j = 0, tab_job = -1;
   for (uint64_t u = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < total;
-       u += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    while (u >= b.unit_start[j + 1]) ++j;  // a thread's units increase
+       u += static_cast<uint64_t>(gridDim.x) * blockDim.x) {  // whole warps: the loop is uniform
+    while (u >= b.unit_start[j + 1]) ++j;  // a thread's units increase; uniform across the warp
     const EncJob& J = b.job[j];
     const TorchopPlan* plan = plan_of(J);
+    if (j != tab_job) {
+      __syncwarp();  // the lanes are done with the previous job's tables
+      const uint32_t* from = reinterpret_cast<const uint32_t*>(plan->rank);
+      for (int i = lane; i < 80; i += 32) reinterpret_cast<uint32_t*>(tab)[i] = from[i];
+      __syncwarp();
+      tab_job = j;
+    }
     const uint64_t n = J.n, unit = u - b.unit_start[j], g = kUnitWords * unit;
-    const uint32_t valid = static_cast<uint32_t>(min(n - g, static_cast<uint64_t>(kUnitWords)));
+    const uint64_t unit0 = unit - static_cast<uint64_t>(lane);  // the warp's first unit
+    const uint32_t valid = g < n ? static_cast<uint32_t>(min(n - g, static_cast<uint64_t>(kUnitWords))) : 0u;
     uint32_t w16[kUnitWords];
     if (b.vec[j] && valid == kUnitWords) {
       const uint4* p = reinterpret_cast<const uint4*>(J.src + layout_addr(J.L, g));
@@ -322,44 +380,38 @@ __global__ void __launch_bounds__(256) TorchopEncodeKernel(const __grid_constant
     }
     const uint32_t mode = __ldg(&plan->mode);
     uint8_t* s = J.dst;
-    if (mode == 6) {
+    if (mode == 6) {  // the words as they are
+      uint32_t x[8];
 #pragma unroll
-      for (int i = 0; i < kUnitWords; ++i) {
-        if (static_cast<uint32_t>(i) < valid) {
-          s[1 + 2 * (g + i)] = static_cast<uint8_t>(w16[i]);
-          s[2 + 2 * (g + i)] = static_cast<uint8_t>(w16[i] >> 8);
-        }
-      }
+      for (int i = 0; i < 8; ++i) x[i] = w16[2 * i] | (w16[2 * i + 1] << 16);
+      warp_store<uint32_t, 8>(s + 1 + 32 * unit0, run_valid(2 * n, 32 * unit0, 32 * 32), x, lane);
       continue;
     }
     if (mode == 2 || mode == 0) {  // the low bytes
-      uint8_t* low = s + (mode == 2 ? 3 : 258) + g;
+      uint32_t lw[4];
 #pragma unroll
-      for (int i = 0; i < kUnitWords; ++i)
-        if (static_cast<uint32_t>(i) < valid) low[i] = static_cast<uint8_t>(w16[i]);
+      for (int q = 0; q < 4; ++q)
+        lw[q] = (w16[4 * q] & 0xFFu) | ((w16[4 * q + 1] & 0xFFu) << 8) | ((w16[4 * q + 2] & 0xFFu) << 16) |
+                (w16[4 * q + 3] << 24);
+      warp_store<uint32_t, 4>(s + (mode == 2 ? 3 : 258) + 16 * unit0, run_valid(n, 16 * unit0, 32 * 16), lw,
+                              lane);
     }
     uint32_t c[16];
-    uint64_t lo, hi;
     if (mode == 2) {
       const uint32_t w = __ldg(&plan->width), m0 = __ldg(&plan->mag_min);
       const uint64_t sign_bytes = (n + 7) / 8;
 #pragma unroll
       for (int i = 0; i < 16; ++i) c[i] = static_cast<uint32_t>(i) < valid ? (w16[i] >> 15) : 0u;
-      pack16(c, 1, lo, hi);
-      put_bytes(s + 3 + n + 2 * unit, lo, hi, static_cast<uint32_t>(min(uint64_t{2}, sign_bytes - 2 * unit)));
+      put_plane_w<1>(s + 3 + n + 2 * unit0, run_valid(sign_bytes, 2 * unit0, 32 * 2), c, lane);
 #pragma unroll
       for (int i = 0; i < 16; ++i) c[i] = static_cast<uint32_t>(i) < valid ? ((w16[i] >> 8) & 0x7Fu) - m0 : 0u;
-      pack16(c, w, lo, hi);
-      const uint64_t off = uint64_t{2} * w * unit;
-      put_bytes(s + 3 + n + sign_bytes + off, lo, hi,
-                static_cast<uint32_t>(min(uint64_t{2} * w, code_bytes(n, w) - off)));
+      put_plane(w, s + 3 + n + sign_bytes + 2 * w * unit0, run_valid(code_bytes(n, w), 2 * w * unit0, 64 * w), c,
+                lane);
     } else if (mode == 0) {
       const uint32_t w = __ldg(&plan->width);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) c[i] = static_cast<uint32_t>(i) < valid ? __ldg(&plan->rank[w16[i] >> 8]) : 0u;
-      pack16(c, w, lo, hi);
-      const uint64_t off = uint64_t{2} * w * unit;
-      put_bytes(s + 258 + n + off, lo, hi, static_cast<uint32_t>(min(uint64_t{2} * w, code_bytes(n, w) - off)));
+      for (int i = 0; i < 16; ++i) c[i] = static_cast<uint32_t>(i) < valid ? tab[w16[i] >> 8] : 0u;
+      put_plane(w, s + 258 + n + 2 * w * unit0, run_valid(code_bytes(n, w), 2 * w * unit0, 64 * w), c, lane);
     } else {  // mode 1
       const uint32_t widths = __ldg(&plan->nib_width);
       uint8_t* plane = s + 69;
@@ -368,10 +420,8 @@ __global__ void __launch_bounds__(256) TorchopEncodeKernel(const __grid_constant
         const uint32_t w = (widths >> (8 * q)) & 0xFFu;
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          c[i] = static_cast<uint32_t>(i) < valid ? __ldg(&plan->nib_rank[16 * q + ((w16[i] >> (4 * q)) & 0xFu)]) : 0u;
-        pack16(c, w, lo, hi);
-        const uint64_t off = uint64_t{2} * w * unit;
-        put_bytes(plane + off, lo, hi, static_cast<uint32_t>(min(uint64_t{2} * w, code_bytes(n, w) - off)));
+          c[i] = static_cast<uint32_t>(i) < valid ? tab[256 + 16 * q + ((w16[i] >> (4 * q)) & 0xFu)] : 0u;
+        put_plane(w, plane + 2 * w * unit0, run_valid(code_bytes(n, w), 2 * w * unit0, 64 * w), c, lane);
         plane += code_bytes(n, w);
       }
     }
