@@ -181,6 +181,45 @@ def test_gpu_torchop_encoder_matches_oracle_and_round_trips(kind):
         assert np.array_equal(got[:, ids], cache[:, ids])
 
 
+def test_gpu_torchop_batch_of_ragged_jobs_matches_oracle():
+    """Jobs of every form and of sizes that are not whole warps of 16-word
+    units (each job's units are padded to whole warps inside the kernel) in
+    one batch: every stream equals the oracle's, and no byte between the
+    streams changes."""
+    rng = np.random.Generator(np.random.PCG64(77))
+    specs = [("mode2_w3", 13, 37), ("mode0_9", 96, 5), ("mode1", 7, 61), ("mode0_128", 1024, 3),
+             ("mode2_w6", 21, 29), ("raw", 40, 7)]
+    jobs, keep, cases, offs = [], [], [], []
+    total = 0
+    for kind, bw, blocks in specs:
+        pool = blocks + 3
+        if kind == "raw":
+            cache = rng.integers(0, 1 << 16, size=(2, pool, bw), dtype=np.uint16)
+        else:
+            cache = words_for(kind, rng, (2, pool, bw))
+        ids = rng.permutation(pool)[:blocks]
+        n = 2 * blocks * bw
+        cap = (S.torchop_capacity(n) + 15) // 16 * 16
+        cases.append((cache, ids, n))
+        offs.append((total, cap))
+        total += cap + 64  # a gap after each buffer, checked below
+    buf = torch.full((total,), 0xA5, dtype=torch.uint8, device="cuda")
+    for (cache, ids, n), (o, cap) in zip(cases, offs):
+        kv = dev(cache.view(np.int16)).view(torch.bfloat16)
+        ids_t = dev(np.asarray(ids, dtype=np.int64))
+        keep += [kv, ids_t]
+        jobs.append(S.make_job(kv, ids_t, buf[o:o + cap]))
+    assert S.encode_torchop_batch(jobs) == sum(1 + 2 * n for _, _, n in cases)
+    torch.cuda.synchronize()
+    host = buf.cpu().numpy()
+    for (cache, ids, n), (o, cap) in zip(cases, offs):
+        result, expected = oracle.encode_torchop_blocks(cache, ids)
+        if result == 0:  # the reference sends it raw
+            expected = np.concatenate([[6], cache[:, ids].reshape(-1).view(np.uint8)]).astype(np.uint8)
+        assert np.array_equal(host[o:o + expected.size], expected)
+        assert np.all(host[o + cap:o + cap + 64] == 0xA5)
+
+
 def test_gpu_torchop_encoder_falls_back_to_raw():
     rng = np.random.Generator(np.random.PCG64(41))
     cache = rng.integers(0, 1 << 16, size=(2, 20, 512), dtype=np.uint16)
