@@ -953,7 +953,8 @@ long long launch_modes(const std::vector<DecJob>& jobs, size_t first, size_t cou
   for (size_t i = 0; i < count; ++i) {
     b.unit_start[i] = units;
     b.job[i] = jobs[first + i];
-    units += (b.job[i].n + kUnitWords - 1) / kUnitWords;
+    // whole warps per job: a warp keeps one job's palette
+    units += ((b.job[i].n + kUnitWords - 1) / kUnitWords + 31) / 32 * 32;
   }
   b.unit_start[count] = units;
   int device = 0, sms = 0;

@@ -1821,9 +1821,10 @@ __global__ void __launch_bounds__(256) EscapePatchKernel(const __grid_constant__
 // untouched).  Every plane of these forms holds a whole number of bytes per
 // 16-word unit (16 codes of w bits are 2w bytes), so one thread decodes one
 // unit from its bytes of each plane, read with aligned 4-byte loads that
-// stay inside the stream; the header (mode, widths, palettes) comes through
-// the read-only cache.  These forms are the receiver's fallbacks (the hot
-// path is modes 5, 3 and 6), so this is a plain grid-stride kernel.
+// stay inside the stream; the mode and widths come through the read-only
+// cache and each warp copies its job's palette into shared memory.  These
+// forms are the receiver's fallbacks (the hot path is modes 5, 3 and 6), so
+// this is a grid-stride kernel without a staging ring.
 
 template <int kMax>
 struct ModeBatch {
@@ -1857,18 +1858,85 @@ __device__ __forceinline__ uint32_t bit_field(const uint32_t (&bits)[5], uint32_
 
 __device__ __forceinline__ uint64_t plane_bytes(uint64_t n, uint32_t w) { return (n * w + 7) / 8; }
 
+// High bytes of a unit's 16 words from their W-bit codes (W a constant, so
+// every field is a fixed funnel shift) through a palette in shared memory.
+template <int W>
+__device__ __forceinline__ void palette_his(const uint32_t (&c)[5], const uint8_t* pal, uint32_t (&hi)[kUnitWords]) {
+#pragma unroll
+  for (int i = 0; i < kUnitWords; ++i) hi[i] = pal[bit_field(c, i, W)];
+}
+
+__device__ __forceinline__ void palette_his(uint32_t w, const uint32_t (&c)[5], const uint8_t* pal,
+                                            uint32_t (&hi)[kUnitWords]) {
+  switch (w) {  // uniform across the warp (a job's width)
+    case 1: palette_his<1>(c, pal, hi); break;
+    case 2: palette_his<2>(c, pal, hi); break;
+    case 3: palette_his<3>(c, pal, hi); break;
+    case 4: palette_his<4>(c, pal, hi); break;
+    case 5: palette_his<5>(c, pal, hi); break;
+    case 6: palette_his<6>(c, pal, hi); break;
+    default: palette_his<7>(c, pal, hi); break;
+  }
+}
+
+// Sign/magnitude high bytes of a unit (mode 2) with W-bit magnitudes.
+template <int W>
+__device__ __forceinline__ void signmag_his(const uint32_t (&sg)[5], const uint32_t (&mg)[5], uint32_t mag_min,
+                                            uint32_t (&hi)[kUnitWords]) {
+#pragma unroll
+  for (int i = 0; i < kUnitWords; ++i) hi[i] = (bit_field(sg, i, 1) << 7) | (bit_field(mg, i, W) + mag_min);
+}
+
+__device__ __forceinline__ void signmag_his(uint32_t w, const uint32_t (&sg)[5], const uint32_t (&mg)[5],
+                                            uint32_t mag_min, uint32_t (&hi)[kUnitWords]) {
+  switch (w) {
+    case 1: signmag_his<1>(sg, mg, mag_min, hi); break;
+    case 2: signmag_his<2>(sg, mg, mag_min, hi); break;
+    case 3: signmag_his<3>(sg, mg, mag_min, hi); break;
+    case 4: signmag_his<4>(sg, mg, mag_min, hi); break;
+    case 5: signmag_his<5>(sg, mg, mag_min, hi); break;
+    default: signmag_his<6>(sg, mg, mag_min, hi); break;
+  }
+}
+
+// One nibble plane of a unit (mode 1): OR the plane's nibbles into hi.
+template <int W>
+__device__ __forceinline__ void nibble_his(const uint32_t (&c)[5], const uint8_t* pal, int shift,
+                                           uint32_t (&hi)[kUnitWords]) {
+#pragma unroll
+  for (int i = 0; i < kUnitWords; ++i) hi[i] |= static_cast<uint32_t>(pal[bit_field(c, i, W)]) << shift;
+}
+
+// One thread per 16-word unit.  A job's units are padded to whole warps
+// (the host's unit_start), so a warp works on one job at a time and keeps
+// that job's palette (mode 0: 256 high bytes, mode 1: four 16-entry nibble
+// palettes, mode 4: 32 high bytes) in shared memory; the code widths are
+// dispatched once per job to code paths with constant field offsets.
 template <int kMax>
 __global__ void __launch_bounds__(256) ModeDecodeKernel(const __grid_constant__ ModeBatch<kMax> b) {
-  const uint64_t total = b.unit_start[b.jobs];
-  int j = 0;
+  __shared__ __align__(16) uint8_t spal[8][256];
+  const uint64_t total = b.unit_start[b.jobs];  // a multiple of 32
+  const int lane = threadIdx.x & 31;
+  uint8_t* pal = spal[threadIdx.x >> 5];
+  int j = 0, pal_job = -1;
   for (uint64_t u = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < total;
-       u += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    while (u >= b.unit_start[j + 1]) ++j;  // a thread's units increase
+       u += static_cast<uint64_t>(gridDim.x) * blockDim.x) {  // whole warps: the loop is uniform
+    while (u >= b.unit_start[j + 1]) ++j;  // a thread's units increase; uniform across the warp
     const DecJob& J = b.job[j];
     const uint8_t* s = J.src;
-    const uint64_t n = J.n, unit = u - b.unit_start[j], g = kUnitWords * unit;
-    const uint32_t valid = static_cast<uint32_t>(min(n - g, static_cast<uint64_t>(kUnitWords)));
     const uint32_t mode = __ldg(s);
+    if (j != pal_job) {  // the job's palette bytes, from the stream's header
+      __syncwarp();      // the lanes are done with the previous job's palette
+      const uint32_t at = mode == 0 ? 2 : mode == 1 ? 5 : 1;
+      const uint32_t bytes = mode == 0 ? 256 : mode == 1 ? 64 : mode == 4 ? 32 : 0;
+      if (J.src_bytes >= at + bytes)
+        for (uint32_t i = lane; i < bytes; i += 32) pal[i] = __ldg(s + at + i);
+      __syncwarp();
+      pal_job = j;
+    }
+    const uint64_t n = J.n, unit = u - b.unit_start[j], g = kUnitWords * unit;
+    if (g >= n) continue;  // a unit of the padding
+    const uint32_t valid = static_cast<uint32_t>(min(n - g, static_cast<uint64_t>(kUnitWords)));
     uint32_t hi[kUnitWords];  // high byte (modes 0, 2, 4) or the whole word (mode 1)
     uint32_t low[5] = {0, 0, 0, 0, 0};
     if (mode == 0) {
@@ -1878,8 +1946,7 @@ __global__ void __launch_bounds__(256) ModeDecodeKernel(const __grid_constant__ 
       const uint64_t off = uint64_t{2} * w * unit;
       ldg_bytes16(s + 258 + n + off, static_cast<uint32_t>(min(uint64_t{2} * w, plane_bytes(n, w) - off)), c);
       ldg_bytes16(s + 258 + g, valid, low);
-#pragma unroll
-      for (int i = 0; i < kUnitWords; ++i) hi[i] = __ldg(s + 2 + bit_field(c, i, w));
+      palette_his(w, c, pal, hi);
     } else if (mode == 2) {
       const uint32_t w = __ldg(s + 1), mag_min = __ldg(s + 2);
       const uint64_t sign_bytes = (n + 7) / 8;
@@ -1889,16 +1956,14 @@ __global__ void __launch_bounds__(256) ModeDecodeKernel(const __grid_constant__ 
       ldg_bytes16(s + 3 + n + 2 * unit, static_cast<uint32_t>(min(uint64_t{2}, sign_bytes - 2 * unit)), sg);
       ldg_bytes16(s + 3 + n + sign_bytes + off, static_cast<uint32_t>(min(uint64_t{2} * w, plane_bytes(n, w) - off)), mg);
       ldg_bytes16(s + 3 + g, valid, low);
-#pragma unroll
-      for (int i = 0; i < kUnitWords; ++i) hi[i] = (bit_field(sg, i, 1) << 7) | (bit_field(mg, i, w) + mag_min);
+      signmag_his(w, sg, mg, mag_min, hi);
     } else if (mode == 4) {
       if (J.src_bytes != 33 + n + plane_bytes(n, 5)) continue;
       uint32_t c[5];
       const uint64_t off = uint64_t{10} * unit;
       ldg_bytes16(s + 33 + n + off, static_cast<uint32_t>(min(uint64_t{10}, plane_bytes(n, 5) - off)), c);
       ldg_bytes16(s + 33 + g, valid, low);
-#pragma unroll
-      for (int i = 0; i < kUnitWords; ++i) hi[i] = __ldg(s + 1 + bit_field(c, i, 5));
+      palette_his<5>(c, pal, hi);
     } else if (mode == 1) {
       if (J.src_bytes < 69) continue;
       uint32_t w[4];
@@ -1919,8 +1984,9 @@ __global__ void __launch_bounds__(256) ModeDecodeKernel(const __grid_constant__ 
         uint32_t c[5];
         const uint64_t off = uint64_t{2} * w[q] * unit;
         ldg_bytes16(plane + off, static_cast<uint32_t>(min(uint64_t{2} * w[q], plane_bytes(n, w[q]) - off)), c);
-#pragma unroll
-        for (int i = 0; i < kUnitWords; ++i) hi[i] |= static_cast<uint32_t>(__ldg(s + 5 + 16 * q + bit_field(c, i, w[q]))) << (4 * q);
+        if (w[q] == 1) nibble_his<1>(c, pal + 16 * q, 4 * q, hi);
+        else if (w[q] == 2) nibble_his<2>(c, pal + 16 * q, 4 * q, hi);
+        else nibble_his<4>(c, pal + 16 * q, 4 * q, hi);
         plane += plane_bytes(n, w[q]);
       }
     } else {
