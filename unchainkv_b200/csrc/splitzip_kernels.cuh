@@ -568,37 +568,49 @@ __device__ __forceinline__ void warp_write_escapes(const EncJob& J, uint64_t t0,
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const uint32_t lower = (1u << lane) - 1u;
-  uint8_t* entries = J.dst + 5 + J.n + (J.n + 1) / 2;
+  // slots are counted from `base`: the run of entries starts at `run`, and
+  // `room` of its slots lie below the capacity (at most ceil(n/200) < 2^32)
+  uint8_t* run = J.dst + 5 + J.n + (J.n + 1) / 2 + 5 * base;
+  const uint32_t room = base < J.cap ? static_cast<uint32_t>(J.cap - base) : 0u;
+  uint32_t rel = 0;
 #pragma unroll
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t m = masks[s];
     const uint32_t lanes = __ballot_sync(kFull, m != 0);
     if (lanes == 0) continue;  // uniform
-    uint32_t off, total;
+    const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
     if (__ballot_sync(kFull, (m & (m - 1)) != 0) == 0) {
-      off = __popc(lanes & lower);
-      total = __popc(lanes);
-    } else {
-      const uint32_t mine = __popc(m);
-      uint32_t incl = mine;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += v;
+      // at most one escape per lane: no loop
+      const uint32_t slot = rel + __popc(lanes & lower);
+      if (m != 0 && slot < room) {
+        const uint32_t w = w0 + (__ffs(m) - 1);
+        const uint32_t pos = static_cast<uint32_t>(t0) + w;
+        uint8_t* en = run + 5 * static_cast<uint64_t>(slot);
+        en[0] = static_cast<uint8_t>(pos);
+        en[1] = static_cast<uint8_t>(pos >> 8);
+        en[2] = static_cast<uint8_t>(pos >> 16);
+        en[3] = static_cast<uint8_t>(pos >> 24);
+        en[4] = static_cast<uint8_t>(sin[w] >> 7);
       }
-      off = incl - mine;
-      total = __shfl_sync(kFull, incl, 31);
+      rel += __popc(lanes);
+      continue;
+    }
+    const uint32_t mine = __popc(m);
+    uint32_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
     }
     if (m != 0) {
-      const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-      uint64_t slot = base + off;
+      uint32_t slot = rel + incl - mine;
       uint32_t bits = m;
       do {
         const uint32_t w = w0 + (__ffs(bits) - 1);
         bits &= bits - 1;
-        if (slot < J.cap) {
-          const uint32_t pos = static_cast<uint32_t>(t0 + w);
-          uint8_t* en = entries + slot * 5;
+        if (slot < room) {
+          const uint32_t pos = static_cast<uint32_t>(t0) + w;
+          uint8_t* en = run + 5 * static_cast<uint64_t>(slot);
           en[0] = static_cast<uint8_t>(pos);
           en[1] = static_cast<uint8_t>(pos >> 8);
           en[2] = static_cast<uint8_t>(pos >> 16);
@@ -608,7 +620,7 @@ __device__ __forceinline__ void warp_write_escapes(const EncJob& J, uint64_t t0,
         ++slot;
       } while (bits);
     }
-    base += total;
+    rel += __shfl_sync(kFull, incl, 31);
   }
 }
 
