@@ -26,7 +26,14 @@ namespace ukv {
 
 constexpr int kMaxBatch = 96;
 constexpr int kEncStages = 2;  // ring depth of the encode kernels (32 KiB stages, 3 CTAs per SM)
-constexpr int kDecStages = 3;  // ring depth of the decode kernel (32.1 KiB stages, 2 CTAs per SM)
+// Ring depth of the decode kernel: 4 stages of 32.1 KiB, so that one CTA
+// fills an SM's shared memory.  With 3 stages two CTAs fit, and the decode
+// was slower both ways: two CTAs per SM took 192 us on configs[1]'s 32
+// layers against 172 for one; a grid capped at one CTA per SM left the
+// block scheduler free to put two of them on one SM while the previous
+// kernel's CTAs drained (launches overlap), 0.548 ms per round trip against
+// 0.49.
+constexpr int kDecStages = 4;
 constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 32 KiB of words
 constexpr uint32_t kDecStageBytes = 2 * kTileWords + 128;
 constexpr uint32_t kDecCodesOffset = kTileWords + 128;  // top16/fixed6 codes inside a stage
@@ -836,7 +843,13 @@ __global__ void __launch_bounds__(kCtaThreads, 3) PresenceKernel(const __grid_co
 // ------------------------------------------------------------ fixed encode
 
 // Palette rank of every high byte from a 256-bit presence bitmap (ascending
-// order) into srank[h]; thread tid handles high byte tid.
+// order) into srank[rank_slot(h)]; thread tid handles high byte tid.  The
+// slot copies the sign (bit 7) into bit 5, so a positive and a negative high
+// byte of the same magnitude sit 8 banks apart: a warp's lookups of +e and
+// -e do not collide.  rank_words applies the same swap to both words of a
+// pair at once, ahead of the byte extraction.
+__device__ __forceinline__ uint32_t rank_slot(uint32_t h) { return h ^ ((h >> 2) & 0x20u); }
+__device__ __forceinline__ uint32_t rank_words(uint32_t x) { return x ^ ((x >> 2) & 0x20002000u); }
 __device__ __forceinline__ void palette_ranks(const uint32_t* bitmap, uint8_t* srank, uint32_t& distinct,
                                               bool& present, uint32_t& rank) {
   const int tid = threadIdx.x;
@@ -852,7 +865,7 @@ __device__ __forceinline__ void palette_ranks(const uint32_t* bitmap, uint8_t* s
 #pragma unroll
   for (int w = 0; w < 8; ++w)
     if (w < (tid >> 5)) rank += __popc(bm[w]);
-  srank[tid] = static_cast<uint8_t>(rank);
+  srank[rank_slot(tid)] = static_cast<uint8_t>(rank);
 }
 
 // Header + palette of a fixed stream (written by one CTA).
@@ -884,10 +897,11 @@ __device__ __forceinline__ void fixed6_tile_full(const EncJob& J, uint64_t t0, c
     uint32_t g[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const uint32_t c0 = srank[__byte_perm(x[2 * q], 0, 0x4441)];
-      const uint32_t c1 = srank[x[2 * q] >> 24];
-      const uint32_t c2 = srank[__byte_perm(x[2 * q + 1], 0, 0x4441)];
-      const uint32_t c3 = srank[x[2 * q + 1] >> 24];
+      const uint32_t y0 = rank_words(x[2 * q]), y1 = rank_words(x[2 * q + 1]);
+      const uint32_t c0 = srank[__byte_perm(y0, 0, 0x4441)];
+      const uint32_t c1 = srank[y0 >> 24];
+      const uint32_t c2 = srank[__byte_perm(y1, 0, 0x4441)];
+      const uint32_t c3 = srank[y1 >> 24];
       g[q] = c0 | (c1 << 6) | (c2 << 12) | (c3 << 18);
     }
     qw[s][0] = g[0] | (g[1] << 24);
@@ -923,8 +937,9 @@ __device__ __forceinline__ void fixed_tile_body(const EncJob& J, uint64_t t0, ui
     uint32_t c[16];
 #pragma unroll
     for (int p = 0; p < 8; ++p) {
-      c[2 * p] = srank[__byte_perm(x[p], 0, 0x4441)];
-      c[2 * p + 1] = srank[x[p] >> 24];
+      const uint32_t y = rank_words(x[p]);
+      c[2 * p] = srank[__byte_perm(y, 0, 0x4441)];
+      c[2 * p + 1] = srank[y >> 24];
     }
     const bool full = step_valid == kStepWords;
     if (!full) {
@@ -1461,12 +1476,15 @@ struct DecDesc {
   uint16_t* step_dst[kStepsPerTile];   // 16-byte aligned contiguous destination of a step, or null
 };
 
-// fixed6 pair table of the consumers' current job: entry (c0 | c1 << 6)
-// holds the high bytes of a word pair whose codes are c0 and c1,
-// pal[c0] << 8 | pal[c1] << 24.
+// fixed6 pair table of the consumers' current job: the high bytes of a word
+// pair whose codes are c0 and c1, pal[c0] | pal[c1] << 8, as 16 bits at
+// entry (c0 | c1 << 6) ^ ((c1 & 31) << 1).  The swizzle spreads the lanes of
+// a warp that share c0 over the banks by c1 (a warp's code pairs share c0
+// often: the palette ranks of one layer are few), and a 2-byte entry merges
+// with the pair's low bytes in one byte permute.
 struct DecodeExtra {
   uint8_t pal[64];
-  uint32_t pair[4096];
+  uint16_t pair[4096];
 };
 
 // Destination of the 16-word unit at packed index g (valid words `valid`).
@@ -1675,6 +1693,8 @@ __device__ __forceinline__ void decode_fixed6_compute(const DecJob& J, const Dec
   const int warp = threadIdx.x >> 5;
   const uint32_t pad_x = d.pad_x, pad_y = d.pad_y;
   const uint8_t* pair = reinterpret_cast<const uint8_t*>(X.pair);
+  // byte offset of the swizzled entry of a 12-bit field held at bits 1..12
+  auto swz = [](uint32_t fo) { return fo ^ ((fo >> 5) & 0x7Cu); };
 #pragma unroll
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t step = warp * kStepsPerWarp + s;
@@ -1688,19 +1708,18 @@ __device__ __forceinline__ void decode_fixed6_compute(const DecJob& J, const Dec
     smem_read_words<3>(stage + kDecCodesOffset, pad_y + 3 * w0 / 4, Q);
     // byte offsets into the pair table of the 12-bit fields 12i..12i+11
     uint32_t f[8];
-    f[0] = (Q[0] << 2) & 0x3FFCu;
-    f[1] = (Q[0] >> 10) & 0x3FFCu;
-    f[2] = __funnelshift_r(Q[0], Q[1], 22) & 0x3FFCu;
-    f[3] = (Q[1] >> 2) & 0x3FFCu;
-    f[4] = (Q[1] >> 14) & 0x3FFCu;
-    f[5] = __funnelshift_r(Q[1], Q[2], 26) & 0x3FFCu;
-    f[6] = (Q[2] >> 6) & 0x3FFCu;
-    f[7] = (Q[2] >> 18) & 0x3FFCu;
+    f[0] = swz((Q[0] << 1) & 0x1FFEu);
+    f[1] = swz((Q[0] >> 11) & 0x1FFEu);
+    f[2] = swz(__funnelshift_r(Q[0], Q[1], 23) & 0x1FFEu);
+    f[3] = swz((Q[1] >> 3) & 0x1FFEu);
+    f[4] = swz((Q[1] >> 15) & 0x1FFEu);
+    f[5] = swz(__funnelshift_r(Q[1], Q[2], 27) & 0x1FFEu);
+    f[6] = swz((Q[2] >> 7) & 0x1FFEu);
+    f[7] = swz((Q[2] >> 19) & 0x1FFEu);
     uint32_t o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      o[i] = __byte_perm(Lw[i >> 1], 0, (i & 1) ? 0x4342 : 0x4140) |
-             *reinterpret_cast<const uint32_t*>(pair + f[i]);
+      o[i] = __byte_perm(Lw[i >> 1], *reinterpret_cast<const uint16_t*>(pair + f[i]), (i & 1) ? 0x5342 : 0x5140);
     store_step(J, d, t0, step, valid, lane, o);
   }
 }
@@ -1773,7 +1792,8 @@ __global__ void __launch_bounds__(kCtaThreads, 3) DecodeKernel(const __grid_cons
           if (tid < 64) X.pal[tid] = __ldg(J.src + 1 + tid);
           consumer_sync();
           for (int i = tid; i < 4096; i += kThreads)
-            X.pair[i] = (static_cast<uint32_t>(X.pal[i & 63]) << 8) | (static_cast<uint32_t>(X.pal[i >> 6]) << 24);
+            X.pair[i ^ (((i >> 6) & 31) << 1)] =
+                static_cast<uint16_t>(X.pal[i & 63] | (static_cast<uint32_t>(X.pal[i >> 6]) << 8));
           pair_job = ji;
           consumer_sync();
         }
