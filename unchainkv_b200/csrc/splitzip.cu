@@ -461,9 +461,10 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
     return rc;
   } else {
     if (rc < 0) return rc;
-    // the escaped words of the top16 streams, one thread per entry: grid
-    // rows are the jobs (all patched at once), each row covers the largest
-    // job's capacity (at most 4 x SMs blocks, striding beyond)
+    // the escaped words of the top16 streams: grid rows are the jobs (all
+    // patched at once), each row striding over its job's entries; the grid
+    // holds about 8 CTAs per SM in all, so a batch without top16 streams
+    // (each CTA reads one mode byte) costs one short wave
     static thread_local PatchBatch<kMax> pb;
     pb.jobs = b.jobs;
     uint64_t entries = 0;
@@ -475,8 +476,8 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
     cudaError_t st = cudaGetDevice(&device);
     if (st == cudaSuccess) st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
-    const uint64_t blocks =
-        std::max<uint64_t>(1, std::min<uint64_t>((entries + 255) / 256, static_cast<uint64_t>(sms) * 4));
+    const uint64_t per_row = std::max<uint64_t>(1, static_cast<uint64_t>(sms) * 8 / std::max<uint32_t>(1, b.jobs));
+    const uint64_t blocks = std::max<uint64_t>(1, std::min<uint64_t>((entries + 255) / 256, per_row));
     const long long prof = prof_begin(stream);
     st = launch_dependent(EscapePatchKernel<kMax, kMode>, dim3(static_cast<unsigned>(blocks), b.jobs), dim3(256), 0,
                           stream, pb);
