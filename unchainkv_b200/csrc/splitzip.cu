@@ -456,7 +456,7 @@ long long launch_decode(const std::vector<DecJob>& jobs, size_t first, size_t co
   b.tile_start[count] = tiles;
   const char* name =
       kMode == 5 ? "DecodeTop16Kernel" : kMode == 3 ? "DecodeFixed6Kernel" : "DecodeAutoKernel";
-  const long long rc = launch_persistent(DecodeKernel<kMax, kMode>, name, kDecSmemBytes, b, tiles, stream);
+  const long long rc = launch_persistent(DecodeKernel<kMax, kMode>, name, kDecCtaSmemBytes, b, tiles, stream);
   if constexpr (kMode == 3) {
     return rc;
   } else {

@@ -26,19 +26,22 @@ namespace ukv {
 
 constexpr int kMaxBatch = 96;
 constexpr int kEncStages = 2;  // ring depth of the encode kernels (32 KiB stages, 3 CTAs per SM)
-// Ring depth of the decode kernel: 4 stages of 32.1 KiB, so that one CTA
-// fills an SM's shared memory.  With 3 stages two CTAs fit, and the decode
-// was slower both ways: two CTAs per SM took 192 us on configs[1]'s 32
-// layers against 172 for one; a grid capped at one CTA per SM left the
-// block scheduler free to put two of them on one SM while the previous
-// kernel's CTAs drained (launches overlap), 0.548 ms per round trip against
-// 0.49.
-constexpr int kDecStages = 4;
+// Ring depth of the decode kernel: 3 stages of 32.1 KiB, one CTA per SM.
+// Two CTAs would fit; the launch asks for kDecCtaSmemBytes of dynamic
+// shared memory so that they do not.  Two CTAs per SM took 192 us on
+// configs[1]'s 32 layers against 172 for one; a grid capped at one CTA per
+// SM left the block scheduler free to put two of them on one SM while the
+// previous kernel's CTAs drained (launches overlap): 0.548 ms per round trip
+// against 0.49.  4 and 6 stages ran as fast in the timed loop, but their
+// event-timed launches on an idle GPU took 182-190 us.
+constexpr int kDecStages = 3;
 constexpr uint32_t kEncStageBytes = kTileWords * 2;  // 32 KiB of words
 constexpr uint32_t kDecStageBytes = 2 * kTileWords + 128;
 constexpr uint32_t kDecCodesOffset = kTileWords + 128;  // top16/fixed6 codes inside a stage
 constexpr uint32_t kEncSmemBytes = kEncStages * kEncStageBytes;
 constexpr uint32_t kDecSmemBytes = kDecStages * kDecStageBytes;
+constexpr uint32_t kDecCtaSmemBytes = 128 * 1024;  // > half an SM's shared memory: one CTA per SM
+static_assert(kDecCtaSmemBytes >= kDecSmemBytes, "the decode ring fits the request");
 
 // ------------------------------------------------------------------ jobs
 
