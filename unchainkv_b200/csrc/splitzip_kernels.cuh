@@ -2071,23 +2071,44 @@ struct WritebackBatch {
 
 template <int kMax>
 __global__ void __launch_bounds__(256) WritebackKernel(const __grid_constant__ WritebackBatch<kMax> b) {
+  // four 16-byte chunks a thread per round, their loads issued before any
+  // store: a plain copy needs bytes in flight more than anything else
+  constexpr int kU = 4;
   const uint64_t total = b.chunk_start[b.jobs];
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   int j = 0;
-  for (uint64_t c = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
-       c += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    while (c >= b.chunk_start[j + 1]) ++j;
-    const WritebackJob& W = b.job[j];
-    const uint64_t off = 16 * (c - b.chunk_start[j]);
-    const uint64_t n = min(uint64_t{16}, W.bytes - off);
-    const int s = off >= W.seg_bytes ? 1 : 0;
-    uint8_t* dst = W.seg[s] + (off - (s ? W.seg_bytes : 0));
-    if (W.vec && n == 16) {
-      *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(W.src + off));
-    } else {
-      for (uint64_t k = 0; k < n; ++k) {
-        const uint64_t o = off + k;
-        const int t = o >= W.seg_bytes ? 1 : 0;
-        W.seg[t][o - (t ? W.seg_bytes : 0)] = __ldg(W.src + o);
+  for (uint64_t c0 = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c0 < total; c0 += kU * stride) {
+    uint4 v[kU];
+    int jk[kU];
+#pragma unroll
+    for (int k = 0; k < kU; ++k) {
+      const uint64_t c = c0 + k * stride;
+      jk[k] = -1;
+      v[k] = make_uint4(0, 0, 0, 0);
+      if (c >= total) continue;
+      while (c >= b.chunk_start[j + 1]) ++j;  // chunks increase
+      jk[k] = j;
+      const WritebackJob& W = b.job[j];
+      const uint64_t off = 16 * (c - b.chunk_start[j]);
+      if (W.vec && off + 16 <= W.bytes) v[k] = __ldg(reinterpret_cast<const uint4*>(W.src + off));
+    }
+#pragma unroll
+    for (int k = 0; k < kU; ++k) {
+      if (jk[k] < 0) continue;
+      const uint64_t c = c0 + k * stride;
+      const WritebackJob& W = b.job[jk[k]];
+      const uint64_t off = 16 * (c - b.chunk_start[jk[k]]);
+      const uint64_t n = min(uint64_t{16}, W.bytes - off);
+      const int s = off >= W.seg_bytes ? 1 : 0;
+      uint8_t* dst = W.seg[s] + (off - (s ? W.seg_bytes : 0));
+      if (W.vec && n == 16) {
+        *reinterpret_cast<uint4*>(dst) = v[k];
+      } else {
+        for (uint64_t q = 0; q < n; ++q) {
+          const uint64_t o = off + q;
+          const int t = o >= W.seg_bytes ? 1 : 0;
+          W.seg[t][o - (t ? W.seg_bytes : 0)] = __ldg(W.src + o);
+        }
       }
     }
   }
