@@ -893,19 +893,36 @@ __device__ __forceinline__ void fixed6_tile_full(const EncJob& J, uint64_t t0, c
 #pragma unroll
   for (int s = 0; s < kStepsPerWarp; ++s) {
     const uint32_t w0 = (warp * kStepsPerWarp + s) * kStepWords + lane * kUnitWords;
-    uint32_t x[8];
-    load_unit(sin, w0, x);
+    // the lane's 16 words are 32 bytes: lanes 4-7 of each quarter warp load
+    // their second 16 bytes first, so that each 16-byte load instruction of
+    // a quarter warp covers all 32 banks once; the halves' results are put
+    // back in word order with selects
+    const bool sw = (lane & 4) != 0;
+    const uint4* pu = reinterpret_cast<const uint4*>(sin + w0);
+    const uint4 va = pu[sw ? 1 : 0];
+    const uint4 vb = pu[sw ? 0 : 1];
+    const uint32_t xh[2][4] = {{va.x, va.y, va.z, va.w}, {vb.x, vb.y, vb.z, vb.w}};
+    uint32_t lh[2][2], gh[2][2];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) low[s][q] = __byte_perm(x[2 * q], x[2 * q + 1], 0x6420);
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        lh[h][q] = __byte_perm(xh[h][2 * q], xh[h][2 * q + 1], 0x6420);
+        const uint32_t y0 = rank_words(xh[h][2 * q]), y1 = rank_words(xh[h][2 * q + 1]);
+        const uint32_t c0 = srank[__byte_perm(y0, 0, 0x4441)];
+        const uint32_t c1 = srank[y0 >> 24];
+        const uint32_t c2 = srank[__byte_perm(y1, 0, 0x4441)];
+        const uint32_t c3 = srank[y1 >> 24];
+        gh[h][q] = c0 | (c1 << 6) | (c2 << 12) | (c3 << 18);
+      }
+    }
     uint32_t g[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t y0 = rank_words(x[2 * q]), y1 = rank_words(x[2 * q + 1]);
-      const uint32_t c0 = srank[__byte_perm(y0, 0, 0x4441)];
-      const uint32_t c1 = srank[y0 >> 24];
-      const uint32_t c2 = srank[__byte_perm(y1, 0, 0x4441)];
-      const uint32_t c3 = srank[y1 >> 24];
-      g[q] = c0 | (c1 << 6) | (c2 << 12) | (c3 << 18);
+    for (int q = 0; q < 2; ++q) {
+      low[s][q] = sw ? lh[1][q] : lh[0][q];
+      low[s][2 + q] = sw ? lh[0][q] : lh[1][q];
+      g[q] = sw ? gh[1][q] : gh[0][q];
+      g[2 + q] = sw ? gh[0][q] : gh[1][q];
     }
     qw[s][0] = g[0] | (g[1] << 24);
     qw[s][1] = (g[1] >> 8) | (g[2] << 16);
