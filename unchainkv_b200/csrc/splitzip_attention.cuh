@@ -336,12 +336,11 @@ __device__ __forceinline__ void top16_load(const AttnDesc& d, const uint8_t* sta
   }
 }
 
-// A top16 word pair: body bytes of words 4q..4q+3 in bw, their book
-// exponents in e4; `upper` takes words 4q+2, 4q+3 instead of 4q, 4q+1.
-__device__ __forceinline__ uint32_t top16_pair(uint32_t bw, uint32_t e4, bool upper) {
-  const uint32_t body2 = __byte_perm(bw, 0, upper ? 0x3322 : 0x1100);
-  const uint32_t ex = __byte_perm(e4, 0, upper ? 0x4342 : 0x4140) << 7;
-  return (body2 & 0x807F807Fu) | ex;
+// A top16 word pair: the body bytes of words 4q..4q+3 in bw (`upper` takes
+// words 4q+2, 4q+3 instead of 4q, 4q+1) and the pair's code-byte table
+// entry, which holds the two words' book exponents at bits 7 and 23.
+__device__ __forceinline__ uint32_t top16_pair_t(uint32_t bw, uint32_t exps, bool upper) {
+  return (__byte_perm(bw, 0, upper ? 0x3322 : 0x1100) & 0x807F807Fu) | exps;
 }
 
 // Exponent of the stage's escape of rank r (its place in the stage's slice
@@ -602,12 +601,23 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
       const AttnItem& I = b.item[item];
       const int req = static_cast<int>(I.req);
       if (req != pair_req) {
-        // the request's fixed6 pair table: every consumer warp is past the
-        // previous item; the palette comes from the item's first stage
+        // the request's pair table: every consumer warp is past the previous
+        // item.  fixed6: from the palette of the item's first stage; top16:
+        // per plane, the book exponents of a code byte's two words at their
+        // places in a word pair (bits 7 and 23), 256 entries a plane
         attn_consumer_sync();
         consumer_wait(R, p, nullptr);
-        const uint8_t* pal = D[p.s].pal;
-        for (int i = tid; i < 4096; i += kAttnKThreads) pair[i] = pair_entry(pal, i);
+        if (kTop16 && D[p.s].mode == 5) {
+          const uint8_t* books = b.req[I.req].tables + 512;
+          for (int i = tid; i < 512; i += kAttnKThreads) {
+            const uint8_t* bk = books + 16 * (i >> 8);
+            pair[i] = (static_cast<uint32_t>(__ldg(bk + (i & 15))) << 7) |
+                      (static_cast<uint32_t>(__ldg(bk + ((i >> 4) & 15))) << 23);
+          }
+        } else {
+          const uint8_t* pal = D[p.s].pal;
+          for (int i = tid; i < 4096; i += kAttnKThreads) pair[i] = pair_entry(pal, i);
+        }
         pair_req = req;
         attn_consumer_sync();
       }
@@ -640,8 +650,7 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
                      raw_word_pair(d, stage, gid + 8, dim, 2 * kk), raw_word_pair(d, stage, gid, dim, 2 * kk + 1),
                      raw_word_pair(d, stage, gid + 8, dim, 2 * kk + 1), qb[2 * kk], qb[2 * kk + 1]);
         } else if (kTop16 && d.mode == 5) {
-          const uint4 bv = *reinterpret_cast<const uint4*>(d.pal);
-          const uint32_t bk[4] = {bv.x, bv.y, bv.z, bv.w};
+          const uint32_t* t16 = pair;  // the K plane's code-byte table
           uint32_t B0[8], N0[4], B1[8], N1[4];
           top16_load<16>(d, stage, gid, dim, B0, N0);
           top16_load<16>(d, stage, gid + 8, dim, B1, N1);
@@ -655,10 +664,11 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
           const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t e0 = book_exps4(bk, (N0[kk >> 1] >> (16 * (kk & 1))) & 0xFFFFu);
-            const uint32_t e1 = book_exps4(bk, (N1[kk >> 1] >> (16 * (kk & 1))) & 0xFFFFu);
-            uint32_t a0 = top16_pair(B0[kk], e0, false), a2 = top16_pair(B0[kk], e0, true);
-            uint32_t a1 = top16_pair(B1[kk], e1, false), a3 = top16_pair(B1[kk], e1, true);
+            const uint32_t n0 = N0[kk >> 1] >> (16 * (kk & 1)), n1 = N1[kk >> 1] >> (16 * (kk & 1));
+            uint32_t a0 = top16_pair_t(B0[kk], t16[n0 & 0xFFu], false);
+            uint32_t a2 = top16_pair_t(B0[kk], t16[(n0 >> 8) & 0xFFu], true);
+            uint32_t a1 = top16_pair_t(B1[kk], t16[n1 & 0xFFu], false);
+            uint32_t a3 = top16_pair_t(B1[kk], t16[(n1 >> 8) & 0xFFu], true);
             if (((r0 | r1) >> (4 * kk)) & 0xFu) {
               const uint32_t below = (1u << (4 * kk)) - 1u;
               a0 = top16_patch(a0, (r0 >> (4 * kk)) & 3u, p0 + __popc(r0 & below), stage, entries, d.esc_first, d.esc_count);
@@ -791,8 +801,7 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
             mma_step(m, raw_word_pair(d, stage, t0, dim, m), raw_word_pair(d, stage, t0 + 1, dim, m),
                      raw_word_pair(d, stage, t2, dim, m), raw_word_pair(d, stage, t2 + 1, dim, m));
         } else if (kTop16 && d.mode == 5) {
-          const uint4 bv = *reinterpret_cast<const uint4*>(d.pal);
-          const uint32_t bk[4] = {bv.x, bv.y, bv.z, bv.w};
+          const uint32_t* t16 = pair + 256;  // the V plane's code-byte table
           const uint32_t tok[4] = {t0, t0 + 1, t2, t2 + 1};
           uint32_t B[4][4], N[4][2], r[4], pre[4];
           const uint32_t* bm = reinterpret_cast<const uint32_t*>(stage + kAttnEscBitmap);
@@ -813,8 +822,7 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
             uint32_t v[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint32_t e = book_exps4(bk, (N[j][m >> 2] >> (16 * ((m >> 1) & 1))) & 0xFFFFu);
-              v[j] = top16_pair(B[j][m >> 1], e, (m & 1) != 0);
+              v[j] = top16_pair_t(B[j][m >> 1], t16[(N[j][m >> 2] >> (8 * (m & 3))) & 0xFFu], (m & 1) != 0);
               const uint32_t bits2 = (r[j] >> (2 * m)) & 3u;
               if (bits2) v[j] = top16_patch(v[j], bits2, pre[j] + __popc(r[j] & ((1u << (2 * m)) - 1u)), stage,
                                            entries, d.esc_first, d.esc_count);
