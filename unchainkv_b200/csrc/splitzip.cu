@@ -134,8 +134,7 @@ cudaError_t launch_dependent(Kernel kernel, dim3 grid, dim3 block, size_t dyn_sm
 }
 
 template <typename Kernel>
-long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* grid, int threads = kCtaThreads,
-                   int max_per_sm = 0) {
+long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* grid, int threads = kCtaThreads) {
   int device = 0;
   cudaError_t st = cudaGetDevice(&device);
   if (st != cudaSuccess) return Fail("cudaGetDevice", st);
@@ -154,7 +153,6 @@ long long grid_for(Kernel kernel, size_t dyn_smem, uint64_t tiles, unsigned* gri
     if (st != cudaSuccess) return Fail("cudaOccupancyMaxActiveBlocksPerMultiprocessor", st);
     st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     if (st != cudaSuccess) return Fail("cudaDeviceGetAttribute", st);
-    if (max_per_sm > 0) per_sm = std::min(per_sm, max_per_sm);
     resident = std::max(1, per_sm) * std::max(1, sms);
     std::lock_guard<std::mutex> lock(g_geometry_mu);
     g_geometry[key] = resident;
@@ -352,9 +350,9 @@ long long launch_zero(const std::vector<Prepared>& jobs, size_t first, size_t co
 // Launch one persistent kernel over `tiles` tiles, bracketed by the profiler.
 template <typename Kernel, typename Batch>
 long long launch_persistent(Kernel kernel, const char* name, size_t dyn_smem, const Batch& b, uint64_t tiles,
-                            cudaStream_t stream, int max_per_sm = 0) {
+                            cudaStream_t stream) {
   unsigned grid = 0;
-  const long long rc = grid_for(kernel, dyn_smem, tiles, &grid, kCtaThreads, max_per_sm);
+  const long long rc = grid_for(kernel, dyn_smem, tiles, &grid);
   if (rc < 0) return rc;
   const long long prof = prof_begin(stream);
   cudaError_t st = launch_dependent(kernel, dim3(grid), dim3(kCtaThreads), dyn_smem, stream, b);
