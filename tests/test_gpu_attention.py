@@ -165,14 +165,17 @@ def test_top16_fixed6_and_raw_streams_in_one_batch():
     run([64, 64], [3, 3], seed=8, reqs=[request(8000, 64, 0, 3), request(8001, 64, 1, 3)])
 
 
-def test_top16_stage_with_more_escapes_than_it_holds():
-    """A block plane with about 6000 escapes (more than a stage keeps; the
-    rest come from the stream) in a stream still within capacity."""
+@pytest.mark.parametrize("plane", [0, 1])
+def test_top16_stage_with_more_escapes_than_it_holds(plane):
+    """A block plane with about 6000 escapes in a stream still within
+    capacity.  K plane: runs of one token and head span many 32-entry chunks
+    of the escape warp's sums.  V plane: more escapes than a stage keeps;
+    the rest come from the stream."""
     ctx = 64 * BT
-    rng = np.random.Generator(np.random.PCG64(9))
+    rng = np.random.Generator(np.random.PCG64(9 + plane))
     shape = (2, ctx, HEADS, DIM)
     hot = np.zeros(shape, bool)
-    hot[0, 3 * BT:4 * BT] = rng.random((BT, HEADS, DIM)) < 0.37  # the K plane of block 3
+    hot[plane, 3 * BT:4 * BT] = rng.random((BT, HEADS, DIM)) < 0.37  # block 3 of the plane
     words = top16_words(rng, shape, 0.0005, hot=hot)
     res, stream = oracle.encode_top16(words.reshape(-1), TABLE)
     assert stream[0] == 5 and int(hot.sum()) > 5088

@@ -7,7 +7,7 @@
 // into its cache and runs attention on the bf16 copy.
 //
 // Shape (the Llama-3-8B decode of the benchmark configuration): 8 kv heads x
-// 128 dims, 16-token blocks, GQA group g <= 16 q heads per kv head.
+// 128 dims, 16-token blocks, GQA group g <= 8 q heads per kv head.
 //
 // Work: the blocks of all requests, in order, are split evenly over the
 // persistent CTAs; an item is one CTA's run of blocks of one request (a CTA
@@ -16,8 +16,9 @@
 //     8 heads x 128 dims), then the V plane block, into a ring of shared
 //     memory stages by TMA (the rows' low bytes and 6-bit codes for fixed6,
 //     their words for raw, their body bytes and 4-bit codes for top16);
-//   - escape warp (top16 kernels only): writes each top16 stage's escape
-//     tables (from the stream's sorted entries) into the stage's tail;
+//   - escape warp (top16 kernels only): from the stream's sorted escape
+//     entries, writes into each top16 stage's tail the escaped words' share
+//     of S^T (K stages) or the stage's escape tables (V stages);
 //   - K warp h (kv head h): decodes its head's slice of each K block
 //     straight into the A fragments of S^T = K Q^T (16 tokens x g q heads,
 //     one m16n8k16 bf16 MMA per 16 dims) and hands the S^T fragments to the
@@ -305,6 +306,18 @@ constexpr uint32_t kAttnEscExps = kAttnEscPrefix + 2 * (kAttnBlockWords / 32);
 constexpr uint32_t kAttnEscExpCap = kAttnStageBytes - kAttnEscExps;  // exponents held in the stage
 static_assert(kAttnCodesOffset + 16 + kAttnBlockTokens * kAttnNibblePitch <= kAttnEscBitmap, "nibble rows");
 static_assert(kAttnEscExps + 1024 <= kAttnStageBytes, "escape exponents");
+// A K stage's tail holds, in place of the bitmap, the escapes' share of S^T:
+// fp32 [token][kv head ^ (token & 7)][q head slot of the group], 16 x 8 x 8.
+constexpr uint32_t kAttnEscCorr = kAttnEscBitmap;
+constexpr uint32_t kAttnCorrBytes = kAttnBlockTokens * kAttnKvHeads * kAttnMaxGroup * 4;
+static_assert(kAttnEscCorr % 16 == 0 && kAttnEscCorr + kAttnCorrBytes <= kAttnStageBytes, "escape share of S^T");
+
+// Float index of (token t, kv head hk, q head slot q) in a K stage's escape
+// share: the kv head is swizzled by the token, so the K warp's reads of 8
+// tokens of one head fall on different banks.
+__device__ __forceinline__ uint32_t corr_index(uint32_t t, uint32_t hk, uint32_t q) {
+  return t * (kAttnKvHeads * kAttnMaxGroup) + ((hk ^ (t & 7u)) * kAttnMaxGroup) + q;
+}
 
 __device__ __forceinline__ const uint8_t* nibble_row(const uint8_t* stage, uint32_t t) {
   return stage + kAttnCodesOffset + t * kAttnNibblePitch;
@@ -525,8 +538,85 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
         producer_acquire(R, p, nullptr);
         AttnDesc& d = D[p.s];
         uint8_t* stage = ring + p.s * kAttnStageBytes;
-        if (mode == 5) {
-          // the block plane's escapes: entries [first, first + count) from
+        if (mode == 5 && plane == 0) {
+          // K plane: the K warps decode an escaped word from its book
+          // exponent like any other word; the difference between its true
+          // and its book value times q, summed per token and q head, is
+          // their correction of S^T.  Chunks of 32 entries from the cursor,
+          // each lane one entry, summed over runs of equal (token, kv head)
+          // (the entries are sorted by position).
+          const uint64_t w_start = static_cast<uint64_t>(blk) * kAttnBlockWords;
+          const uint32_t first = cursor[0];
+          float4* zero = reinterpret_cast<float4*>(stage + kAttnEscCorr);
+#pragma unroll
+          for (int z = 0; z < static_cast<int>(kAttnCorrBytes / 16 / 32); ++z)
+            zero[lane + 32 * z] = make_float4(0.f, 0.f, 0.f, 0.f);
+          __syncwarp();
+          float* cs = reinterpret_cast<float*>(stage + kAttnEscCorr);
+          const uint32_t group = b.group;
+          uint32_t count = 0;
+          for (;;) {
+            const uint32_t i = first + count + lane;
+            uint64_t at = ~0ull;
+            uint32_t ex = 0;
+            if (i < esc_total) {
+              at = entry_pos(entries, i) - w_start;
+              ex = __ldg(entries + 5ull * i + 4);
+            }
+            const bool in = i < esc_total && at < kAttnBlockWords;
+            const uint32_t bal = __ballot_sync(kFull, in);
+            if ((bal & (bal + 1)) != 0 && lane == 0) raise_error(nullptr);  // entries out of order
+            uint32_t body = 0, nib = 0;
+            if (in) {
+              const uint64_t w = w_start + at;
+              body = __ldg(Q.stream + 5 + w);
+              nib = (static_cast<uint32_t>(__ldg(Q.stream + 5 + Q.n + (w >> 1))) >> (4 * static_cast<uint32_t>(w & 1))) & 15u;
+            }
+            const uint32_t bexp = __shfl_sync(kFull, books, nib) & 0xFFu;  // lanes 0-15 hold the K book
+            const uint32_t sm = (body & 0x7Fu) | ((body & 0x80u) << 8);
+            const float delta =
+                in ? __uint_as_float((sm | (ex << 7)) << 16) - __uint_as_float((sm | (bexp << 7)) << 16) : 0.f;
+            const uint32_t key = in ? static_cast<uint32_t>(at >> 7) : 0xFFFFFFFFu;  // token * 8 + kv head
+            const uint32_t hk = key & 7u, t = (key >> 3) & 15u, dl = static_cast<uint32_t>(at) & 127u;
+            // the scan steps that stay inside the lane's run, and the run's last lane
+            uint32_t same = 0;
+#pragma unroll
+            for (int s = 0; s < 5; ++s) {
+              const uint32_t k2 = __shfl_up_sync(kFull, key, 1u << s);
+              if (lane >= (1u << s) && k2 == key) same |= 1u << s;
+            }
+            const uint32_t knext = __shfl_down_sync(kFull, key, 1);
+            const bool last = in && (lane == 31 || knext != key);
+            const uint16_t* qrow = Q.q + static_cast<uint64_t>(hk) * group * kAttnHeadDim + dl;
+            float qv[kAttnMaxGroup];
+#pragma unroll
+            for (int q = 0; q < kAttnMaxGroup; ++q)
+              qv[q] = in && q < static_cast<int>(group)
+                          ? __uint_as_float(static_cast<uint32_t>(__ldg(qrow + q * kAttnHeadDim)) << 16)
+                          : 0.f;
+#pragma unroll
+            for (int q = 0; q < kAttnMaxGroup; ++q) {
+              if (q >= static_cast<int>(group)) break;
+              float v = delta * qv[q];
+#pragma unroll
+              for (int s = 0; s < 5; ++s) {
+                const float u = __shfl_up_sync(kFull, v, 1u << s);
+                if ((same >> s) & 1u) v += u;
+              }
+              if (last) cs[corr_index(t, hk, q)] += v;
+            }
+            __syncwarp();  // a run that continues in the next chunk adds to this chunk's sum
+            count += __popc(bal);
+            if (bal != kFull) break;
+          }
+          cursor[0] = first + count;
+          if (lane == 0) {
+            d.esc_first = first;
+            d.esc_count = count;
+          }
+          if (lane < 16) d.pal[lane] = static_cast<uint8_t>(books);
+        } else if (mode == 5) {
+          // V plane: the block plane's escapes: entries [first, first + count) from
           // the plane's cursor, then the stage's bitmap, prefix and exponents
           const uint64_t w_start = plane * (Q.n / 2) + static_cast<uint64_t>(blk) * kAttnBlockWords;
           const uint32_t first = cursor[plane];
@@ -654,32 +744,23 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
           uint32_t B0[8], N0[4], B1[8], N1[4];
           top16_load<16>(d, stage, gid, dim, B0, N0);
           top16_load<16>(d, stage, gid + 8, dim, B1, N1);
-          // escape bits of the lane's 32 dims of each token, and the escapes before them
-          const uint32_t w0 = (gid * kAttnRowWords + dim) >> 5, w1 = w0 + 8 * kAttnRowWords / 32;
-          const uint32_t* bm = reinterpret_cast<const uint32_t*>(stage + kAttnEscBitmap);
-          const uint16_t* pf = reinterpret_cast<const uint16_t*>(stage + kAttnEscPrefix);
-          const uint32_t r0 = bm[w0], r1 = bm[w1];
-          const uint32_t p0 = r0 ? pf[w0] : 0u, p1 = r1 ? pf[w1] : 0u;
-          const AttnReq& Q = b.req[I.req];
-          const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t n0 = N0[kk >> 1] >> (16 * (kk & 1)), n1 = N1[kk >> 1] >> (16 * (kk & 1));
-            uint32_t a0 = top16_pair_t(B0[kk], t16[n0 & 0xFFu], false);
-            uint32_t a2 = top16_pair_t(B0[kk], t16[(n0 >> 8) & 0xFFu], true);
-            uint32_t a1 = top16_pair_t(B1[kk], t16[n1 & 0xFFu], false);
-            uint32_t a3 = top16_pair_t(B1[kk], t16[(n1 >> 8) & 0xFFu], true);
-            if (((r0 | r1) >> (4 * kk)) & 0xFu) {
-              const uint32_t below = (1u << (4 * kk)) - 1u;
-              a0 = top16_patch(a0, (r0 >> (4 * kk)) & 3u, p0 + __popc(r0 & below), stage, entries, d.esc_first, d.esc_count);
-              a2 = top16_patch(a2, (r0 >> (4 * kk + 2)) & 3u, p0 + __popc(r0 & (below | (3u << (4 * kk)))), stage,
-                               entries, d.esc_first, d.esc_count);
-              a1 = top16_patch(a1, (r1 >> (4 * kk)) & 3u, p1 + __popc(r1 & below), stage, entries, d.esc_first, d.esc_count);
-              a3 = top16_patch(a3, (r1 >> (4 * kk + 2)) & 3u, p1 + __popc(r1 & (below | (3u << (4 * kk)))), stage,
-                               entries, d.esc_first, d.esc_count);
-            }
+            const uint32_t a0 = top16_pair_t(B0[kk], t16[n0 & 0xFFu], false);
+            const uint32_t a2 = top16_pair_t(B0[kk], t16[(n0 >> 8) & 0xFFu], true);
+            const uint32_t a1 = top16_pair_t(B1[kk], t16[n1 & 0xFFu], false);
+            const uint32_t a3 = top16_pair_t(B1[kk], t16[(n1 >> 8) & 0xFFu], true);
             mma_bf16((kk & 1) ? sd : sc, a0, a1, a2, a3, qb[2 * kk], qb[2 * kk + 1]);
           }
+          // the escapes' share, from the escape warp: (gid, 2 tig .. +1) and (gid + 8, ..)
+          const float* cs = reinterpret_cast<const float*>(stage + kAttnEscCorr);
+          const float2 e0 = *reinterpret_cast<const float2*>(cs + corr_index(gid, head, 2 * tig));
+          const float2 e1 = *reinterpret_cast<const float2*>(cs + corr_index(gid + 8, head, 2 * tig));
+          sc[0] += e0.x;
+          sc[1] += e0.y;
+          sc[2] += e1.x;
+          sc[3] += e1.y;
         }  // else: a stream this kernel does not read (the producer raised an error): S^T = 0
         const uint32_t valid = d.valid;
         consumer_release(R, p);
@@ -817,15 +898,20 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
           }
           const AttnReq& Q = b.req[I.req];
           const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
+          const uint32_t rall = r[0] | r[1] | r[2] | r[3];
 #pragma unroll
           for (int m = 0; m < 8; ++m) {
             uint32_t v[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 4; ++j)
               v[j] = top16_pair_t(B[j][m >> 1], t16[(N[j][m >> 2] >> (8 * (m & 3))) & 0xFFu], (m & 1) != 0);
-              const uint32_t bits2 = (r[j] >> (2 * m)) & 3u;
-              if (bits2) v[j] = top16_patch(v[j], bits2, pre[j] + __popc(r[j] & ((1u << (2 * m)) - 1u)), stage,
-                                           entries, d.esc_first, d.esc_count);
+            if ((rall >> (2 * m)) & 3u) {  // an escape among the step's words of the 4 tokens
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t bits2 = (r[j] >> (2 * m)) & 3u;
+                if (bits2) v[j] = top16_patch(v[j], bits2, pre[j] + __popc(r[j] & ((1u << (2 * m)) - 1u)), stage,
+                                             entries, d.esc_first, d.esc_count);
+              }
             }
             mma_step(m, v[0], v[1], v[2], v[3]);
           }
