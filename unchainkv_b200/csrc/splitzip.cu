@@ -1116,6 +1116,7 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
       b.item[items].req = static_cast<uint32_t>(r);
       b.item[items].block0 = static_cast<uint32_t>(at - req_first);
       b.item[items].blocks = static_cast<uint32_t>(stop - at);
+      b.item[items].gblock0 = static_cast<uint32_t>(at);
       if (b.req[r].items == 0) b.req[r].first_item = items;
       ++b.req[r].items;
       ++items;
@@ -1128,7 +1129,9 @@ bool plan_attention(const kvq_splitzip_attn_request* reqs, uint64_t count, uint6
   b.items = items;
   b.group = static_cast<uint32_t>(group);
   b.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kAttnHeadDim));
-  *workspace = 16 + static_cast<uint64_t>(items) * kAttnKvHeads * group * kAttnRecord * sizeof(float);
+  // the items' partials, then (top16 batches) the blocks' scaled scores
+  *workspace = 16 + static_cast<uint64_t>(items) * kAttnKvHeads * group * kAttnRecord * sizeof(float) +
+               (top16 ? total * kAttnKvHeads * kAttnBlockTokens * group * sizeof(float) : 0);
   return true;
 }
 
@@ -1156,6 +1159,7 @@ extern "C" KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_at
   b.partials = reinterpret_cast<float*>(workspace_ptr + 16);
   bool top16 = false;
   for (uint32_t r = 0; r < b.reqs; ++r) top16 = top16 || b.req[r].tables != nullptr;
+  b.scores = top16 ? b.partials + static_cast<uint64_t>(b.items) * kAttnKvHeads * b.group * kAttnRecord : nullptr;
   long long prof = prof_begin(stream);
   if (top16) {
     // + the escape warp
@@ -1166,6 +1170,16 @@ extern "C" KVQ_API long long kvq_splitzip_attention_decode(const kvq_splitzip_at
   prof_end(prof, "AttnKernel", stream);
   cudaError_t st = cudaGetLastError();
   if (st != cudaSuccess) return Fail("AttnKernel", st);
+  if (top16) {  // the V escapes' shares of the top16 items' partials
+    unsigned unused = 0;  // (sets the kernel's shared-memory limit once per device)
+    if (grid_for(AttnEscapeKernel<kAttnMaxReqs, kAttnMaxItems>, kAttnEscSmem, b.items, &unused, kAttnEscThreads) < 0)
+      return -1;
+    prof = prof_begin(stream);
+    AttnEscapeKernel<kAttnMaxReqs, kAttnMaxItems><<<b.items, kAttnEscThreads, kAttnEscSmem, stream>>>(b);
+    prof_end(prof, "AttnEscapeKernel", stream);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return Fail("AttnEscapeKernel", st);
+  }
   const uint64_t warps = static_cast<uint64_t>(b.reqs) * kAttnKvHeads * b.group;
   prof = prof_begin(stream);
   AttnCombineKernel<kAttnMaxReqs, kAttnMaxItems><<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(b);

@@ -17,8 +17,9 @@
 //     memory stages by TMA (the rows' low bytes and 6-bit codes for fixed6,
 //     their words for raw, their body bytes and 4-bit codes for top16);
 //   - escape warp (top16 kernels only): from the stream's sorted escape
-//     entries, writes into each top16 stage's tail the escaped words' share
-//     of S^T (K stages) or the stage's escape tables (V stages);
+//     entries, writes into each top16 K stage's tail the escaped words'
+//     share of S^T; AttnEscapeKernel adds the V escapes' share of O to the
+//     items' partials;
 //   - K warp h (kv head h): decodes its head's slice of each K block
 //     straight into the A fragments of S^T = K Q^T (16 tokens x g q heads,
 //     one m16n8k16 bf16 MMA per 16 dims) and hands the S^T fragments to the
@@ -89,7 +90,7 @@ struct AttnItem {
   uint32_t req;
   uint32_t block0;
   uint32_t blocks;
-  uint32_t pad;
+  uint32_t gblock0;  // the item's first block in the batch's order (all requests' blocks in turn)
 };
 
 template <int kMaxR, int kMaxI>
@@ -99,6 +100,7 @@ struct AttnBatch {
   uint32_t group;      // q heads per kv head
   float scale_log2;    // softmax scale * log2(e)
   float* partials;     // [items][kv_heads * group][kAttnRecord] (o, then m, l)
+  float* scores;       // top16 batches: [batch blocks][kv heads][16 tokens][group] scaled scores, or null
   uint32_t ctas;
   uint16_t cta_item[kAttnMaxCtas + 1];  // items of CTA c: [cta_item[c], cta_item[c + 1])
   AttnReq req[kMaxR];
@@ -294,22 +296,19 @@ __device__ __forceinline__ uint32_t raw_word_pair(const AttnDesc& d, const uint8
 
 // ---- top16 streams (the kTop16 kernel).  A stage holds the block plane's
 // body rows (one byte a word) in place of the low-byte rows and its nibble
-// rows (512 bytes a token) in place of the code rows.  Its tail holds the
-// stage's escapes, written by the producer from the stream's sorted entries:
-// a bitmap of the block plane's 16384 words, the escapes before each bitmap
-// word that holds one (u16; the other words' slots are never read), and the
-// escaped exponents in position order.
+// rows (512 bytes a token) in place of the code rows.  The consumers decode
+// every word from its book exponent, escaped words included; the escapes
+// are corrected outside the MMAs:
+//   - K stages: the escape warp writes into the stage's tail the escaped
+//     words' share of S^T, (true - book value) x q summed per token and q
+//     head, fp32 [token][kv head ^ (token & 7)][q head slot], 16 x 8 x 8;
+//     the K warps add it to their S^T fragments;
+//   - V stages: the V warps save their scaled scores, and AttnEscapeKernel
+//     adds each escape's (true - book value) x p to the item's partial O.
 constexpr uint32_t kAttnNibblePitch = kAttnRowWords / 2;
-constexpr uint32_t kAttnEscBitmap = 24640;
-constexpr uint32_t kAttnEscPrefix = kAttnEscBitmap + kAttnBlockWords / 8;
-constexpr uint32_t kAttnEscExps = kAttnEscPrefix + 2 * (kAttnBlockWords / 32);
-constexpr uint32_t kAttnEscExpCap = kAttnStageBytes - kAttnEscExps;  // exponents held in the stage
-static_assert(kAttnCodesOffset + 16 + kAttnBlockTokens * kAttnNibblePitch <= kAttnEscBitmap, "nibble rows");
-static_assert(kAttnEscExps + 1024 <= kAttnStageBytes, "escape exponents");
-// A K stage's tail holds, in place of the bitmap, the escapes' share of S^T:
-// fp32 [token][kv head ^ (token & 7)][q head slot of the group], 16 x 8 x 8.
-constexpr uint32_t kAttnEscCorr = kAttnEscBitmap;
+constexpr uint32_t kAttnEscCorr = 24640;
 constexpr uint32_t kAttnCorrBytes = kAttnBlockTokens * kAttnKvHeads * kAttnMaxGroup * 4;
+static_assert(kAttnCodesOffset + 16 + kAttnBlockTokens * kAttnNibblePitch <= kAttnEscCorr, "nibble rows");
 static_assert(kAttnEscCorr % 16 == 0 && kAttnEscCorr + kAttnCorrBytes <= kAttnStageBytes, "escape share of S^T");
 
 // Float index of (token t, kv head hk, q head slot q) in a K stage's escape
@@ -356,25 +355,10 @@ __device__ __forceinline__ uint32_t top16_pair_t(uint32_t bw, uint32_t exps, boo
   return (__byte_perm(bw, 0, upper ? 0x3322 : 0x1100) & 0x807F807Fu) | exps;
 }
 
-// Exponent of the stage's escape of rank r (its place in the stage's slice
-// of `count` entries): from the stage, or from the stream past the stage's
-// room.  A rank outside the slice reads nothing: it cannot come from tables
-// built from the slice, and the stream is never read past it.
-__device__ __forceinline__ uint32_t esc_exp(const uint8_t* stage, const uint8_t* entries, uint32_t first,
-                                            uint32_t count, uint32_t r) {
-  if (r >= count) return 0;
-  return r < kAttnEscExpCap ? stage[kAttnEscExps + r] : __ldg(entries + 5ull * (first + r) + 4);
-}
-
-// The escaped words of a word pair: bits2 (bit 0: the low word, bit 1: the
-// high word), rank0 = the stage rank of the low word's escape, or of the
-// high word's when only it escaped.  The exponent field (bits 7..14 of
-// each bf16 word) is replaced, as the reference's patch does.
-__device__ __forceinline__ uint32_t top16_patch(uint32_t w, uint32_t bits2, uint32_t rank0, const uint8_t* stage,
-                                                const uint8_t* entries, uint32_t first, uint32_t count) {
-  if (bits2 & 1u) w = (w & ~0x7F80u) | (esc_exp(stage, entries, first, count, rank0) << 7);
-  if (bits2 & 2u) w = (w & ~0x7F800000u) | (esc_exp(stage, entries, first, count, rank0 + (bits2 & 1u)) << 23);
-  return w;
+// The bf16 value (as fp32) of a top16 word with body byte `body` (sign at
+// bit 7, mantissa below) and exponent `e`.
+__device__ __forceinline__ float top16_value(uint32_t body, uint32_t e) {
+  return __uint_as_float((((body & 0x7Fu) | ((body & 0x80u) << 8)) | (e << 7)) << 16);
 }
 
 // First entry index in [0, total) whose position is >= target (total if
@@ -521,17 +505,15 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
       uint32_t mode = __ldg(Q.stream);
       const uint64_t cap = (Q.n + 199) / 200;
       if (mode != 5 || Q.tables == nullptr || 5 + Q.n + (Q.n + 1) / 2 + 5 * cap > Q.stream_bytes) mode = 0;
-      // the entries (sorted by position) and one cursor per plane, at the
-      // first entry of the item's first block
+      // the entries (sorted by position) and a cursor at the first entry
+      // of the item's first K block
       const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
-      uint32_t esc_total = 0, cursor[2] = {0, 0};
-      uint32_t books = 0;  // lane l: book byte l & 15 of plane l >> 4
+      uint32_t esc_total = 0, cursor = 0;
+      uint32_t books = 0;  // lanes 0-15: the K plane's book
       if (mode == 5) {
         esc_total = static_cast<uint32_t>(min(static_cast<uint64_t>(load_u32le(Q.stream + 1)), cap));
-        cursor[0] = entries_lower_bound(entries, esc_total, static_cast<uint64_t>(I.block0) * kAttnBlockWords);
-        cursor[1] = entries_lower_bound(entries, esc_total,
-                                        Q.n / 2 + static_cast<uint64_t>(I.block0) * kAttnBlockWords);
-        books = __ldg(Q.tables + 512 + lane);
+        cursor = entries_lower_bound(entries, esc_total, static_cast<uint64_t>(I.block0) * kAttnBlockWords);
+        books = __ldg(Q.tables + 512 + (lane & 15));
       }
       for (uint32_t k = 0; k < 2 * I.blocks; ++k) {
         const uint32_t blk = I.block0 + (k >> 1), plane = k & 1;
@@ -546,7 +528,7 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
           // each lane one entry, summed over runs of equal (token, kv head)
           // (the entries are sorted by position).
           const uint64_t w_start = static_cast<uint64_t>(blk) * kAttnBlockWords;
-          const uint32_t first = cursor[0];
+          const uint32_t first = cursor;
           float4* zero = reinterpret_cast<float4*>(stage + kAttnEscCorr);
 #pragma unroll
           for (int z = 0; z < static_cast<int>(kAttnCorrBytes / 16 / 32); ++z)
@@ -572,10 +554,8 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
               body = __ldg(Q.stream + 5 + w);
               nib = (static_cast<uint32_t>(__ldg(Q.stream + 5 + Q.n + (w >> 1))) >> (4 * static_cast<uint32_t>(w & 1))) & 15u;
             }
-            const uint32_t bexp = __shfl_sync(kFull, books, nib) & 0xFFu;  // lanes 0-15 hold the K book
-            const uint32_t sm = (body & 0x7Fu) | ((body & 0x80u) << 8);
-            const float delta =
-                in ? __uint_as_float((sm | (ex << 7)) << 16) - __uint_as_float((sm | (bexp << 7)) << 16) : 0.f;
+            const uint32_t bexp = __shfl_sync(kFull, books, nib) & 0xFFu;
+            const float delta = in ? top16_value(body, ex) - top16_value(body, bexp) : 0.f;
             const uint32_t key = in ? static_cast<uint32_t>(at >> 7) : 0xFFFFFFFFu;  // token * 8 + kv head
             const uint32_t hk = key & 7u, t = (key >> 3) & 15u, dl = static_cast<uint32_t>(at) & 127u;
             // the scan steps that stay inside the lane's run, and the run's last lane
@@ -609,59 +589,13 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
             count += __popc(bal);
             if (bal != kFull) break;
           }
-          cursor[0] = first + count;
+          cursor = first + count;
           if (lane == 0) {
             d.esc_first = first;
             d.esc_count = count;
           }
           if (lane < 16) d.pal[lane] = static_cast<uint8_t>(books);
-        } else if (mode == 5) {
-          // V plane: the block plane's escapes: entries [first, first + count) from
-          // the plane's cursor, then the stage's bitmap, prefix and exponents
-          const uint64_t w_start = plane * (Q.n / 2) + static_cast<uint64_t>(blk) * kAttnBlockWords;
-          const uint32_t first = cursor[plane];
-          uint4* zero = reinterpret_cast<uint4*>(stage + kAttnEscBitmap);
-#pragma unroll
-          for (int z = 0; z < static_cast<int>(kAttnBlockWords / 8 / 16 / 32); ++z) zero[lane + 32 * z] = make_uint4(0, 0, 0, 0);
-          __syncwarp();
-          // chunks of 32 entries from the cursor, each read once (position
-          // and exponent), until the first at or past the block plane's end
-          uint32_t* bm = reinterpret_cast<uint32_t*>(stage + kAttnEscBitmap);
-          uint16_t* pf = reinterpret_cast<uint16_t*>(stage + kAttnEscPrefix);
-          uint32_t count = 0, last_word = 0xFFFFFFFFu;
-          for (;;) {
-            const uint32_t i = first + count + lane;
-            uint64_t at = ~0ull;
-            uint32_t ex = 0;
-            if (i < esc_total) {
-              at = entry_pos(entries, i) - w_start;
-              ex = __ldg(entries + 5ull * i + 4);
-            }
-            const bool in = i < esc_total && at < kAttnBlockWords;
-            const uint32_t bal = __ballot_sync(kFull, in);
-            if ((bal & (bal + 1)) != 0 && lane == 0) raise_error(nullptr);  // entries out of order
-            // the escapes before a bitmap word are the rank of its first
-            // entry; only words that hold escapes are ever read
-            const uint32_t word = in ? static_cast<uint32_t>(at >> 5) : 0xFFFFFFFFu;
-            const uint32_t up = __shfl_up_sync(kFull, word, 1);
-            const uint32_t before = lane == 0 ? last_word : up;
-            if (in) {
-              atomicOr(&bm[word], 1u << (at & 31));
-              if (word != before) pf[word] = static_cast<uint16_t>(count + lane);
-              if (count + lane < kAttnEscExpCap) stage[kAttnEscExps + count + lane] = static_cast<uint8_t>(ex);
-            }
-            last_word = __shfl_sync(kFull, word, 31);
-            count += __popc(bal);
-            if (bal != kFull) break;
-          }
-          cursor[plane] = first + count;
-          if (lane == 0) {
-            d.esc_first = first;
-            d.esc_count = count;
-          }
-          const uint32_t book = __shfl_sync(kFull, books, 16 * plane + (lane & 15));
-          if (lane < 16) d.pal[lane] = static_cast<uint8_t>(book);
-        }
+        }  // V stages: their escapes are added to the items' partials by AttnEscapeKernel
         __syncwarp();  // the lanes' table stores precede lane 0's arrival
         if (lane == 0) mbar_arrive(&R.full[p.s]);
         p.next();
@@ -884,36 +818,28 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
         } else if (kTop16 && d.mode == 5) {
           const uint32_t* t16 = pair + 256;  // the V plane's code-byte table
           const uint32_t tok[4] = {t0, t0 + 1, t2, t2 + 1};
-          uint32_t B[4][4], N[4][2], r[4], pre[4];
-          const uint32_t* bm = reinterpret_cast<const uint32_t*>(stage + kAttnEscBitmap);
-          const uint16_t* pf = reinterpret_cast<const uint16_t*>(stage + kAttnEscPrefix);
-          const uint32_t half = 16 * (gid & 1);  // the lane's 16 dims are this half of a bitmap word
+          uint32_t B[4][4], N[4][2];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            top16_load<8>(d, stage, tok[j], dim, B[j], N[j]);
-            const uint32_t wi = (tok[j] * kAttnRowWords + dim) >> 5;
-            const uint32_t word = bm[wi];
-            r[j] = (word >> half) & 0xFFFFu;
-            pre[j] = r[j] ? pf[wi] + (half ? __popc(word & 0xFFFFu) : 0u) : 0u;
-          }
-          const AttnReq& Q = b.req[I.req];
-          const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
-          const uint32_t rall = r[0] | r[1] | r[2] | r[3];
+          for (int j = 0; j < 4; ++j) top16_load<8>(d, stage, tok[j], dim, B[j], N[j]);
 #pragma unroll
           for (int m = 0; m < 8; ++m) {
             uint32_t v[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               v[j] = top16_pair_t(B[j][m >> 1], t16[(N[j][m >> 2] >> (8 * (m & 3))) & 0xFFu], (m & 1) != 0);
-            if ((rall >> (2 * m)) & 3u) {  // an escape among the step's words of the 4 tokens
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint32_t bits2 = (r[j] >> (2 * m)) & 3u;
-                if (bits2) v[j] = top16_patch(v[j], bits2, pre[j] + __popc(r[j] & ((1u << (2 * m)) - 1u)), stage,
-                                             entries, d.esc_first, d.esc_count);
-              }
-            }
             mma_step(m, v[0], v[1], v[2], v[3]);
+          }
+          // the block's scaled scores (masked past the context), for the
+          // escapes' correction: [kv head][token][q head slot] of the block
+          float* sx = b.scores + (static_cast<uint64_t>(I.gblock0 + blk) * kAttnKvHeads + head) *
+                                     kAttnBlockTokens * group;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const uint32_t col = 2 * tig + e;
+            if (col < group) {
+              sx[gid * group + col] = x[e];
+              sx[(gid + 8) * group + col] = x[2 + e];
+            }
           }
         }
       }
@@ -937,6 +863,145 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
           dst[kAttnHeadDim + 1] = lsum[e];
         }
       }
+    }
+  }
+}
+
+// V-plane escapes of top16 streams.  The V warps decode an escaped V word
+// from its book exponent, so each q head's partial O of the item lacks
+// p * delta at the word's dim: delta = true - book value of the word, p =
+// 2^(x - m) the weight of the word's token in the partial's scale (x the
+// token's scaled score, saved by the V warps; m the partial's running max).
+// One CTA per item, in batches of the item's V escapes:
+//   - two warps find the item's V escapes by searches of the sorted entries;
+//   - every thread computes the shares of a few escapes (four at a time, so
+//     that their loads overlap) into shared memory;
+//   - warp h adds those of kv head h to the item's sums in shared memory,
+//     [q head][dim], 32 entries at a time: the lanes of entries with the
+//     same dim take turns in lane order, so a sum takes its terms in entry
+//     order;
+//   - at the end warp h adds its head's sums to the partials.
+// Every run adds the same terms in the same order (no atomics).
+constexpr uint32_t kAttnEscSmem = 96 * 1024;        // dynamic shared bytes: sums, then a batch
+constexpr int kAttnEscThreads = 64 * kAttnKvHeads;  // 16 warps; warps 0-7 also add the shares
+static_assert(kAttnKvHeads * kAttnMaxGroup * kAttnHeadDim * 4 + 4096 * 6 <= kAttnEscSmem, "escape batch room");
+
+template <int kMaxR, int kMaxI>
+__global__ void __launch_bounds__(kAttnEscThreads, 2) AttnEscapeKernel(const __grid_constant__ AttnBatch<kMaxR, kMaxI> b) {
+  extern __shared__ __align__(16) uint8_t esm[];
+  __shared__ uint32_t range[2];
+  __shared__ float mq[kAttnKvHeads * kAttnMaxGroup];  // the item's running max per q head
+  const uint32_t item = blockIdx.x;
+  if (item >= b.items) return;
+  const AttnItem& I = b.item[item];
+  const AttnReq& Q = b.req[I.req];
+  if (Q.tables == nullptr) return;
+  const uint64_t cap = (Q.n + 199) / 200;
+  // a stream the attention kernel did not read as top16 (it raised the error)
+  if (__ldg(Q.stream) != 5 || 5 + Q.n + (Q.n + 1) / 2 + 5 * cap > Q.stream_bytes) return;
+  const uint8_t* entries = Q.stream + 5 + Q.n + (Q.n + 1) / 2;
+  const uint32_t esc_total = static_cast<uint32_t>(min(static_cast<uint64_t>(load_u32le(Q.stream + 1)), cap));
+  const uint64_t half = Q.n / 2;  // the V plane's first word
+  const uint64_t v0 = half + static_cast<uint64_t>(I.block0) * kAttnBlockWords;
+  const uint64_t v1 = v0 + static_cast<uint64_t>(I.blocks) * kAttnBlockWords;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr uint32_t T = kAttnEscThreads;
+  const uint32_t group = b.group, heads = kAttnKvHeads * group;
+  float* partial = b.partials + static_cast<uint64_t>(item) * heads * kAttnRecord;
+  if (warp < 2) {
+    const uint32_t r = entries_lower_bound(entries, esc_total, warp == 0 ? v0 : v1);
+    if (lane == 0) range[warp] = r;
+  }
+  float* sums = reinterpret_cast<float*>(esm);  // [q head][dim]
+  for (uint32_t i = tid; i < heads * kAttnHeadDim; i += T) sums[i] = 0.f;
+  if (static_cast<uint32_t>(tid) < heads) mq[tid] = partial[tid * kAttnRecord + kAttnHeadDim];
+  __syncthreads();
+  const uint32_t lo = range[0], hi = range[1];
+  if (lo >= hi) return;
+  // the batch: entries that fit the rest as a u16 key and `group` shares each
+  const uint32_t room = kAttnEscSmem - heads * kAttnHeadDim * 4;
+  const uint32_t batch = min(4096u, (room - 16) / (2 + 4 * group) / 256 * 256);
+  uint16_t* skey = reinterpret_cast<uint16_t*>(esm + heads * kAttnHeadDim * 4);  // kv head << 7 | dim, or 0xFFFF
+  float* sval = reinterpret_cast<float*>(esm + heads * kAttnHeadDim * 4 + ((2 * batch + 15) & ~15u));
+  const uint8_t* vbook = Q.tables + 528;
+  for (uint32_t e0 = lo; e0 < hi; e0 += batch) {
+    const uint32_t cnt = min(hi - e0, batch);
+    for (uint32_t k0 = 0; k0 < cnt; k0 += 4 * T) {
+      uint32_t kk[4], key[4], ex[4], body[4], nb[4];
+      uint64_t pos[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        kk[j] = k0 + T * j + tid;
+        pos[j] = kk[j] < cnt ? entry_pos(entries, e0 + kk[j]) : v1;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        key[j] = 0xFFFFu;
+        if (kk[j] < cnt && (pos[j] < v0 || pos[j] >= v1)) raise_error(nullptr);  // entries out of order
+        if (pos[j] >= v0 && pos[j] < v1) {
+          const uint32_t wv = static_cast<uint32_t>(pos[j] - v0);  // word of the item's V blocks
+          if (I.block0 * kAttnBlockTokens + wv / kAttnRowWords < Q.ctx) {  // words past the context are read as 0
+            key[j] = wv % kAttnRowWords;  // kv head << 7 | dim
+            ex[j] = __ldg(entries + 5ull * (e0 + kk[j]) + 4);
+            body[j] = __ldg(Q.stream + 5 + pos[j]);
+            nb[j] = __ldg(Q.stream + 5 + Q.n + (pos[j] >> 1));
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (key[j] != 0xFFFFu) {
+          const uint32_t wv = static_cast<uint32_t>(pos[j] - v0);
+          const uint32_t hk = key[j] >> 7;
+          const uint32_t nib = (nb[j] >> (4 * static_cast<uint32_t>(pos[j] & 1))) & 15u;
+          const float delta = top16_value(body[j], ex[j]) - top16_value(body[j], __ldg(vbook + nib));
+          // scores of the token: [batch block][kv head][token][q head slot]
+          const float* xs = b.scores + ((static_cast<uint64_t>(I.gblock0 + wv / kAttnBlockWords) * kAttnKvHeads + hk) *
+                                            kAttnBlockTokens + (wv / kAttnRowWords) % kAttnBlockTokens) * group;
+          float xv[kAttnMaxGroup];
+#pragma unroll
+          for (int q = 0; q < kAttnMaxGroup; ++q) xv[q] = q < static_cast<int>(group) ? xs[q] : 0.f;
+#pragma unroll
+          for (int q = 0; q < kAttnMaxGroup; ++q)
+            if (q < static_cast<int>(group)) sval[kk[j] * group + q] = exp2f(xv[q] - mq[hk * group + q]) * delta;
+        }
+        if (kk[j] < cnt) skey[kk[j]] = static_cast<uint16_t>(key[j]);
+      }
+    }
+    __syncthreads();
+    if (warp < kAttnKvHeads) {
+      // kv head `warp`: 32 entries at a time, the lanes of one dim in turn
+      for (uint32_t c = 0; c < cnt; c += 32) {
+        const uint32_t key = c + lane < cnt ? skey[c + lane] : 0xFFFFu;
+        const bool mine = (key >> 7) == static_cast<uint32_t>(warp);
+        if (__ballot_sync(kFull, mine) == 0) continue;
+        const uint32_t dl = key & 127u;
+        const uint32_t peers = __match_any_sync(kFull, mine ? dl : 128u + lane);
+        const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+        const uint32_t turns = __reduce_max_sync(kFull, mine ? rank : 0u);
+        for (uint32_t t = 0; t <= turns; ++t) {
+          if (mine && rank == t) {
+            const float* v = sval + (c + lane) * group;
+            float* dst = sums + warp * group * kAttnHeadDim + dl;
+            for (uint32_t q = 0; q < group; ++q) dst[q * kAttnHeadDim] += v[q];
+          }
+          __syncwarp();
+        }
+      }
+    }
+    __syncthreads();  // the batch is read before the next one is written
+  }
+  if (warp < kAttnKvHeads) {
+    float* o = partial + static_cast<uint64_t>(warp) * group * kAttnRecord + 4 * lane;
+    const float* sm = sums + warp * group * kAttnHeadDim + 4 * lane;
+    for (uint32_t q = 0; q < group; ++q) {
+      const float4 a = *reinterpret_cast<const float4*>(sm + q * kAttnHeadDim);
+      float4 r = *reinterpret_cast<float4*>(o + q * kAttnRecord);
+      r.x += a.x;
+      r.y += a.y;
+      r.z += a.z;
+      r.w += a.w;
+      *reinterpret_cast<float4*>(o + q * kAttnRecord) = r;
     }
   }
 }
