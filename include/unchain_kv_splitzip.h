@@ -359,7 +359,10 @@ typedef struct kvq_splitzip_attn_request {
 } kvq_splitzip_attn_request;
 
 /* Device workspace bytes kvq_splitzip_attention_decode needs for this batch
- * on the current device (0 if the batch would be declined). */
+ * on the current device (0 if the batch would be declined): the partial
+ * results of the kernel's work items and, when a request carries top16
+ * tables, the scaled scores of every block (512 x group bytes a block),
+ * from which the V escapes' correction is computed. */
 KVQ_API long long kvq_splitzip_attention_workspace_bytes(const kvq_splitzip_attn_request* reqs,
                                                          unsigned long long count,
                                                          unsigned long long group);
