@@ -116,10 +116,8 @@ struct AttnDesc {
   uint32_t pad_y;
   uint32_t valid;  // valid tokens of the block
   uint32_t unused;
-  uint32_t esc_first;  // top16: the stage's escapes are entries [esc_first, esc_first + esc_count)
-  uint32_t esc_count;
-  uint32_t pad2[2];
-  uint8_t pal[64];  // fixed6 palette of the request; top16: the plane's 16 book exponents
+  uint32_t pad2[4];
+  uint8_t pal[64];  // fixed6 palette of the request
 };
 
 using AttnRing = Ring<kAttnStages>;
@@ -518,7 +516,6 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
       for (uint32_t k = 0; k < 2 * I.blocks; ++k) {
         const uint32_t blk = I.block0 + (k >> 1), plane = k & 1;
         producer_acquire(R, p, nullptr);
-        AttnDesc& d = D[p.s];
         uint8_t* stage = ring + p.s * kAttnStageBytes;
         if (mode == 5 && plane == 0) {
           // K plane: the K warps decode an escaped word from its book
@@ -590,13 +587,8 @@ __global__ void __launch_bounds__(kTop16 ? kAttnThreads + 32 : kAttnThreads, 1)
             if (bal != kFull) break;
           }
           cursor = first + count;
-          if (lane == 0) {
-            d.esc_first = first;
-            d.esc_count = count;
-          }
-          if (lane < 16) d.pal[lane] = static_cast<uint8_t>(books);
         }  // V stages: their escapes are added to the items' partials by AttnEscapeKernel
-        __syncwarp();  // the lanes' table stores precede lane 0's arrival
+        __syncwarp();  // the lanes' stores of the stage's share precede lane 0's arrival
         if (lane == 0) mbar_arrive(&R.full[p.s]);
         p.next();
       }
