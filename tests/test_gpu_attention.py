@@ -156,7 +156,8 @@ def test_batch_of_config4():
 @pytest.mark.parametrize("aligned", [False, True, 11])
 def test_top16_streams(aligned):
     """top16 streams (mode 5, with the layer's table): body and nibbles
-    decoded into the fragments, escapes patched from the sorted entries."""
+    decoded into the fragments from the books; the escapes, read from the
+    sorted entries, corrected in S^T (K) and in the partials (V)."""
     run([1, 37, 16, 300, 1029], [5] * 5, seed=6, aligned=aligned)
 
 
