@@ -170,8 +170,8 @@ def test_top16_fixed6_and_raw_streams_in_one_batch():
 def test_top16_stage_with_more_escapes_than_it_holds(plane):
     """A block plane with about 6000 escapes in a stream still within
     capacity.  K plane: runs of one token and head span many 32-entry chunks
-    of the escape warp's sums.  V plane: more escapes than a stage keeps;
-    the rest come from the stream."""
+    of the escape warp's sums.  V plane: more escapes than one batch of the
+    correction kernel holds (4096 at group 4), so the item takes two."""
     ctx = 64 * BT
     rng = np.random.Generator(np.random.PCG64(9 + plane))
     shape = (2, ctx, HEADS, DIM)
